@@ -1,0 +1,125 @@
+/*
+ * smeai_q2k.h -- C-ABI of the sm_100a Q2_K x Q8_K mul_mat path.
+ *
+ * Replaces the ggml 0.9.8 Q2_K matrix-multiply path that the reference grafts
+ * into llama.cpp (llama.cpp/doc/SME_Q2K_OPTIMIZATION.md:82-136,
+ * docs/architecture.md:41-46).  ggml's own sources are not part of the
+ * reference tree; the ggml-shaped entry points below keep the signatures of
+ * ggml's CPU type traits so a ggml build can bind them in place of its own.
+ *
+ * Two groups of entry points:
+ *
+ *  1. ggml-shaped (host pointers, ggml's block layouts, ggml's semantics).
+ *     Each call stages its data to the GPU, runs the same kernels as the
+ *     coarse entry points, and copies the result back.  They cannot report
+ *     errors (ggml's signatures return void); on failure they leave the
+ *     outputs zeroed and smeai_last_error() says why.  They are reentrant:
+ *     each calling thread gets its own stream and staging buffers.
+ *
+ *  2. Coarse GPU entry points (device pointers, explicit stream, int status:
+ *     0 = OK, negative = the sme_ai_status codes of sme_ai_ops.h, -5 = CUDA
+ *     error).  Weights are repacked once into a device-resident tile layout
+ *     (the analogue of ggml's CPU_REPACK extra buffer type) and referenced by
+ *     an opaque handle.
+ *
+ * Block layouts (bytes):  block_q2_K = scales[16] qs[64] d(fp16) dmin(fp16)
+ *                         = 84 per 256 weights;
+ *                         block_q8_K = d(f32) qs[256](int8) bsums[16](int16)
+ *                         = 292 per 256 activations.
+ * Streams are passed as `void *` (a cudaStream_t; NULL = legacy default).
+ */
+#ifndef SMEAI_Q2K_H
+#define SMEAI_Q2K_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define SMEAI_QK_K 256
+#define SMEAI_BLOCK_Q2_K_BYTES 84
+#define SMEAI_BLOCK_Q8_K_BYTES 292
+
+/* ---------------- 1. ggml type-trait shaped entry points ----------------- */
+
+/* Replaces ggml-cpu quantize_row_q8_K (generic C quantize_row_q8_K_ref):
+ * k floats (k % 256 == 0) -> k/256 block_q8_K at y. */
+void quantize_row_q8_K(const float *x, void *y, int64_t k);
+
+/* Replaces ggml-quants.c quantize_row_q2_K_ref (Q2_K from_float). */
+void quantize_row_q2_K(const float *x, void *y, int64_t k);
+
+/* Replaces ggml-quants.c dequantize_row_q2_K (Q2_K to_float). */
+void dequantize_row_q2_K(const void *x, float *y, int64_t k);
+
+/* Replaces ggml-cpu ggml_vec_dot_q2_K_q8_K (type_traits_cpu[Q2_K].vec_dot):
+ * *s = dot(row vx, row vy) over n values (n % 256 == 0).  nrc must be 1
+ * (ggml never requests more for Q2_K); bs, bx, by are then unused. */
+void ggml_vec_dot_q2_K_q8_K(int n, float *s, size_t bs, const void *vx, size_t bx, const void *vy, size_t by,
+                            int nrc);
+
+/* ---------------- 2. coarse GPU entry points ----------------------------- */
+
+/* Is a compute-capability-10.x device present and usable?  1 / 0. */
+int smeai_device_ready(void);
+
+/* Text of the last error raised on the calling thread ("" if none). */
+const char *smeai_last_error(void);
+
+/* Repack n_rows x k of block_q2_K (row-major, host or device memory) into the
+ * device tile layout; *w_dev_out receives an opaque handle.  The analogue of
+ * ggml's CPU_REPACK buffer placement (q2_K_8x8_q8_K traits). */
+int smeai_q2k_repack(const void *w_q2k, int64_t n_rows, int64_t k, void **w_dev_out);
+void smeai_q2k_free(void *w_dev);
+/* Device bytes held by a repacked weight. */
+size_t smeai_q2k_weight_bytes(const void *w_dev);
+
+/* Q8_K quantization of n_cols rows of k floats (device memory, row stride
+ * ld_x floats) into n_cols * k/256 contiguous block_q8_K. */
+int smeai_q8k_quantize(const float *x_dev, int64_t ld_x, int64_t n_cols, int64_t k, void *y_q8k_dev,
+                       void *stream);
+/* The same after an RMSNorm of each row: x / sqrt(mean(x^2) + eps)
+ * (sme_ai_library/src/sme_ai_ops.c:1060-1092), fused into one kernel. */
+int smeai_rms_q8k_quantize(const float *x_dev, int64_t ld_x, int64_t n_cols, int64_t k, float eps,
+                           void *y_q8k_dev, void *stream);
+
+/* y[c*ldy + r] = sum_k W[r,k] * X[c,k]  for r < n_rows, c < n_cols: the
+ * result of ggml's mul_mat for a Q2_K src0 and Q8_K-quantized src1 (dst
+ * rows contiguous).  n_rows and k must match the handle. */
+int smeai_q2k_mul_mat(const void *w_dev, int64_t n_rows, int64_t k, const void *x_q8k_dev, int64_t n_cols,
+                      float *y_dev, size_t ldy, void *stream);
+
+/* Fused epilogues of the decode GEMV (n_cols <= 8 per launch, larger counts
+ * are split):
+ *   SMEAI_EPI_STORE     y = W x
+ *   SMEAI_EPI_RESIDUAL  y = resid + W x          (resid may alias y)
+ *   SMEAI_EPI_SILU_MUL  rows of W interleave (gate_i, up_i);
+ *                       y[i] = silu(gate_i . x) * (up_i . x)   (n_rows/2 outputs) */
+#define SMEAI_EPI_STORE 0
+#define SMEAI_EPI_RESIDUAL 1
+#define SMEAI_EPI_SILU_MUL 2
+int smeai_q2k_mul_mat_ex(const void *w_dev, const void *x_q8k_dev, int64_t n_cols, float *y_dev, size_t ldy,
+                         int epilogue, const float *resid_dev, size_t ld_resid, void *stream);
+
+/* fp32 activations in, fp32 out: quantizes X to Q8_K into a library-owned
+ * device scratch buffer (grown on demand, one per device), then mul_mat. */
+int smeai_q2k_mul_mat_f32(const void *w_dev, const float *x_dev, int64_t n_cols, float *y_dev, size_t ldy,
+                          void *stream);
+
+/* Exactness probe: the integer parts of the dot for every (row, super-block)
+ * against ONE Q8_K row, [n_rows][k/256] int32 each:
+ *   isum  = sum_j scale_j * sum_{i in sub-block j} q2_i * q8_i
+ *   summs = sum_j min_j * bsums_j                                          */
+int smeai_q2k_block_sums(const void *w_dev, const void *x_q8k_dev, int32_t *isum_dev, int32_t *summs_dev,
+                         void *stream);
+
+/* Device-side weight quantizer / decoder (fp32 <-> block_q2_K, n % 256 == 0). */
+int smeai_q2k_quantize_device(const float *x_dev, int64_t n, void *y_q2k_dev, void *stream);
+int smeai_q2k_dequantize_device(const void *w_q2k_dev, int64_t n, float *y_dev, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,564 @@
+/*
+ * smeai_oracle.c -- CPU restatement of the reference's hot-path arithmetic.
+ *
+ * TEST INFRASTRUCTURE ONLY: loaded by tests, the smoke check and the CPU
+ * baseline leg of the benchmark, never by the product library.
+ *
+ * Build: oracle/Makefile (gcc -O2 -ffp-contract=off -fopenmp).  Contraction is
+ * disabled so that every fused multiply-add below is an explicit fmaf() and the
+ * float semantics are stated in the source, not chosen by the compiler.
+ */
+#include "smeai_oracle.h"
+
+#include <math.h>
+#include <stdlib.h>
+#include <string.h>
+#ifdef _OPENMP
+#include <omp.h>
+#endif
+
+/* ------------------------------------------------------------------------ */
+/* fp16 <-> fp32.  _Float16 is IEEE binary16, the same storage as the       */
+/* reference's __fp16 (sme_ai_library/include/sme_ai_ops.h:75); conversions  */
+/* to half round to nearest-even, conversions to float are exact.            */
+/* ------------------------------------------------------------------------ */
+float orc_half_to_float(uint16_t h) {
+    _Float16 v;
+    memcpy(&v, &h, 2);
+    return (float) v;
+}
+
+uint16_t orc_float_to_half(float f) {
+    _Float16 v = (_Float16) f;
+    uint16_t h;
+    memcpy(&h, &v, 2);
+    return h;
+}
+
+void orc_halves_to_floats(const uint16_t *src, float *dst, uint64_t n) {
+    for (uint64_t i = 0; i < n; ++i) dst[i] = orc_half_to_float(src[i]);
+}
+
+void orc_floats_to_halves(const float *src, uint16_t *dst, uint64_t n) {
+    for (uint64_t i = 0; i < n; ++i) dst[i] = orc_float_to_half(src[i]);
+}
+
+/* ------------------------------------------------------------------------ */
+/* The reference benches' deterministic data: a 32-bit LCG                   */
+/* (state = state*1664525 + 1013904223), value (r % 2001)/2000 - 0.5,        */
+/* rounded to fp16 for half inputs.                                           */
+/* sme_ai_library/test_bench/bench_sme_full_timing.c:33-51                    */
+/* sme_ai_library/test_bench/verify_sme_ai_timing.c:68-86                     */
+/* ------------------------------------------------------------------------ */
+static float lcg_value(uint32_t *state) {
+    *state = *state * 1664525u + 1013904223u;
+    return ((float) (*state % 2001u) / 2000.0f) - 0.5f;
+}
+
+void orc_lcg_fill_f16(uint16_t *dst, uint64_t count, uint32_t seed) {
+    uint32_t s = seed;
+    for (uint64_t i = 0; i < count; ++i) dst[i] = orc_float_to_half(lcg_value(&s));
+}
+
+void orc_lcg_fill_f32(float *dst, uint64_t count, uint32_t seed) {
+    uint32_t s = seed;
+    for (uint64_t i = 0; i < count; ++i) dst[i] = lcg_value(&s);
+}
+
+/* ======================================================================== */
+/* Path A: sme_ai_library                                                    */
+/* ======================================================================== */
+
+/* gelu_approx, sme_ai_ops.c:107-112 (tanh form, libm tanhf). */
+static float gelu_tanh(float x) {
+    const float c0 = 0.7978845608f;
+    const float c1 = 0.044715f;
+    float cube = x * x * x;
+    float inner = c0 * (x + c1 * cube);
+    return 0.5f * x * (1.0f + tanhf(inner));
+}
+
+/* Activations applied in place after the GEMM + bias.
+ * ReLU: sme_ai_ops.c:834-846 (max(x, 0)); GELU: :867-874 via gelu_approx;
+ * SiLU: :879-887 (x / (1 + expf(-x))). */
+static void apply_act(float *v, uint64_t n, int act) {
+    for (uint64_t i = 0; i < n; ++i) {
+        float x = v[i];
+        switch (act) {
+            case ORC_ACT_RELU: v[i] = x > 0.0f ? x : 0.0f; break;
+            case ORC_ACT_GELU: v[i] = gelu_tanh(x); break;
+            case ORC_ACT_SILU: v[i] = x / (1.0f + expf(-x)); break;
+            default: break;
+        }
+    }
+}
+
+/* Row-wise bias add after the GEMM; a NULL bias is allowed.
+ * add_bias_f32, sme_ai_ops.c:207-221. */
+static void add_bias(float *out, const float *bias, uint64_t rows, uint64_t cols) {
+    if (bias == NULL) return;
+    for (uint64_t r = 0; r < rows; ++r)
+        for (uint64_t c = 0; c < cols; ++c) out[r * cols + c] += bias[c];
+}
+
+/*
+ * Linear on fp16 data: out[r][c] = sum_k in[r][k] * w[k][c], k ascending, in
+ * fp32, then + bias, then the activation.
+ *   scalar_matmul_f16f16_f32   sme_ai_ops.c:251-267
+ *   sme_ai_linear_ref_f16f32   sme_ai_ops.c:653-671
+ *   linear_activation_ref      sme_ai_ops.c:465-480
+ * The product of two fp16 values is exact in fp32, so the fused form below is
+ * bit-identical to the reference's unfused acc += a*b under any contraction.
+ */
+int orc_linear_f16f32(const uint16_t *input, uint64_t batch, uint64_t in_features,
+                      const uint16_t *weight, uint64_t out_features,
+                      const float *bias, float *output, int act) {
+    if (!input || !weight || !output || !batch || !in_features || !out_features) return -1;
+    float *wf = (float *) malloc(in_features * out_features * sizeof(float));
+    float *xf = (float *) malloc(batch * in_features * sizeof(float));
+    if (!wf || !xf) { free(wf); free(xf); return -2; }
+    orc_halves_to_floats(weight, wf, in_features * out_features);
+    orc_halves_to_floats(input, xf, batch * in_features);
+    for (uint64_t r = 0; r < batch; ++r) {
+        for (uint64_t c = 0; c < out_features; ++c) {
+            float acc = 0.0f;
+            for (uint64_t k = 0; k < in_features; ++k)
+                acc = fmaf(xf[r * in_features + k], wf[k * out_features + c], acc);
+            output[r * out_features + c] = acc;
+        }
+    }
+    free(wf);
+    free(xf);
+    add_bias(output, bias, batch, out_features);
+    apply_act(output, batch * out_features, act);
+    return 0;
+}
+
+/*
+ * The same operator for true fp32 inputs (a new-API variant with no reference
+ * counterpart; it keeps scalar_matmul_f16f16_f32's loop order).  The multiply
+ * -add is fused, which is what the reference's GCC build (default
+ * -ffp-contract=fast on an FMA target) makes of acc += a*b.
+ */
+int orc_linear_f32f32(const float *input, uint64_t batch, uint64_t in_features,
+                      const float *weight, uint64_t out_features,
+                      const float *bias, float *output, int act) {
+    if (!input || !weight || !output || !batch || !in_features || !out_features) return -1;
+    for (uint64_t r = 0; r < batch; ++r) {
+        for (uint64_t c = 0; c < out_features; ++c) {
+            float acc = 0.0f;
+            for (uint64_t k = 0; k < in_features; ++k)
+                acc = fmaf(input[r * in_features + k], weight[k * out_features + c], acc);
+            output[r * out_features + c] = acc;
+        }
+    }
+    add_bias(output, bias, batch, out_features);
+    apply_act(output, batch * out_features, act);
+    return 0;
+}
+
+/*
+ * Two-layer MLP: h = act(in*W1 + b1) rounded to fp16, out = h*W2 + b2.
+ * mlp_activation_ref, sme_ai_ops.c:504-529 (fp16 re-round via
+ * convert_fp32_to_fp16, :175-179).
+ */
+int orc_mlp_f16f32(const uint16_t *input, uint64_t batch, uint64_t in_features,
+                   const uint16_t *fc1_weight, uint64_t hidden_features, const float *fc1_bias,
+                   const uint16_t *fc2_weight, uint64_t out_features, const float *fc2_bias,
+                   float *output, int act) {
+    float *h = (float *) malloc(batch * hidden_features * sizeof(float));
+    uint16_t *h16 = (uint16_t *) malloc(batch * hidden_features * sizeof(uint16_t));
+    int rc = -2;
+    if (h && h16) {
+        rc = orc_linear_f16f32(input, batch, in_features, fc1_weight, hidden_features, fc1_bias, h, act);
+        if (rc == 0) {
+            orc_floats_to_halves(h, h16, batch * hidden_features);
+            rc = orc_linear_f16f32(h16, batch, hidden_features, fc2_weight, out_features, fc2_bias,
+                                   output, ORC_ACT_NONE);
+        }
+    }
+    free(h);
+    free(h16);
+    return rc;
+}
+
+/*
+ * SwiGLU: g = in*Wg + bg, u = in*Wu + bu, h = fp16(silu(g) * u),
+ * out = h*Wd + bd.   sme_ai_swiglu_ref_f16f32, sme_ai_ops.c:1188-1225
+ * (silu :879-887, elementwise mul :801-814, fp16 round :175-179).
+ */
+int orc_swiglu_f16f32(const uint16_t *input, uint64_t batch, uint64_t in_features,
+                      const uint16_t *gate_weight, uint64_t hidden_features, const float *gate_bias,
+                      const uint16_t *up_weight, const float *up_bias,
+                      const uint16_t *down_weight, uint64_t out_features, const float *down_bias,
+                      float *output) {
+    uint64_t n = batch * hidden_features;
+    float *g = (float *) malloc(n * sizeof(float));
+    float *u = (float *) malloc(n * sizeof(float));
+    uint16_t *h16 = (uint16_t *) malloc(n * sizeof(uint16_t));
+    int rc = -2;
+    if (g && u && h16) {
+        rc = orc_linear_f16f32(input, batch, in_features, gate_weight, hidden_features, gate_bias, g, ORC_ACT_NONE);
+        if (rc == 0)
+            rc = orc_linear_f16f32(input, batch, in_features, up_weight, hidden_features, up_bias, u, ORC_ACT_NONE);
+        if (rc == 0) {
+            for (uint64_t i = 0; i < n; ++i) {
+                float s = g[i] / (1.0f + expf(-g[i]));
+                h16[i] = orc_float_to_half(s * u[i]);
+            }
+            rc = orc_linear_f16f32(h16, batch, hidden_features, down_weight, out_features, down_bias,
+                                   output, ORC_ACT_NONE);
+        }
+    }
+    free(g);
+    free(u);
+    free(h16);
+    return rc;
+}
+
+/*
+ * The reference's packed layout: packed[n_tile][k_pad][16] fp32, zero padded,
+ * k_pad/n_pad = round_up(., 16).  prepack_weight_fp16_to_sme_tiles,
+ * sme_ai_ops.c:281-301.  (Used by tests to document the reference layout.)
+ */
+void orc_pack_weight_f16_tiles(const uint16_t *weight, float *packed,
+                               uint64_t in_features, uint64_t out_features) {
+    uint64_t kpad = (in_features + 15) / 16 * 16;
+    uint64_t npad = (out_features + 15) / 16 * 16;
+    memset(packed, 0, kpad * npad * sizeof(float));
+    for (uint64_t c = 0; c < out_features; ++c)
+        for (uint64_t k = 0; k < in_features; ++k)
+            packed[(c / 16) * kpad * 16 + k * 16 + (c % 16)] =
+                orc_half_to_float(weight[k * out_features + c]);
+}
+
+/* ======================================================================== */
+/* Path B: ggml Q2_K x Q8_K (ggml 0.9.8 generic C, restated)                 */
+/* ======================================================================== */
+
+/*
+ * ggml's nearest_int: add 1.5*2^23 so that the float adder rounds to an
+ * integer (round-half-to-even), then read the integer out of the mantissa.
+ * Valid for |v| < 2^22.
+ */
+static int magic_round(float v_plus_magic) {
+    int32_t bits;
+    memcpy(&bits, &v_plus_magic, 4);
+    return (bits & 0x007fffff) - 0x00400000;
+}
+static const float kMagic = 12582912.0f;
+
+static int round_separate(float v) { return magic_round(v + kMagic); }
+
+/*
+ * quantize_row_q8_K (ggml-quants.c quantize_row_q8_K_ref; the activation
+ * quantizer the reference's Q2_K path runs on every src1 row,
+ * llama.cpp/doc/SME_Q2K_OPTIMIZATION.md:127-131).  Per 256 values:
+ *   - pick the value of largest magnitude (first one on ties), call it max;
+ *   - an all-zero block gives d = 0 and zero quants (bsums written as 0);
+ *   - iscale = -127/max; q = nearest(iscale*x) capped at 127;
+ *   - bsums[j] = sum of q[16j .. 16j+15];  d = 1/iscale.
+ * rounding = ORC_Q8K_ROUND_FUSED evaluates nearest(iscale*x) as one fused
+ * multiply-add with the magic constant -- what GCC's default
+ * -ffp-contract=fast makes of the inlined nearest_int on an FMA target such
+ * as the reference's AArch64 build; ORC_Q8K_ROUND_SEPARATE rounds the product
+ * first (a -ffp-contract=off build).
+ */
+void orc_quantize_row_q8_K(const float *x, orc_block_q8_K *y, int64_t k, int rounding) {
+    int64_t nb = k / ORC_QK_K;
+    for (int64_t b = 0; b < nb; ++b) {
+        const float *xb = x + b * ORC_QK_K;
+        float amax = 0.0f, vmax = 0.0f;
+        for (int j = 0; j < ORC_QK_K; ++j) {
+            float a = fabsf(xb[j]);
+            if (a > amax) { amax = a; vmax = xb[j]; }
+        }
+        memset(y[b].bsums, 0, sizeof(y[b].bsums));
+        if (amax == 0.0f) {
+            y[b].d = 0.0f;
+            memset(y[b].qs, 0, sizeof(y[b].qs));
+            continue;
+        }
+        float iscale = -127.0f / vmax;
+        for (int j = 0; j < ORC_QK_K; ++j) {
+            int q = rounding == ORC_Q8K_ROUND_FUSED ? magic_round(fmaf(iscale, xb[j], kMagic))
+                                                    : round_separate(iscale * xb[j]);
+            y[b].qs[j] = (int8_t) (q > 127 ? 127 : q);
+        }
+        for (int g = 0; g < 16; ++g) {
+            int s = 0;
+            for (int i = 0; i < 16; ++i) s += y[b].qs[16 * g + i];
+            y[b].bsums[g] = (int16_t) s;
+        }
+        y[b].d = 1.0f / iscale;
+    }
+}
+
+/*
+ * make_qkx2_quants restated (ggml-quants.c): fit x ~ scale*L + min over one
+ * 16-value group with L in [0, nmax], weighted by w, starting from the
+ * (min, max) range and then trying nstep+1 perturbed inverse scales with a
+ * weighted least-squares (scale, min) refit, keeping the best mean-absolute
+ * error.  Returns the scale; *neg_min receives -min (>= 0).
+ */
+static float fit_group(int n, int nmax, const float *x, const float *w, uint8_t *L,
+                       float *neg_min, float rmin, float rdelta, int nstep) {
+    uint8_t trial[16];
+    float lo = x[0], hi = x[0];
+    float sw = w[0], swx = w[0] * x[0];
+    for (int i = 1; i < n; ++i) {
+        if (x[i] < lo) lo = x[i];
+        if (x[i] > hi) hi = x[i];
+        sw += w[i];
+        swx += w[i] * x[i];
+    }
+    if (lo > 0.0f) lo = 0.0f;
+    if (hi == lo) {
+        memset(L, 0, (size_t) n);
+        *neg_min = -lo;
+        return 0.0f;
+    }
+    float inv = (float) nmax / (hi - lo);
+    float scale = 1.0f / inv;
+    float best = 0.0f;
+    for (int i = 0; i < n; ++i) {
+        int l = round_separate(inv * (x[i] - lo));
+        l = l < 0 ? 0 : (l > nmax ? nmax : l);
+        L[i] = (uint8_t) l;
+        float diff = scale * (float) l + lo - x[i];
+        best += w[i] * fabsf(diff);
+    }
+    for (int step = 0; step <= nstep; ++step) {
+        float inv_t = (rmin + rdelta * (float) step + (float) nmax) / (hi - lo);
+        float sl = 0.0f, sl2 = 0.0f, sxl = 0.0f;
+        for (int i = 0; i < n; ++i) {
+            int l = round_separate(inv_t * (x[i] - lo));
+            l = l < 0 ? 0 : (l > nmax ? nmax : l);
+            trial[i] = (uint8_t) l;
+            sl += w[i] * (float) l;
+            sl2 += w[i] * (float) l * (float) l;
+            sxl += w[i] * (float) l * x[i];
+        }
+        float det = sw * sl2 - sl * sl;
+        if (det > 0.0f) {
+            float s_t = (sw * sxl - swx * sl) / det;
+            float m_t = (sl2 * swx - sl * sxl) / det;
+            if (m_t > 0.0f) {
+                m_t = 0.0f;
+                s_t = sxl / sl2;
+            }
+            float err = 0.0f;
+            for (int i = 0; i < n; ++i) {
+                float diff = s_t * (float) trial[i] + m_t - x[i];
+                err += w[i] * fabsf(diff);
+            }
+            if (err < best) {
+                memcpy(L, trial, (size_t) n);
+                best = err;
+                scale = s_t;
+                lo = m_t;
+            }
+        }
+    }
+    *neg_min = -lo;
+    return scale;
+}
+
+/*
+ * quantize_row_q2_K (ggml-quants.c quantize_row_q2_K_ref restated): per
+ * 16-value group fit (scale, min) with fit_group(nmax = 3, rmin = -0.5,
+ * rdelta = 0.1, nstep = 15, |x| weights); quantize the 16 scales and 16 mins
+ * to 4 bits against their maxima (d = max_scale/15, dmin = max_min/15, fp16);
+ * requantize every value against the 4-bit-rounded (scale, min); pack four
+ * 2-bit values per byte, byte l of each 32-byte half holding values
+ * l, l+32, l+64, l+96 of that 128-value half at bit offsets 0, 2, 4, 6.
+ * This is the weight generator for tests and benchmarks; parity of the
+ * hot path is defined on identical blocks, so bit-identity with ggml's own
+ * quantizer is not required (and is not claimed).
+ */
+void orc_quantize_row_q2_K(const float *x, orc_block_q2_K *y, int64_t k) {
+    int64_t nb = k / ORC_QK_K;
+    for (int64_t b = 0; b < nb; ++b) {
+        const float *xb = x + b * ORC_QK_K;
+        uint8_t L[ORC_QK_K];
+        float wts[16], scales[16], mins[16];
+        float max_scale = 0.0f, max_min = 0.0f;
+        for (int g = 0; g < 16; ++g) {
+            for (int i = 0; i < 16; ++i) wts[i] = fabsf(xb[16 * g + i]);
+            scales[g] = fit_group(16, 3, xb + 16 * g, wts, L + 16 * g, &mins[g], -0.5f, 0.1f, 15);
+            if (scales[g] > max_scale) max_scale = scales[g];
+            if (mins[g] > max_min) max_min = mins[g];
+        }
+        memset(y[b].scales, 0, 16);
+        if (max_scale > 0.0f) {
+            float inv = 15.0f / max_scale;
+            for (int g = 0; g < 16; ++g) y[b].scales[g] = (uint8_t) round_separate(inv * scales[g]);
+            y[b].d = orc_float_to_half(max_scale / 15.0f);
+        } else {
+            y[b].d = orc_float_to_half(0.0f);
+        }
+        if (max_min > 0.0f) {
+            float inv = 15.0f / max_min;
+            for (int g = 0; g < 16; ++g)
+                y[b].scales[g] |= (uint8_t) (round_separate(inv * mins[g]) << 4);
+            y[b].dmin = orc_float_to_half(max_min / 15.0f);
+        } else {
+            y[b].dmin = orc_float_to_half(0.0f);
+        }
+        float dd = orc_half_to_float(y[b].d), dm = orc_half_to_float(y[b].dmin);
+        for (int g = 0; g < 16; ++g) {
+            float ds = dd * (float) (y[b].scales[g] & 0xF);
+            if (ds == 0.0f) continue;
+            float ms = dm * (float) (y[b].scales[g] >> 4);
+            for (int i = 0; i < 16; ++i) {
+                int l = round_separate((xb[16 * g + i] + ms) / ds);
+                L[16 * g + i] = (uint8_t) (l < 0 ? 0 : (l > 3 ? 3 : l));
+            }
+        }
+        for (int half = 0; half < 2; ++half)
+            for (int l = 0; l < 32; ++l) {
+                const uint8_t *s = L + half * 128 + l;
+                y[b].qs[half * 32 + l] = (uint8_t) (s[0] | (s[32] << 2) | (s[64] << 4) | (s[96] << 6));
+            }
+    }
+}
+
+/* Value i of a Q2_K block: d*sc_j*q_i - dmin*m_j, j = i/16 (the layout
+ * gguf-py Q2_K.dequantize_blocks decodes, gguf/quants.py:404-428). */
+void orc_dequantize_row_q2_K(const orc_block_q2_K *x, float *y, int64_t k) {
+    int64_t nb = k / ORC_QK_K;
+    for (int64_t b = 0; b < nb; ++b) {
+        float d = orc_half_to_float(x[b].d), dmin = orc_half_to_float(x[b].dmin);
+        for (int i = 0; i < ORC_QK_K; ++i) {
+            int half = i / 128, within = i % 128, shift = 2 * (within / 32), l = within % 32;
+            int q = (x[b].qs[half * 32 + l] >> shift) & 3;
+            int j = i / 16;
+            float dl = d * (float) (x[b].scales[j] & 0xF);
+            float ml = dmin * (float) (x[b].scales[j] >> 4);
+            y[b * ORC_QK_K + i] = dl * (float) q - ml;
+        }
+    }
+}
+
+/*
+ * The integer part of ggml_vec_dot_q2_K_q8_K (generic C) for each super-block:
+ *   isum  = sum_j sc_j * sum_{i in sub-block j} q2_i * q8_i
+ *   summs = sum_j m_j  * bsums_j
+ * These are exact integers; the GPU kernels must reproduce them bit for bit.
+ */
+void orc_q2k_block_sums(int n, const orc_block_q2_K *x, const orc_block_q8_K *y,
+                        int32_t *isum, int32_t *summs) {
+    int nb = n / ORC_QK_K;
+    for (int b = 0; b < nb; ++b) {
+        int32_t mm = 0;
+        for (int j = 0; j < 16; ++j) mm += (int32_t) y[b].bsums[j] * (int32_t) (x[b].scales[j] >> 4);
+        int32_t acc = 0;
+        for (int j = 0; j < 16; ++j) {
+            int32_t part = 0;
+            for (int t = 0; t < 16; ++t) {
+                int i = 16 * j + t;
+                int half = i / 128, within = i % 128, shift = 2 * (within / 32), l = within % 32;
+                int q = (x[b].qs[half * 32 + l] >> shift) & 3;
+                part += q * (int32_t) y[b].qs[i];
+            }
+            acc += (int32_t) (x[b].scales[j] & 0xF) * part;
+        }
+        isum[b] = acc;
+        summs[b] = mm;
+    }
+}
+
+/*
+ * ggml_vec_dot_q2_K_q8_K (generic C, nrc == 1): per super-block
+ *   dall = d_y * fp32(d_x),  dmin = d_y * fp32(dmin_x)
+ *   sumf += dall*isum - dmin*summs          (blocks in ascending order)
+ * combine = ORC_COMBINE_FUSED evaluates the term as
+ * fmaf(dall, isum, -(dmin*summs)), which is what GCC's default contraction
+ * forms from that expression on an FMA target (the first product is fused
+ * into the subtraction); ORC_COMBINE_SEPARATE rounds both products.
+ */
+float orc_vec_dot_q2_K_q8_K(int n, const orc_block_q2_K *x, const orc_block_q8_K *y, int combine) {
+    int nb = n / ORC_QK_K;
+    float sumf = 0.0f;
+    for (int b = 0; b < nb; ++b) {
+        int32_t isum, summs;
+        orc_q2k_block_sums(ORC_QK_K, x + b, y + b, &isum, &summs);
+        float dall = y[b].d * orc_half_to_float(x[b].d);
+        float dmin = y[b].d * orc_half_to_float(x[b].dmin);
+        float term;
+        if (combine == ORC_COMBINE_FUSED) {
+            term = fmaf(dall, (float) isum, -(dmin * (float) summs));
+        } else {
+            float t1 = dall * (float) isum;
+            float t2 = dmin * (float) summs;
+            term = t1 - t2;
+        }
+        sumf = sumf + term;
+    }
+    return sumf;
+}
+
+/*
+ * mul_mat of a Q2_K weight [n_rows, k] with Q8_K activations [n_cols, k]:
+ * y[c*ldy + r] = vec_dot(row r, col c) -- ggml's dst layout (ne0 = rows
+ * contiguous).  Rows are split over n_threads like ggml's CPU threads.
+ */
+void orc_q2k_mul_mat(const orc_block_q2_K *w, int64_t n_rows, int64_t k,
+                     const orc_block_q8_K *xq, int64_t n_cols, float *y, int64_t ldy,
+                     int combine, int n_threads) {
+    int64_t nb = k / ORC_QK_K;
+#ifdef _OPENMP
+    if (n_threads < 1) n_threads = 1;
+#pragma omp parallel for schedule(static) num_threads(n_threads)
+#endif
+    for (int64_t r = 0; r < n_rows; ++r)
+        for (int64_t c = 0; c < n_cols; ++c)
+            y[c * ldy + r] = orc_vec_dot_q2_K_q8_K((int) k, w + r * nb, xq + c * nb, combine);
+    (void) n_threads;
+}
+
+/* ======================================================================== */
+/* Decode-stack helpers (RMSNorm is the reference's sme_ai_rmsnorm_f32,      */
+/* sme_ai_ops.c:1060-1092: y = x / sqrt(mean(x^2) + eps)).  The sum of       */
+/* squares is taken in the fixed order the GPU kernel uses, so both sides    */
+/* round identically: per 256-value block, 32 partial sums of 8 consecutive  */
+/* squares (fused, ascending), folded pairwise at distances 16, 8, 4, 2, 1;  */
+/* then the block sums added in ascending block order.                       */
+/* ======================================================================== */
+float orc_rms_inv(const float *x, int64_t k, float eps) {
+    int64_t nb = k / ORC_QK_K;
+    float total = 0.0f;
+    for (int64_t b = 0; b < nb; ++b) {
+        float part[32];
+        for (int l = 0; l < 32; ++l) {
+            float s = 0.0f;
+            for (int i = 0; i < 8; ++i) {
+                float v = x[b * ORC_QK_K + l * 8 + i];
+                s = fmaf(v, v, s);
+            }
+            part[l] = s;
+        }
+        for (int width = 16; width >= 1; width /= 2)
+            for (int l = 0; l < width; ++l) part[l] = part[l] + part[l + width];
+        total = total + part[0];
+    }
+    float mean = total / (float) k;
+    return 1.0f / sqrtf(mean + eps);
+}
+
+void orc_rmsnorm_quantize_q8_K(const float *x, orc_block_q8_K *y, int64_t k, float eps, int rounding) {
+    float inv = orc_rms_inv(x, k, eps);
+    float *tmp = (float *) malloc((size_t) k * sizeof(float));
+    for (int64_t i = 0; i < k; ++i) tmp[i] = x[i] * inv;
+    orc_quantize_row_q8_K(tmp, y, k, rounding);
+    free(tmp);
+}
+
+/* h = silu(g) * u with silu(g) = g / (1 + expf(-g)), sme_ai_ops.c:879-887
+ * then :801-814. */
+void orc_silu_mul(const float *g, const float *u, float *h, int64_t n) {
+    for (int64_t i = 0; i < n; ++i) {
+        float s = g[i] / (1.0f + expf(-g[i]));
+        h[i] = s * u[i];
+    }
+}

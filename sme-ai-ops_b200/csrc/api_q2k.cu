@@ -1,0 +1,261 @@
+// api_q2k.cu -- the C-ABI of include/smeai_q2k.h.
+#include <map>
+#include <mutex>
+#include <string.h>
+#include <utility>
+
+#include "common.cuh"
+#include "kernels.h"
+#include "runtime.h"
+#include "../../include/smeai_q2k.h"
+
+using namespace smeai;
+
+namespace {
+
+constexpr uint32_t kHandleMagic = 0x51324b57u;  // "Q2KW"
+
+struct Handle {
+  uint32_t magic = kHandleMagic;
+  Q2KWeight w;
+};
+
+const Handle* as_handle(const void* p) {
+  const Handle* h = static_cast<const Handle*>(p);
+  if (!h || h->magic != kHandleMagic) {
+    set_last_error("not a repacked Q2_K weight handle");
+    return nullptr;
+  }
+  return h;
+}
+
+cudaStream_t as_stream(void* s) { return static_cast<cudaStream_t>(s); }
+
+// Per-thread state of the ggml-shaped entry points: own stream + staging.
+struct ThreadCtx {
+  cudaStream_t stream = nullptr;
+  Staged a, b;
+  DeviceBuffer tiles, y;
+  int init() {
+    if (stream) return kOk;
+    SMEAI_CUDA_TRY(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking));
+    return kOk;
+  }
+};
+
+ThreadCtx& tctx() {
+  thread_local ThreadCtx ctx;
+  return ctx;
+}
+
+// Library-owned Q8_K scratch for smeai_q2k_mul_mat_f32, one per (device, stream).
+std::mutex g_scratch_mu;
+std::map<std::pair<int, cudaStream_t>, DeviceBuffer*> g_scratch;
+
+void* scratch_for(cudaStream_t s, size_t bytes, int* st) {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::lock_guard<std::mutex> lock(g_scratch_mu);
+  DeviceBuffer*& b = g_scratch[{dev, s}];
+  if (!b) b = new DeviceBuffer();
+  *st = b->reserve(bytes);
+  return *st == kOk ? b->ptr : nullptr;
+}
+
+}  // namespace
+
+extern "C" {
+
+int smeai_device_ready(void) { return device_ready() ? 1 : 0; }
+
+const char* smeai_last_error(void) { return last_error(); }
+
+// ---- ggml-shaped entry points ------------------------------------------------
+
+void quantize_row_q8_K(const float* x, void* y, int64_t k) {
+  if (!x || !y || k <= 0 || k % QK_K) {
+    set_last_error("quantize_row_q8_K: k must be a positive multiple of 256");
+    return;
+  }
+  ThreadCtx& c = tctx();
+  const size_t out_bytes = (size_t)(k / QK_K) * Q8K_BLOCK_BYTES;
+  if (c.init() || c.a.in(x, (size_t)k * 4, c.stream) || c.b.out(y, out_bytes) ||
+      q8k_quantize(static_cast<const float*>(c.a.dev), k, 1, k, c.b.dev, c.stream) || c.b.finish(c.stream) ||
+      cudaStreamSynchronize(c.stream) != cudaSuccess) {
+    if (!is_device_pointer(y)) memset(y, 0, out_bytes);
+  }
+}
+
+void quantize_row_q2_K(const float* x, void* y, int64_t k) {
+  if (!x || !y || k <= 0 || k % QK_K) {
+    set_last_error("quantize_row_q2_K: k must be a positive multiple of 256");
+    return;
+  }
+  ThreadCtx& c = tctx();
+  const size_t out_bytes = (size_t)(k / QK_K) * Q2K_BLOCK_BYTES;
+  if (c.init() || c.a.in(x, (size_t)k * 4, c.stream) || c.b.out(y, out_bytes) ||
+      q2k_quantize(static_cast<const float*>(c.a.dev), k, c.b.dev, c.stream) || c.b.finish(c.stream) ||
+      cudaStreamSynchronize(c.stream) != cudaSuccess) {
+    if (!is_device_pointer(y)) memset(y, 0, out_bytes);
+  }
+}
+
+void dequantize_row_q2_K(const void* x, float* y, int64_t k) {
+  if (!x || !y || k <= 0 || k % QK_K) {
+    set_last_error("dequantize_row_q2_K: k must be a positive multiple of 256");
+    return;
+  }
+  ThreadCtx& c = tctx();
+  if (c.init() || c.a.in(x, (size_t)(k / QK_K) * Q2K_BLOCK_BYTES, c.stream) || c.b.out(y, (size_t)k * 4) ||
+      q2k_dequantize(c.a.dev, k, static_cast<float*>(c.b.dev), c.stream) || c.b.finish(c.stream) ||
+      cudaStreamSynchronize(c.stream) != cudaSuccess) {
+    if (!is_device_pointer(y)) memset(y, 0, (size_t)k * 4);
+  }
+}
+
+void ggml_vec_dot_q2_K_q8_K(int n, float* s, size_t bs, const void* vx, size_t bx, const void* vy, size_t by,
+                            int nrc) {
+  (void)bs;
+  (void)bx;
+  (void)by;
+  if (!s) return;
+  *s = 0.f;
+  if (!vx || !vy || n <= 0 || n % QK_K || nrc != 1) {
+    set_last_error("ggml_vec_dot_q2_K_q8_K: needs n %% 256 == 0 and nrc == 1");
+    return;
+  }
+  ThreadCtx& c = tctx();
+  const int64_t nb = n / QK_K;
+  Q2KWeight w;
+  if (c.init() || c.a.in(vx, nb * Q2K_BLOCK_BYTES, c.stream) || c.b.in(vy, nb * Q8K_BLOCK_BYTES, c.stream) ||
+      c.tiles.reserve(q2k_tile_bytes(1, n)) || c.y.reserve(4) ||
+      q2k_repack_into(c.a.dev, 1, n, static_cast<uint8_t*>(c.tiles.ptr), &w, c.stream) ||
+      q2k_gemv(w, c.b.dev, 1, static_cast<float*>(c.y.ptr), 1, kEpiStore, nullptr, 0, c.stream) ||
+      cudaMemcpyAsync(s, c.y.ptr, 4, cudaMemcpyDeviceToHost, c.stream) != cudaSuccess ||
+      cudaStreamSynchronize(c.stream) != cudaSuccess) {
+    *s = 0.f;
+  }
+}
+
+// ---- coarse GPU entry points ---------------------------------------------------
+
+int smeai_q2k_repack(const void* w_q2k, int64_t n_rows, int64_t k, void** w_dev_out) {
+  if (!w_q2k || !w_dev_out || n_rows <= 0 || k <= 0 || k % QK_K) {
+    set_last_error("smeai_q2k_repack: bad arguments");
+    return kBadArgument;
+  }
+  *w_dev_out = nullptr;
+  if (!device_ready()) {
+    set_last_error("smeai_q2k_repack: no compute-capability-10.x device");
+    return kUnsupported;
+  }
+  Staged src;
+  const size_t bytes = (size_t)n_rows * (size_t)(k / QK_K) * Q2K_BLOCK_BYTES;
+  int st = src.in(w_q2k, bytes, nullptr);
+  if (st) return st;
+  Handle* h = new Handle();
+  st = q2k_repack(src.dev, n_rows, k, &h->w, nullptr);
+  if (st == kOk && cudaStreamSynchronize(nullptr) != cudaSuccess) {
+    set_last_error("smeai_q2k_repack: %s", cudaGetErrorString(cudaGetLastError()));
+    st = kCudaError;
+  }
+  if (st) {
+    if (h->w.tiles) cudaFree(h->w.tiles);
+    delete h;
+    return st;
+  }
+  *w_dev_out = h;
+  return kOk;
+}
+
+void smeai_q2k_free(void* w_dev) {
+  Handle* h = static_cast<Handle*>(w_dev);
+  if (!h || h->magic != kHandleMagic) return;
+  if (h->w.tiles) cudaFree(h->w.tiles);
+  h->magic = 0;
+  delete h;
+}
+
+size_t smeai_q2k_weight_bytes(const void* w_dev) {
+  const Handle* h = as_handle(w_dev);
+  return h ? h->w.bytes : 0;
+}
+
+int smeai_q8k_quantize(const float* x_dev, int64_t ld_x, int64_t n_cols, int64_t k, void* y_q8k_dev,
+                       void* stream) {
+  if (!x_dev || !y_q8k_dev) {
+    set_last_error("smeai_q8k_quantize: NULL pointer");
+    return kBadArgument;
+  }
+  return q8k_quantize(x_dev, ld_x, n_cols, k, y_q8k_dev, as_stream(stream));
+}
+
+int smeai_rms_q8k_quantize(const float* x_dev, int64_t ld_x, int64_t n_cols, int64_t k, float eps,
+                           void* y_q8k_dev, void* stream) {
+  if (!x_dev || !y_q8k_dev) {
+    set_last_error("smeai_rms_q8k_quantize: NULL pointer");
+    return kBadArgument;
+  }
+  return rms_q8k_quantize(x_dev, ld_x, n_cols, k, eps, y_q8k_dev, as_stream(stream));
+}
+
+int smeai_q2k_mul_mat(const void* w_dev, int64_t n_rows, int64_t k, const void* x_q8k_dev, int64_t n_cols,
+                      float* y_dev, size_t ldy, void* stream) {
+  const Handle* h = as_handle(w_dev);
+  if (!h) return kBadArgument;
+  if (h->w.n_rows != n_rows || h->w.k != k) {
+    set_last_error("smeai_q2k_mul_mat: shape [%lld,%lld] does not match the handle [%lld,%lld]",
+                   (long long)n_rows, (long long)k, (long long)h->w.n_rows, (long long)h->w.k);
+    return kBadArgument;
+  }
+  return q2k_gemv(h->w, x_q8k_dev, n_cols, y_dev, (int64_t)ldy, kEpiStore, nullptr, 0, as_stream(stream));
+}
+
+int smeai_q2k_mul_mat_ex(const void* w_dev, const void* x_q8k_dev, int64_t n_cols, float* y_dev, size_t ldy,
+                         int epilogue, const float* resid_dev, size_t ld_resid, void* stream) {
+  const Handle* h = as_handle(w_dev);
+  if (!h) return kBadArgument;
+  return q2k_gemv(h->w, x_q8k_dev, n_cols, y_dev, (int64_t)ldy, epilogue, resid_dev, (int64_t)ld_resid,
+                  as_stream(stream));
+}
+
+int smeai_q2k_mul_mat_f32(const void* w_dev, const float* x_dev, int64_t n_cols, float* y_dev, size_t ldy,
+                          void* stream) {
+  const Handle* h = as_handle(w_dev);
+  if (!h) return kBadArgument;
+  if (!x_dev || !y_dev || n_cols <= 0) {
+    set_last_error("smeai_q2k_mul_mat_f32: bad arguments");
+    return kBadArgument;
+  }
+  int st = kOk;
+  void* xq = scratch_for(as_stream(stream), (size_t)n_cols * h->w.nb * Q8K_BLOCK_BYTES, &st);
+  if (st) return st;
+  st = q8k_quantize(x_dev, h->w.k, n_cols, h->w.k, xq, as_stream(stream));
+  if (st) return st;
+  return q2k_gemv(h->w, xq, n_cols, y_dev, (int64_t)ldy, kEpiStore, nullptr, 0, as_stream(stream));
+}
+
+int smeai_q2k_block_sums(const void* w_dev, const void* x_q8k_dev, int32_t* isum_dev, int32_t* summs_dev,
+                         void* stream) {
+  const Handle* h = as_handle(w_dev);
+  if (!h) return kBadArgument;
+  return q2k_block_sums(h->w, x_q8k_dev, isum_dev, summs_dev, as_stream(stream));
+}
+
+int smeai_q2k_quantize_device(const float* x_dev, int64_t n, void* y_q2k_dev, void* stream) {
+  if (!x_dev || !y_q2k_dev) {
+    set_last_error("smeai_q2k_quantize_device: NULL pointer");
+    return kBadArgument;
+  }
+  return q2k_quantize(x_dev, n, y_q2k_dev, as_stream(stream));
+}
+
+int smeai_q2k_dequantize_device(const void* w_q2k_dev, int64_t n, float* y_dev, void* stream) {
+  if (!w_q2k_dev || !y_dev) {
+    set_last_error("smeai_q2k_dequantize_device: NULL pointer");
+    return kBadArgument;
+  }
+  return q2k_dequantize(w_q2k_dev, n, y_dev, as_stream(stream));
+}
+
+}  // extern "C"

@@ -1,0 +1,57 @@
+// kernels.h -- host-side launchers of the sm_100a kernels (internal to the
+// library; the public C entry points live in include/*.h).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace smeai {
+
+// ---- Q8_K activation quantizer (q8k_quant.cu) ----
+int q8k_quantize(const float* x, int64_t ld_x, int64_t n_rows, int64_t k, void* y, cudaStream_t stream);
+int rms_q8k_quantize(const float* x, int64_t ld_x, int64_t n_rows, int64_t k, float eps, void* y,
+                     cudaStream_t stream);
+
+// ---- Q2_K weight quantizer / decoder (q2k_quant.cu) ----
+int q2k_quantize(const float* x, int64_t k_total, void* y, cudaStream_t stream);
+int q2k_dequantize(const void* w, int64_t k_total, float* y, cudaStream_t stream);
+
+// ---- Q2_K weights in the device tile layout (q2k_gemv.cu) ----
+// Rows are grouped by 32; group g, super-block b is one 2688-byte tile:
+//   qs     4 x [32 rows][16 B]   (chunk c holds qs bytes 16c..16c+15)
+//   scales    [32 rows][16 B]
+//   d,dmin    [32 rows][4 B]
+constexpr int kRowsPerGroup = 32;
+constexpr int kTileBytes = 32 * 84;
+
+struct Q2KWeight {
+  int64_t n_rows = 0;
+  int64_t k = 0;
+  int nb = 0;           // super-blocks per row
+  int64_t n_groups = 0; // ceil(n_rows / 32)
+  uint8_t* tiles = nullptr;  // device, n_groups * nb * kTileBytes
+  size_t bytes = 0;
+  int device = 0;
+};
+
+int q2k_repack(const void* w_blocks_dev, int64_t n_rows, int64_t k, Q2KWeight* out, cudaStream_t stream);
+// Same, into caller-provided tiles (tile_bytes(n_rows, k) bytes); allocates nothing.
+size_t q2k_tile_bytes(int64_t n_rows, int64_t k);
+int q2k_repack_into(const void* w_blocks_dev, int64_t n_rows, int64_t k, uint8_t* tiles, Q2KWeight* out,
+                    cudaStream_t stream);
+
+enum Epilogue : int {
+  kEpiStore = 0,     // y[c*ldy + r] = acc
+  kEpiResidual = 1,  // y[c*ldy + r] = resid[c*ld_resid + r] + acc   (resid may alias y)
+  kEpiSiluMul = 2,   // rows interleaved (gate, up): y[c*ldy + r/2] = silu(gate) * up
+};
+
+// y = W x for n_cols Q8_K activation rows (ggml layout, contiguous rows).
+int q2k_gemv(const Q2KWeight& w, const void* xq, int64_t n_cols, float* y, int64_t ldy, int epilogue,
+             const float* resid, int64_t ld_resid, cudaStream_t stream);
+
+// Per-(row, super-block) integer sums (isum, summs), [n_rows][nb] each, for a
+// single activation row -- the exactness check of the GEMV's integer core.
+int q2k_block_sums(const Q2KWeight& w, const void* xq, int32_t* isum, int32_t* summs, cudaStream_t stream);
+
+}  // namespace smeai

@@ -1,0 +1,128 @@
+"""Q2_K x Q8_K path over torch device memory (thin wrappers of smeai_q2k.h)."""
+from __future__ import annotations
+
+import ctypes
+
+import numpy as np
+import torch
+
+from . import (EPI_RESIDUAL, EPI_SILU_MUL, EPI_STORE, Q2K_BLOCK_BYTES, Q8K_BLOCK_BYTES, QK_K, check,
+               lib)
+
+
+def _ptr(t):
+    return ctypes.c_void_p(0 if t is None else t.data_ptr())
+
+
+def cur_stream() -> ctypes.c_void_p:
+    return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+
+def quantize_q8k(x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """fp32 [n, k] (cuda) -> ggml block_q8_K rows, uint8 [n, k/256*292]."""
+    x2 = x.reshape(-1, x.shape[-1])
+    n, k = x2.shape
+    assert x2.dtype == torch.float32 and x2.is_cuda and x2.stride(1) == 1
+    if out is None:
+        out = torch.empty((n, k // QK_K * Q8K_BLOCK_BYTES), dtype=torch.uint8, device=x.device)
+    check(lib().smeai_q8k_quantize(_ptr(x2), x2.stride(0), n, k, _ptr(out), cur_stream()), "q8k_quantize")
+    return out
+
+
+def rms_quantize_q8k(x: torch.Tensor, eps: float, out: torch.Tensor | None = None) -> torch.Tensor:
+    x2 = x.reshape(-1, x.shape[-1])
+    n, k = x2.shape
+    assert x2.dtype == torch.float32 and x2.is_cuda and x2.stride(1) == 1
+    if out is None:
+        out = torch.empty((n, k // QK_K * Q8K_BLOCK_BYTES), dtype=torch.uint8, device=x.device)
+    check(lib().smeai_rms_q8k_quantize(_ptr(x2), x2.stride(0), n, k, ctypes.c_float(eps), _ptr(out),
+                                        cur_stream()), "rms_q8k_quantize")
+    return out
+
+
+def quantize_q2k(x: torch.Tensor) -> torch.Tensor:
+    """fp32 [rows, k] (cuda) -> ggml block_q2_K rows, uint8 [rows, k/256*84]."""
+    x2 = x.reshape(-1, x.shape[-1]).contiguous()
+    rows, k = x2.shape
+    out = torch.empty((rows, k // QK_K * Q2K_BLOCK_BYTES), dtype=torch.uint8, device=x.device)
+    check(lib().smeai_q2k_quantize_device(_ptr(x2), x2.numel(), _ptr(out), cur_stream()), "q2k_quantize")
+    return out
+
+
+def dequantize_q2k(blocks: torch.Tensor, k: int) -> torch.Tensor:
+    rows = blocks.numel() // (k // QK_K * Q2K_BLOCK_BYTES)
+    out = torch.empty((rows, k), dtype=torch.float32, device=blocks.device)
+    check(lib().smeai_q2k_dequantize_device(_ptr(blocks), rows * k, _ptr(out), cur_stream()), "q2k_dequantize")
+    return out
+
+
+def as_bytes(blocks) -> np.ndarray:
+    """numpy structured blocks / raw bytes -> flat uint8 view."""
+    return np.ascontiguousarray(blocks).view(np.uint8).reshape(-1)
+
+
+class Q2KMatrix:
+    """A Q2_K weight [n_rows, k] repacked into the device tile layout."""
+
+    def __init__(self, blocks, n_rows: int, k: int):
+        assert k % QK_K == 0
+        self.n_rows, self.k, self.nb = n_rows, k, k // QK_K
+        handle = ctypes.c_void_p()
+        if isinstance(blocks, torch.Tensor):
+            src = blocks.contiguous()
+            ptr = _ptr(src)
+            torch.cuda.current_stream().synchronize() if src.is_cuda else None
+        else:
+            src = as_bytes(blocks)
+            ptr = ctypes.c_void_p(src.ctypes.data)
+        assert (src.numel() if isinstance(src, torch.Tensor) else src.size) == n_rows * self.nb * Q2K_BLOCK_BYTES
+        check(lib().smeai_q2k_repack(ptr, n_rows, k, ctypes.byref(handle)), "q2k_repack")
+        self.handle = handle
+        self.bytes = lib().smeai_q2k_weight_bytes(handle)
+
+    def mul_mat(self, xq: torch.Tensor, n_cols: int, out: torch.Tensor | None = None, epilogue: int = EPI_STORE,
+                resid: torch.Tensor | None = None) -> torch.Tensor:
+        out_rows = self.n_rows // 2 if epilogue == EPI_SILU_MUL else self.n_rows
+        if out is None:
+            out = torch.empty((n_cols, out_rows), dtype=torch.float32, device=xq.device)
+        ldy = out.stride(0) if out.dim() == 2 else out_rows
+        if epilogue == EPI_STORE:
+            st = lib().smeai_q2k_mul_mat(self.handle, self.n_rows, self.k, _ptr(xq), n_cols, _ptr(out), ldy,
+                                         cur_stream())
+        else:
+            ldr = 0 if resid is None else (resid.stride(0) if resid.dim() == 2 else out_rows)
+            st = lib().smeai_q2k_mul_mat_ex(self.handle, _ptr(xq), n_cols, _ptr(out), ldy, epilogue,
+                                            _ptr(resid), ldr, cur_stream())
+        check(st, "q2k_mul_mat")
+        return out
+
+    def mul_mat_f32(self, x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+        x2 = x.reshape(-1, self.k).contiguous()
+        n_cols = x2.shape[0]
+        if out is None:
+            out = torch.empty((n_cols, self.n_rows), dtype=torch.float32, device=x.device)
+        check(lib().smeai_q2k_mul_mat_f32(self.handle, _ptr(x2), n_cols, _ptr(out), out.stride(0), cur_stream()),
+              "q2k_mul_mat_f32")
+        return out
+
+    def block_sums(self, xq: torch.Tensor):
+        isum = torch.empty((self.n_rows, self.nb), dtype=torch.int32, device=xq.device)
+        summs = torch.empty_like(isum)
+        check(lib().smeai_q2k_block_sums(self.handle, _ptr(xq), _ptr(isum), _ptr(summs), cur_stream()),
+              "q2k_block_sums")
+        return isum, summs
+
+    def free(self):
+        if self.handle:
+            lib().smeai_q2k_free(self.handle)
+            self.handle = ctypes.c_void_p()
+
+    def __del__(self):
+        try:
+            self.free()
+        except Exception:
+            pass
+
+
+__all__ = ["quantize_q8k", "rms_quantize_q8k", "quantize_q2k", "dequantize_q2k", "Q2KMatrix", "as_bytes",
+           "EPI_STORE", "EPI_RESIDUAL", "EPI_SILU_MUL"]

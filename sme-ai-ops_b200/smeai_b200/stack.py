@@ -1,0 +1,194 @@
+"""Llama-2-7B-shape Q2_K linear stack (the decode/prefill benchmark workload).
+
+Per layer, with the inputs of every linear re-quantized to Q8_K:
+    xq  = Q8_K(rmsnorm(x))
+    qkv = [Wq; Wk; Wv] xq                       (one fused GEMV, 3 x 4096 rows)
+    v   = qkv[v]   -- attention over a single position returns v itself, so
+                      the attention math is skipped without changing shapes
+    x   = x + Wo Q8_K(v)                        (residual fused in the epilogue)
+    h   = silu(Wg xq') * (Wu xq'),  xq' = Q8_K(rmsnorm(x))
+                                                (gate/up rows interleaved, one GEMV
+                                                 with the silu*mul epilogue)
+    x   = x + Wd Q8_K(h)
+then logits = Wlm Q8_K(rmsnorm(x)).
+
+Multi-GPU: every weight is row-sharded over the ranks (32-row aligned slices
+of each of Wq/Wk/Wv/Wo/Wg/Wu/Wd/Wlm); activations are replicated and each
+linear's output slices are all-gathered over NCCL.  Weights are drawn from a
+seeded N(0, std) per full matrix and sliced, so every world size computes the
+same model.
+"""
+from __future__ import annotations
+
+import math
+
+import torch
+
+from . import EPI_RESIDUAL, EPI_SILU_MUL, EPI_STORE, Q2K_BLOCK_BYTES, Q8K_BLOCK_BYTES, QK_K
+from . import q2k as Q
+
+LLAMA7B = dict(n_layers=32, hidden=4096, ffn=11008, vocab=32000)
+
+
+def shard_range(n: int, rank: int, world: int, align: int = 32):
+    """Contiguous row slice of rank `rank`: multiples of `align` except the last."""
+    per = int(math.ceil(n / world / align)) * align
+    lo = min(n, rank * per)
+    hi = min(n, lo + per)
+    return lo, hi
+
+
+def gemv_bytes(rows: int, k: int, cols: int, out_rows: int | None = None) -> int:
+    """Algorithmic bytes of one Q2_K GEMV: weights + Q8_K activations + fp32 out."""
+    nb = k // QK_K
+    out_rows = rows if out_rows is None else out_rows
+    return rows * nb * Q2K_BLOCK_BYTES + cols * nb * Q8K_BLOCK_BYTES + cols * out_rows * 4
+
+
+class Q2KDecodeStack:
+    def __init__(self, n_layers=32, hidden=4096, ffn=11008, vocab=32000, batch=1, rank=0, world=1,
+                 device=None, seed=0, std=0.02, eps=1e-5, group=None):
+        self.L, self.H, self.F, self.V = n_layers, hidden, ffn, vocab
+        self.B, self.rank, self.world, self.eps, self.group = batch, rank, world, eps, group
+        self.dev = device or torch.device("cuda", torch.cuda.current_device())
+        assert hidden % QK_K == 0 and ffn % QK_K == 0
+        self.h_lo, self.h_hi = shard_range(hidden, rank, world)
+        self.f_lo, self.f_hi = shard_range(ffn, rank, world)
+        self.v_lo, self.v_hi = shard_range(vocab, rank, world)
+        hs, fs, vs = self.h_hi - self.h_lo, self.f_hi - self.f_lo, self.v_hi - self.v_lo
+        self.hs, self.fs, self.vs = hs, fs, vs
+        self.layers = []
+        self.weight_bytes = 0
+        for li in range(n_layers):
+            wq, wk, wv = (self._draw(seed, li, m, hidden, hidden, self.h_lo, self.h_hi, std) for m in range(3))
+            wqkv = Q.Q2KMatrix(torch.cat([wq, wk, wv], 0), 3 * hs, hidden)
+            del wq, wk, wv
+            wo = Q.Q2KMatrix(self._draw(seed, li, 3, hidden, hidden, self.h_lo, self.h_hi, std), hs, hidden)
+            wg = self._draw(seed, li, 4, ffn, hidden, self.f_lo, self.f_hi, std)
+            wu = self._draw(seed, li, 5, ffn, hidden, self.f_lo, self.f_hi, std)
+            wgu = Q.Q2KMatrix(torch.stack([wg, wu], 1).reshape(2 * fs, -1), 2 * fs, hidden)
+            del wg, wu
+            wd = Q.Q2KMatrix(self._draw(seed, li, 6, hidden, ffn, self.h_lo, self.h_hi, std), hs, ffn)
+            self.layers.append((wqkv, wo, wgu, wd))
+            self.weight_bytes += wqkv.n_rows * wqkv.nb * 84 + wo.n_rows * wo.nb * 84 + \
+                wgu.n_rows * wgu.nb * 84 + wd.n_rows * wd.nb * 84
+        self.lm = Q.Q2KMatrix(self._draw(seed, n_layers, 7, vocab, hidden, self.v_lo, self.v_hi, std), vs, hidden)
+        self.weight_bytes += self.lm.n_rows * self.lm.nb * 84
+        torch.cuda.synchronize()
+        B, d, f32, u8 = batch, self.dev, torch.float32, torch.uint8
+        self.x0 = torch.randn((B, hidden), generator=torch.Generator(device=d).manual_seed(seed + 12345),
+                              device=d, dtype=f32)
+        self.x = torch.empty_like(self.x0)
+        self.xq = torch.empty((B, hidden // QK_K * Q8K_BLOCK_BYTES), dtype=u8, device=d)
+        self.qkv = torch.empty((B, 3 * hs), dtype=f32, device=d)
+        self.v_full = torch.empty((B, hidden), dtype=f32, device=d)
+        self.vq = torch.empty_like(self.xq)
+        self.x_loc = torch.empty((B, hs), dtype=f32, device=d)
+        self.h_loc = torch.empty((B, fs), dtype=f32, device=d)
+        self.h_full = torch.empty((B, ffn), dtype=f32, device=d)
+        self.hq = torch.empty((B, ffn // QK_K * Q8K_BLOCK_BYTES), dtype=u8, device=d)
+        self.lg_loc = torch.empty((B, vs), dtype=f32, device=d)
+        self.logits = torch.empty((B, vocab), dtype=f32, device=d)
+
+    # --------------------------------------------------------------- weights
+    def _draw(self, seed, layer, mat, rows, k, lo, hi, std):
+        g = torch.Generator(device=self.dev).manual_seed(seed * 1_000_003 + layer * 16 + mat)
+        # draw the full matrix in row chunks with one generator: identical for every world size
+        out = None
+        chunk = max(1, (1 << 27) // k)
+        for r0 in range(0, rows, chunk):
+            r1 = min(rows, r0 + chunk)
+            w = torch.randn((r1 - r0, k), generator=g, device=self.dev) * std
+            a, b = max(lo, r0), min(hi, r1)
+            if a < b:
+                part = Q.quantize_q2k(w[a - r0:b - r0])
+                out = part if out is None else torch.cat([out, part], 0)
+        return out
+
+    # --------------------------------------------------------------- collectives
+    def _gather(self, full: torch.Tensor, local: torch.Tensor, lo: int, hi: int):
+        """full[:, :] <- concatenation over ranks of local (row slices)."""
+        if self.world == 1:
+            if full.data_ptr() != local.data_ptr():
+                full.copy_(local)
+            return
+        import torch.distributed as dist
+        per = local.shape[1]
+        n = full.shape[1]
+        if self.B == 1 and per * self.world == n:
+            dist.all_gather_into_tensor(full.view(-1), local.view(-1), group=self.group)
+            return
+        buf = torch.empty((self.world, self.B, per), dtype=local.dtype, device=local.device)
+        dist.all_gather_into_tensor(buf, local.contiguous(), group=self.group)
+        full.copy_(buf.permute(1, 0, 2).reshape(self.B, -1)[:, :n])
+
+    # --------------------------------------------------------------- one token
+    def step(self, x_in: torch.Tensor | None = None):
+        """Enqueue one pass of the stack on the current stream; returns logits."""
+        B, H, hs = self.B, self.H, self.hs
+        self.x.copy_(self.x0 if x_in is None else x_in)
+        one = self.world == 1
+        for wqkv, wo, wgu, wd in self.layers:
+            Q.rms_quantize_q8k(self.x, self.eps, out=self.xq)
+            wqkv.mul_mat(self.xq, B, out=self.qkv)
+            v_loc = self.qkv[:, 2 * hs:3 * hs]
+            if one:
+                Q.quantize_q8k(v_loc, out=self.vq)
+            else:
+                self._gather(self.v_full, v_loc.contiguous(), self.h_lo, self.h_hi)
+                Q.quantize_q8k(self.v_full, out=self.vq)
+            if one:
+                wo.mul_mat(self.vq, B, out=self.x, epilogue=EPI_RESIDUAL, resid=self.x)
+            else:
+                wo.mul_mat(self.vq, B, out=self.x_loc, epilogue=EPI_RESIDUAL,
+                           resid=self.x[:, self.h_lo:self.h_hi])
+                self._gather(self.x, self.x_loc, self.h_lo, self.h_hi)
+            Q.rms_quantize_q8k(self.x, self.eps, out=self.xq)
+            if one:
+                wgu.mul_mat(self.xq, B, out=self.h_full, epilogue=EPI_SILU_MUL)
+            else:
+                wgu.mul_mat(self.xq, B, out=self.h_loc, epilogue=EPI_SILU_MUL)
+                self._gather(self.h_full, self.h_loc, self.f_lo, self.f_hi)
+            Q.quantize_q8k(self.h_full, out=self.hq)
+            if one:
+                wd.mul_mat(self.hq, B, out=self.x, epilogue=EPI_RESIDUAL, resid=self.x)
+            else:
+                wd.mul_mat(self.hq, B, out=self.x_loc, epilogue=EPI_RESIDUAL,
+                           resid=self.x[:, self.h_lo:self.h_hi])
+                self._gather(self.x, self.x_loc, self.h_lo, self.h_hi)
+        Q.rms_quantize_q8k(self.x, self.eps, out=self.xq)
+        if one:
+            self.lm.mul_mat(self.xq, B, out=self.logits)
+        else:
+            self.lm.mul_mat(self.xq, B, out=self.lg_loc)
+            self._gather(self.logits, self.lg_loc, self.v_lo, self.v_hi)
+        return self.logits
+
+    # --------------------------------------------------------------- accounting
+    def launches_per_step(self) -> int:
+        """Kernels of this library per step (quantizers + GEMVs, chunks of 8 tokens)."""
+        g = math.ceil(self.B / 8)
+        return self.L * (4 + 4 * g) + 1 + g
+
+    def gemv_list(self):
+        """(name, matrix, k, cols, out_rows) of every GEMV in a step."""
+        out = []
+        for wqkv, wo, wgu, wd in self.layers:
+            out += [("qkv", wqkv), ("o", wo), ("gate_up", wgu), ("down", wd)]
+        out.append(("lm_head", self.lm))
+        return out
+
+    def algorithmic_bytes(self) -> int:
+        """Bytes one step must move on this rank: every GEMV's weights, Q8_K
+        inputs and fp32 outputs (the quantizers' few KB are not counted)."""
+        tot = 0
+        for name, m in self.gemv_list():
+            out_rows = m.n_rows // 2 if name == "gate_up" else m.n_rows
+            tot += gemv_bytes(m.n_rows, m.k, self.B, out_rows)
+        return tot
+
+    def free(self):
+        for layer in self.layers:
+            for m in layer:
+                m.free()
+        self.lm.free()
