@@ -68,6 +68,12 @@ int smeai_device_ready(void);
 /* Text of the last error raised on the calling thread ("" if none). */
 const char *smeai_last_error(void);
 
+/* Reads and clears the current device's error word.  Kernels never trap or
+ * spin forever: a wait that exceeds its time bound sets bit 0 (timeout) here
+ * and the kernel returns early, leaving its outputs incomplete.  Returns 0,
+ * or a negative status if the word cannot be read. */
+int smeai_take_device_error(unsigned *code);
+
 /* Repack n_rows x k of block_q2_K (row-major, host or device memory) into the
  * device tile layout; *w_dev_out receives an opaque handle.  The analogue of
  * ggml's CPU_REPACK buffer placement (q2_K_8x8_q8_K traits). */
@@ -103,10 +109,17 @@ int smeai_q2k_mul_mat(const void *w_dev, int64_t n_rows, int64_t k, const void *
 int smeai_q2k_mul_mat_ex(const void *w_dev, const void *x_q8k_dev, int64_t n_cols, float *y_dev, size_t ldy,
                          int epilogue, const float *resid_dev, size_t ld_resid, void *stream);
 
-/* fp32 activations in, fp32 out: quantizes X to Q8_K into a library-owned
- * device scratch buffer (grown on demand, one per device), then mul_mat. */
+/* fp32 activations in, fp32 out: each CTA quantizes the activation rows to
+ * Q8_K in its prologue (bit-identical to smeai_q8k_quantize), then runs the
+ * GEMV -- one kernel, no intermediate buffer.  x: n_cols rows of k floats. */
 int smeai_q2k_mul_mat_f32(const void *w_dev, const float *x_dev, int64_t n_cols, float *y_dev, size_t ldy,
                           void *stream);
+/* The same with a row stride, the fused epilogues, and an optional RMSNorm of
+ * each activation row before quantization (rms_eps >= 0; < 0 disables it),
+ * bit-identical to smeai_rms_q8k_quantize followed by smeai_q2k_mul_mat_ex. */
+int smeai_q2k_mul_mat_f32_ex(const void *w_dev, const float *x_dev, size_t ld_x, int64_t n_cols, float *y_dev,
+                             size_t ldy, int epilogue, const float *resid_dev, size_t ld_resid, float rms_eps,
+                             void *stream);
 
 /* Exactness probe: the integer parts of the dot for every (row, super-block)
  * against ONE Q8_K row, [n_rows][k/256] int32 each:

@@ -450,18 +450,26 @@ void orc_q2k_block_sums(int n, const orc_block_q2_K *x, const orc_block_q8_K *y,
                         int32_t *isum, int32_t *summs) {
     int nb = n / ORC_QK_K;
     for (int b = 0; b < nb; ++b) {
+        const uint8_t *sc = x[b].scales;
         int32_t mm = 0;
-        for (int j = 0; j < 16; ++j) mm += (int32_t) y[b].bsums[j] * (int32_t) (x[b].scales[j] >> 4);
+        for (int j = 0; j < 16; ++j) mm += (int32_t) y[b].bsums[j] * (int32_t) (sc[j] >> 4);
+        /* ggml's generic loop nest: two 128-value halves, four 2-bit planes per
+         * half, each plane two 16-value sub-blocks with their own scale. */
+        const uint8_t *q2 = x[b].qs;
+        const int8_t *q8 = y[b].qs;
         int32_t acc = 0;
-        for (int j = 0; j < 16; ++j) {
-            int32_t part = 0;
-            for (int t = 0; t < 16; ++t) {
-                int i = 16 * j + t;
-                int half = i / 128, within = i % 128, shift = 2 * (within / 32), l = within % 32;
-                int q = (x[b].qs[half * 32 + l] >> shift) & 3;
-                part += q * (int32_t) y[b].qs[i];
+        int j = 0;
+        for (int half = 0; half < 2; ++half) {
+            for (int shift = 0; shift < 8; shift += 2) {
+                int32_t lo = 0, hi = 0;
+                for (int l = 0; l < 16; ++l) lo += (int32_t) q8[l] * ((q2[l] >> shift) & 3);
+                for (int l = 16; l < 32; ++l) hi += (int32_t) q8[l] * ((q2[l] >> shift) & 3);
+                acc += (int32_t) (sc[j] & 0xF) * lo;
+                acc += (int32_t) (sc[j + 1] & 0xF) * hi;
+                j += 2;
+                q8 += 32;
             }
-            acc += (int32_t) (x[b].scales[j] & 0xF) * part;
+            q2 += 32;
         }
         isum[b] = acc;
         summs[b] = mm;

@@ -1,8 +1,5 @@
 // api_q2k.cu -- the C-ABI of include/smeai_q2k.h.
-#include <map>
-#include <mutex>
 #include <string.h>
-#include <utility>
 
 #include "common.cuh"
 #include "kernels.h"
@@ -48,20 +45,6 @@ ThreadCtx& tctx() {
   return ctx;
 }
 
-// Library-owned Q8_K scratch for smeai_q2k_mul_mat_f32, one per (device, stream).
-std::mutex g_scratch_mu;
-std::map<std::pair<int, cudaStream_t>, DeviceBuffer*> g_scratch;
-
-void* scratch_for(cudaStream_t s, size_t bytes, int* st) {
-  int dev = 0;
-  cudaGetDevice(&dev);
-  std::lock_guard<std::mutex> lock(g_scratch_mu);
-  DeviceBuffer*& b = g_scratch[{dev, s}];
-  if (!b) b = new DeviceBuffer();
-  *st = b->reserve(bytes);
-  return *st == kOk ? b->ptr : nullptr;
-}
-
 }  // namespace
 
 extern "C" {
@@ -69,6 +52,14 @@ extern "C" {
 int smeai_device_ready(void) { return device_ready() ? 1 : 0; }
 
 const char* smeai_last_error(void) { return last_error(); }
+
+int smeai_take_device_error(unsigned* code) {
+  if (!code) {
+    set_last_error("smeai_take_device_error: NULL pointer");
+    return kBadArgument;
+  }
+  return device_error_take(code);
+}
 
 // ---- ggml-shaped entry points ------------------------------------------------
 
@@ -223,16 +214,17 @@ int smeai_q2k_mul_mat_f32(const void* w_dev, const float* x_dev, int64_t n_cols,
                           void* stream) {
   const Handle* h = as_handle(w_dev);
   if (!h) return kBadArgument;
-  if (!x_dev || !y_dev || n_cols <= 0) {
-    set_last_error("smeai_q2k_mul_mat_f32: bad arguments");
-    return kBadArgument;
-  }
-  int st = kOk;
-  void* xq = scratch_for(as_stream(stream), (size_t)n_cols * h->w.nb * Q8K_BLOCK_BYTES, &st);
-  if (st) return st;
-  st = q8k_quantize(x_dev, h->w.k, n_cols, h->w.k, xq, as_stream(stream));
-  if (st) return st;
-  return q2k_gemv(h->w, xq, n_cols, y_dev, (int64_t)ldy, kEpiStore, nullptr, 0, as_stream(stream));
+  return q2k_gemv_any(h->w, kInF32, x_dev, h->w.k, 0.f, n_cols, y_dev, (int64_t)ldy, kEpiStore, nullptr, 0,
+                      as_stream(stream));
+}
+
+int smeai_q2k_mul_mat_f32_ex(const void* w_dev, const float* x_dev, size_t ld_x, int64_t n_cols, float* y_dev,
+                             size_t ldy, int epilogue, const float* resid_dev, size_t ld_resid, float rms_eps,
+                             void* stream) {
+  const Handle* h = as_handle(w_dev);
+  if (!h) return kBadArgument;
+  return q2k_gemv_any(h->w, rms_eps >= 0.f ? kInF32Rms : kInF32, x_dev, (int64_t)ld_x, rms_eps, n_cols, y_dev,
+                      (int64_t)ldy, epilogue, resid_dev, (int64_t)ld_resid, as_stream(stream));
 }
 
 int smeai_q2k_block_sums(const void* w_dev, const void* x_q8k_dev, int32_t* isum_dev, int32_t* summs_dev,

@@ -46,6 +46,13 @@ enum Epilogue : int {
   kEpiSiluMul = 2,   // rows interleaved (gate, up): y[c*ldy + r/2] = silu(gate) * up
 };
 
+// Activation input of the GEMV: ggml Q8_K blocks (contiguous rows), or fp32
+// rows quantized to Q8_K in the kernel's prologue, optionally after an RMSNorm.
+enum InMode : int { kInQ8K = 0, kInF32 = 1, kInF32Rms = 2 };
+
+int q2k_gemv_any(const Q2KWeight& w, int in_mode, const void* x, int64_t ld_x, float eps, int64_t n_cols,
+                 float* y, int64_t ldy, int epilogue, const float* resid, int64_t ld_resid, cudaStream_t stream);
+
 // y = W x for n_cols Q8_K activation rows (ggml layout, contiguous rows).
 int q2k_gemv(const Q2KWeight& w, const void* xq, int64_t n_cols, float* y, int64_t ldy, int epilogue,
              const float* resid, int64_t ld_resid, cudaStream_t stream);

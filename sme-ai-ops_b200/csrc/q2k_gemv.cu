@@ -2,26 +2,40 @@
 // HBM-bound core of the reference's Q2_K mul_mat (ggml_vec_dot_q2_K_q8_K /
 // ggml_gemv_q2_K_8x8_q8_K, llama.cpp/doc/SME_Q2K_OPTIMIZATION.md:105-136).
 //
-// Work decomposition (one CTA = 32 weight rows, lane = row):
-//   * weights arrive in the tile layout built by q2k_repack_kernel, so every
-//     128-bit load of a warp covers 512 contiguous bytes;
-//   * warp w of the CTA walks a contiguous range of super-blocks; the first
-//     block's weights are loaded before griddepcontrol.wait, so they stream
-//     while the kernel that produced the activations drains;
-//   * the Q8_K activations of the CTA's tokens are staged once into shared
-//     memory (16-byte aligned planes) and read by broadcast;
-//   * the 2-bit quants are masked in place (no shift) and fed to
-//     dp4a.u32.s32; each sub-block's sum is shifted back by 2*shift bits and
-//     scaled by its 4-bit scale -- exact integer arithmetic, identical to
-//     ggml's isum; the min term uses dp2a on the Q8_K bsums;
-//   * per super-block the float term fmaf(d_x*d, isum, -(d_x*dmin*summs)) is
-//     written to shared memory and summed over super-blocks in ascending order
-//     by one thread per (row, token): the same rounding sequence as the CPU
-//     restatement of ggml's generic dot;
-//   * fused epilogues: plain store, residual add, or silu(gate)*up over
-//     interleaved (gate, up) row pairs.
+// Persistent, TMA-fed design (one CTA per SM at most):
+//   * weights live in the tile layout built by q2k_repack_kernel: one 2688-byte
+//     tile per (32-row group, super-block), the tiles of a group contiguous;
+//     a CTA owns a contiguous range of row groups, i.e. one contiguous span of
+//     tiles;
+//   * warp 0 is the producer: one lane streams the CTA's tiles into a ring of
+//     up to 32 shared-memory stages with cp.async.bulk (the TMA engine),
+//     completing on per-stage mbarriers.  It starts at kernel entry, before
+//     griddepcontrol.wait, so the first ~86 KB per SM of this matrix stream in
+//     while the previous kernel in the stream is still running;
+//   * consumer warp w handles super-blocks b = w (mod 8) of every row group;
+//     lane = row.  After griddepcontrol.wait it quantizes its own activation
+//     blocks to Q8_K (fp32 input, optionally RMS-normalized; or stages ggml
+//     Q8_K blocks) into 16-byte aligned shared-memory planes -- the same code
+//     as the standalone quantizer, so the blocks are identical;
+//   * integer core per (row, super-block): 2-bit quants masked in place into
+//     dp4a.u32.s32, one accumulator per shift plane weighted by the 4-bit
+//     scales, planes shifted back at the end -- exact, equal to ggml's isum;
+//     the min term is dp2a on the Q8_K bsums;
+//   * the float term fmaf(d_x*d, isum, -(d_x*dmin*summs)) of each super-block
+//     goes to shared memory; when all warps have finished a row group one warp
+//     sums the terms in ascending super-block order (the rounding sequence of
+//     the CPU restatement of ggml's generic dot, so outputs are bit-identical)
+//     and applies the epilogue: store, residual add, or silu(gate)*up over
+//     interleaved (gate, up) row pairs;
+//   * every wait is an mbarrier wait bounded by wall time: on expiry the
+//     kernel records kDevErrTimeout in the device error word and returns (the
+//     producer first waits, bounded, for its copies in flight).
 #include "common.cuh"
 #include "kernels.h"
+#include "q8k_device.cuh"
+
+#include <stdio.h>
+#include <stdlib.h>
 
 namespace smeai {
 
@@ -33,60 +47,100 @@ struct WBlock {
   unsigned dm;
 };
 
-constexpr int kWarps = 8;
-constexpr int kThreads = kWarps * 32;
+constexpr int kMaxConsumers = 16;
+constexpr int kMaxThreads = (kMaxConsumers + 1) * 32;
+constexpr int kMaxStages = 64;
+constexpr uint64_t kWaitTimeoutNs = 2000000000ull;  // 2 s
 
-__device__ __forceinline__ void load_wblock(const uint8_t* tile, int lane, WBlock& wb) {
-  const uint4* t4 = reinterpret_cast<const uint4*>(tile);
-  wb.q[0] = ldg_stream(t4 + 0 * 32 + lane);
-  wb.q[1] = ldg_stream(t4 + 1 * 32 + lane);
-  wb.q[2] = ldg_stream(t4 + 2 * 32 + lane);
-  wb.q[3] = ldg_stream(t4 + 3 * 32 + lane);
-  wb.s = ldg_stream(t4 + 4 * 32 + lane);
-  wb.dm = ldg_stream(reinterpret_cast<const unsigned*>(tile + 5 * 512) + lane);
-}
-
-// Shared-memory planes for T tokens x nb super-blocks.
-struct ActSmem {
-  int4* qs;      // [T*nb][16]  (256 int8 per block)
-  int* bs;       // [T*nb][8]   (16 int16 bsums per block)
-  float* d;      // [T*nb]
-  float* terms;  // [T*nb][32]
+struct GemvParams {
+  const uint8_t* tiles;
+  int nb;
+  int64_t n_rows;
+  int64_t n_groups;
+  const void* x;     // Q8_K blocks (kInQ8K) or fp32 rows
+  int64_t ld_x;      // fp32 row stride in floats
+  float eps;         // RMSNorm epsilon (kInF32Rms)
+  float* y;
+  int64_t ldy;
+  const float* resid;
+  int64_t ld_resid;
+  int32_t* isum_out;
+  int32_t* summs_out;
+  unsigned* err;
+  int stages;        // ring depth (a power of two)
+  int log2_stages;
 };
 
-__device__ __forceinline__ ActSmem carve(uint8_t* base, int tnb) {
-  ActSmem a;
-  a.qs = reinterpret_cast<int4*>(base);
-  a.bs = reinterpret_cast<int*>(base + (size_t)tnb * 256);
-  a.d = reinterpret_cast<float*>(base + (size_t)tnb * (256 + 32));
-  a.terms = reinterpret_cast<float*>(base + (size_t)tnb * (256 + 32 + 4));
-  return a;
+// Shared-memory carve-up for T tokens (16-byte aligned pieces).
+struct Smem {
+  uint8_t* ring;   // [stages][kTileBytes]
+  int4* qs;        // [T*nb][16]  256 int8 per block
+  int* bs;         // [T*nb][8]   16 int16 bsums per block
+  float* d;        // [T*nb]
+  float* rsum;     // [T][nb + 1] RMS block sums, then 1/rms
+  float* terms;    // [2][T*nb][32]
+  uint64_t* full;  // [stages]
+  uint64_t* empty; // [stages]
+  uint64_t* grp;   // [2] all consumer lanes finished a row group
+  uint64_t* tfree; // [2] the finisher has consumed the terms buffer
+  uint64_t* rms;   // [2] block sums written / 1/rms ready
+};
+
+__host__ __device__ __forceinline__ size_t align16(size_t v) { return (v + 15) & ~(size_t)15; }
+
+__host__ __device__ __forceinline__ size_t smem_fixed_bytes(int T, int nb) {
+  return align16((size_t)T * nb * 256) + align16((size_t)T * nb * 32) + align16((size_t)T * nb * 4) +
+         align16((size_t)T * (nb + 1) * 4) + align16((size_t)2 * T * nb * 128) + 8 * 6;
+}
+__host__ __device__ __forceinline__ size_t smem_total_bytes(int T, int nb, int stages) {
+  return (size_t)stages * kTileBytes + smem_fixed_bytes(T, nb) + (size_t)stages * 16;
 }
 
-// Copy T ggml Q8_K rows (contiguous, 292 B per block) into the planes.
-__device__ __forceinline__ void stage_activations(const uint8_t* __restrict__ xq, int tnb, const ActSmem& a) {
-  const uint32_t* src = reinterpret_cast<const uint32_t*>(xq);
-  const int total = tnb * Q8K_BLOCK_WORDS;
-  for (int i = threadIdx.x; i < total; i += blockDim.x) {
-    const int blk = i / Q8K_BLOCK_WORDS, w = i - blk * Q8K_BLOCK_WORDS;
-    const uint32_t v = src[i];
-    if (w == 0) {
-      a.d[blk] = __uint_as_float(v);
-    } else if (w <= 64) {
-      reinterpret_cast<uint32_t*>(a.qs)[blk * 64 + (w - 1)] = v;
-    } else {
-      a.bs[blk * 8 + (w - 65)] = (int)v;
-    }
-  }
+__device__ __forceinline__ Smem carve(uint8_t* base, int T, int nb, int stages) {
+  Smem m;
+  size_t o = 0;
+  m.ring = base;
+  o += (size_t)stages * kTileBytes;
+  m.qs = reinterpret_cast<int4*>(base + o);
+  o += align16((size_t)T * nb * 256);
+  m.bs = reinterpret_cast<int*>(base + o);
+  o += align16((size_t)T * nb * 32);
+  m.d = reinterpret_cast<float*>(base + o);
+  o += align16((size_t)T * nb * 4);
+  m.rsum = reinterpret_cast<float*>(base + o);
+  o += align16((size_t)T * (nb + 1) * 4);
+  m.terms = reinterpret_cast<float*>(base + o);
+  o += align16((size_t)2 * T * nb * 128);
+  m.full = reinterpret_cast<uint64_t*>(base + o);
+  m.empty = m.full + stages;
+  m.grp = m.empty + stages;
+  m.tfree = m.grp + 2;
+  m.rms = m.tfree + 2;
+  return m;
 }
 
-// Integer core for one super-block of this lane's row against T tokens.
-template <int T>
-__device__ __forceinline__ void block_isums(const WBlock& wb, const ActSmem& a, int nb, int b, int (&isum)[T],
-                                            int (&summs)[T]) {
-  const unsigned sw[4] = {wb.s.x, wb.s.y, wb.s.z, wb.s.w};
+__device__ __forceinline__ void store_q8k_smem(const Q8KLane& r, const Smem& m, int slot) {
+  const int lane = threadIdx.x & 31;
+  uint32_t* q = reinterpret_cast<uint32_t*>(m.qs) + (size_t)slot * 64;
+  q[2 * lane] = r.w0;
+  q[2 * lane + 1] = r.w1;
+  if ((lane & 3) == 0) m.bs[slot * 8 + (lane >> 2)] = (int)r.bsum_pair;
+  if (lane == 0) m.d[slot] = r.d;
+}
+
+// Integer core + float term of super-block b for this lane's row.
+template <int T, bool SUMS>
+__device__ __forceinline__ void block_terms(const WBlock& wb, const Smem& m, int nb, int b, float* terms,
+                                            int lane, int64_t row, int64_t n_rows, int32_t* isum_out,
+                                            int32_t* summs_out) {
+  const unsigned sl[4] = {wb.s.x & 0x0F0F0F0Fu, wb.s.y & 0x0F0F0F0Fu, wb.s.z & 0x0F0F0F0Fu, wb.s.w & 0x0F0F0F0Fu};
+  const unsigned mh[4] = {(wb.s.x >> 4) & 0x0F0F0F0Fu, (wb.s.y >> 4) & 0x0F0F0F0Fu, (wb.s.z >> 4) & 0x0F0F0F0Fu,
+                          (wb.s.w >> 4) & 0x0F0F0F0Fu};
+  int plane[T][4];
 #pragma unroll
-  for (int t = 0; t < T; ++t) isum[t] = 0;
+  for (int t = 0; t < T; ++t)
+#pragma unroll
+    for (int s = 0; s < 4; ++s) plane[t][s] = 0;
 #pragma unroll
   for (int c = 0; c < 4; ++c) {
     const unsigned q0 = wb.q[c].x, q1 = wb.q[c].y, q2 = wb.q[c].z, q3 = wb.q[c].w;
@@ -96,116 +150,254 @@ __device__ __forceinline__ void block_isums(const WBlock& wb, const ActSmem& a, 
       const unsigned mask = 0x03030303u << (2 * s);
       const unsigned m0 = q0 & mask, m1 = q1 & mask, m2 = q2 & mask, m3 = q3 & mask;
       const int j = 8 * h + 2 * s + hf;  // sub-block of these 16 quants
-      const int sc = (int)((sw[j >> 2] >> (8 * (j & 3))) & 0xFu);
+      const int sc = (int)__byte_perm(sl[j >> 2], 0u, 0x4440u | (unsigned)(j & 3));
       const int chunk = h * 8 + s * 2 + hf;  // 16-byte activation chunk within the block
 #pragma unroll
       for (int t = 0; t < T; ++t) {
-        const int4 av = a.qs[(t * nb + b) * 16 + chunk];
+        const int4 av = m.qs[(t * nb + b) * 16 + chunk];
         int acc = dp4a_us(m0, av.x, 0);
         acc = dp4a_us(m1, av.y, acc);
         acc = dp4a_us(m2, av.z, acc);
         acc = dp4a_us(m3, av.w, acc);
-        isum[t] += sc * (acc >> (2 * s));
+        plane[t][s] += sc * acc;
       }
     }
   }
+  const float dw = __half2float(__ushort_as_half((unsigned short)(wb.dm & 0xffffu)));
+  const float dmw = __half2float(__ushort_as_half((unsigned short)(wb.dm >> 16)));
 #pragma unroll
   for (int t = 0; t < T; ++t) {
-    const int* bsp = a.bs + (t * nb + b) * 8;
-    int mm = 0;
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      const unsigned m4 = (sw[k] >> 4) & 0x0F0F0F0Fu;
-      mm = dp2a_lo_su(bsp[2 * k], m4, mm);
-      mm = dp2a_hi_su(bsp[2 * k + 1], m4, mm);
-    }
-    summs[t] = mm;
-  }
-}
-
-__device__ __forceinline__ float half_lo(unsigned v) {
-  __half_raw r;
-  r.x = (unsigned short)(v & 0xffffu);
-  return __half2float(__half(r));
-}
-__device__ __forceinline__ float half_hi(unsigned v) {
-  __half_raw r;
-  r.x = (unsigned short)(v >> 16);
-  return __half2float(__half(r));
-}
-
-template <int T, int EPI, bool SUMS>
-__global__ void __launch_bounds__(kThreads) q2k_gemv_kernel(const uint8_t* __restrict__ tiles, int nb,
-                                                            int64_t n_rows, const uint8_t* __restrict__ xq,
-                                                            float* y, int64_t ldy, const float* resid,
-                                                            int64_t ld_resid, int32_t* __restrict__ isum_out,
-                                                            int32_t* __restrict__ summs_out) {
-  extern __shared__ __align__(16) uint8_t smem[];
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int64_t group = blockIdx.x;
-  const uint8_t* gtiles = tiles + group * (int64_t)nb * kTileBytes;
-  const int b0 = (warp * nb) / kWarps, b1 = ((warp + 1) * nb) / kWarps;
-
-  WBlock cur;
-  if (b0 < b1) load_wblock(gtiles + (int64_t)b0 * kTileBytes, lane, cur);
-  pdl_trigger();
-  pdl_wait();
-
-  const ActSmem a = carve(smem, T * nb);
-  stage_activations(xq, T * nb, a);
-  __syncthreads();
-
-  for (int b = b0; b < b1; ++b) {
-    WBlock nxt;
-    if (b + 1 < b1) load_wblock(gtiles + (int64_t)(b + 1) * kTileBytes, lane, nxt);
-    int isum[T], summs[T];
-    block_isums<T>(cur, a, nb, b, isum, summs);
+    const int isum = plane[t][0] + (plane[t][1] >> 2) + (plane[t][2] >> 4) + (plane[t][3] >> 6);
+    const int* bsp = m.bs + (t * nb + b) * 8;
+    const int4 bs0 = *reinterpret_cast<const int4*>(bsp);
+    const int4 bs1 = *reinterpret_cast<const int4*>(bsp + 4);
+    int mm = dp2a_lo_su(bs0.x, mh[0], 0);
+    mm = dp2a_hi_su(bs0.y, mh[0], mm);
+    mm = dp2a_lo_su(bs0.z, mh[1], mm);
+    mm = dp2a_hi_su(bs0.w, mh[1], mm);
+    mm = dp2a_lo_su(bs1.x, mh[2], mm);
+    mm = dp2a_hi_su(bs1.y, mh[2], mm);
+    mm = dp2a_lo_su(bs1.z, mh[3], mm);
+    mm = dp2a_hi_su(bs1.w, mh[3], mm);
     if constexpr (SUMS) {
-      const int64_t row = group * 32 + lane;
       if (row < n_rows) {
-        isum_out[row * nb + b] = isum[0];
-        summs_out[row * nb + b] = summs[0];
+        isum_out[row * nb + b] = isum;
+        summs_out[row * nb + b] = mm;
       }
     } else {
-      const float dw = half_lo(cur.dm), dmw = half_hi(cur.dm);
-#pragma unroll
-      for (int t = 0; t < T; ++t) {
-        const float dx = a.d[t * nb + b];
-        const float dall = __fmul_rn(dx, dw);
-        const float dmn = __fmul_rn(dx, dmw);
-        const float term = __fmaf_rn(dall, __int2float_rn(isum[t]), -__fmul_rn(dmn, __int2float_rn(summs[t])));
-        a.terms[(t * nb + b) * 32 + lane] = term;
-      }
+      const float dx = m.d[t * nb + b];
+      const float dall = __fmul_rn(dx, dw);
+      const float dmn = __fmul_rn(dx, dmw);
+      terms[(t * nb + b) * 32 + lane] =
+          __fmaf_rn(dall, __int2float_rn(isum), -__fmul_rn(dmn, __int2float_rn(mm)));
     }
-    if (b + 1 < b1) cur = nxt;
   }
-  if constexpr (SUMS) return;
-  __syncthreads();
+}
 
+// Ordered sum over super-blocks of one row group, then the epilogue.
+template <int T, int EPI>
+__device__ __forceinline__ void finish_group(const float* terms, int nb, int64_t group, int lane,
+                                             const GemvParams& p) {
   if constexpr (EPI == kEpiSiluMul) {
-    // 16 (gate, up) pairs per group and token
-    for (int i = threadIdx.x; i < T * 16; i += blockDim.x) {
-      const int t = i >> 4, p = i & 15;
-      float g = 0.f, u = 0.f;
-      for (int b = 0; b < nb; ++b) {
-        g = __fadd_rn(g, a.terms[(t * nb + b) * 32 + 2 * p]);
-        u = __fadd_rn(u, a.terms[(t * nb + b) * 32 + 2 * p + 1]);
-      }
-      const int64_t orow = group * 16 + p;
-      if (2 * orow < n_rows) {
-        const float sg = __fdiv_rn(g, __fadd_rn(1.0f, expf(-g)));
-        y[t * ldy + orow] = __fmul_rn(sg, u);
+    if (lane < 16) {
+      const int64_t orow = group * 16 + lane;
+#pragma unroll 1
+      for (int t = 0; t < T; ++t) {
+        const float* tg = terms + (size_t)t * nb * 32 + 2 * lane;
+        float g = 0.f, u = 0.f;
+        for (int b = 0; b < nb; ++b) {
+          g = __fadd_rn(g, tg[b * 32]);
+          u = __fadd_rn(u, tg[b * 32 + 1]);
+        }
+        if (2 * orow < p.n_rows) {
+          const float sg = __fdiv_rn(g, __fadd_rn(1.0f, expf(-g)));
+          p.y[t * p.ldy + orow] = __fmul_rn(sg, u);
+        }
       }
     }
   } else {
-    for (int i = threadIdx.x; i < T * 32; i += blockDim.x) {
-      const int t = i >> 5, r = i & 31;
+    const int64_t orow = group * 32 + lane;
+#pragma unroll 1
+    for (int t = 0; t < T; ++t) {
+      const float* tr = terms + (size_t)t * nb * 32 + lane;
       float s = 0.f;
-      for (int b = 0; b < nb; ++b) s = __fadd_rn(s, a.terms[(t * nb + b) * 32 + r]);
-      const int64_t row = group * 32 + r;
-      if (row < n_rows) {
-        if constexpr (EPI == kEpiResidual) s = __fadd_rn(resid[t * ld_resid + row], s);
-        y[t * ldy + row] = s;
+      int b = 0;
+      for (; b + 8 <= nb; b += 8) {
+        float v[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) v[k] = tr[(b + k) * 32];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) s = __fadd_rn(s, v[k]);
+      }
+      for (; b < nb; ++b) s = __fadd_rn(s, tr[b * 32]);
+      if (orow < p.n_rows) {
+        if constexpr (EPI == kEpiResidual) s = __fadd_rn(p.resid[t * p.ld_resid + orow], s);
+        p.y[t * p.ldy + orow] = s;
+      }
+    }
+  }
+}
+
+template <int T, int EPI, int IN, bool SUMS>
+__global__ void __launch_bounds__(kMaxThreads) q2k_gemv_kernel(const GemvParams p) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int kConsumers = (blockDim.x >> 5) - 1;
+  const int nb = p.nb, S = p.stages, lgS = p.log2_stages, smask = S - 1;
+  const int64_t C = gridDim.x;
+  const int64_t g0 = (int64_t)blockIdx.x * p.n_groups / C, g1 = ((int64_t)blockIdx.x + 1) * p.n_groups / C;
+  const int ng = (int)(g1 - g0);
+  const int n_stages = ng * nb;
+  const Smem m = carve(smem, T, nb, S);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&m.full[s], 1);
+      mbar_init(&m.empty[s], 32);
+    }
+    mbar_init(&m.grp[0], kConsumers * 32);
+    mbar_init(&m.grp[1], kConsumers * 32);
+    mbar_init(&m.tfree[0], 32);
+    mbar_init(&m.tfree[1], 32);
+    mbar_init(&m.rms[0], kConsumers * 32);
+    mbar_init(&m.rms[1], 32);
+    mbar_fence_init();
+  }
+  __syncthreads();
+  pdl_trigger();
+
+  if (warp == 0) {
+    // ---- producer: stream this CTA's tiles (independent of earlier kernels)
+    if (lane == 0) {
+      const uint8_t* src = p.tiles + g0 * nb * (int64_t)kTileBytes;
+      int i = 0;
+      bool ok = true;
+      for (; i < n_stages; ++i) {
+        const int s = i & smask;
+        if (i >= S && !mbar_wait_bounded(&m.empty[s], (unsigned)(((i >> lgS) - 1) & 1), kWaitTimeoutNs)) {
+          ok = false;
+          break;
+        }
+        mbar_arrive_expect_tx(&m.full[s], kTileBytes);
+        bulk_copy_g2s(m.ring + (size_t)s * kTileBytes, src + (size_t)i * kTileBytes, kTileBytes, &m.full[s]);
+      }
+      if (!ok) {
+        raise_device_error(p.err, kDevErrTimeout);
+        for (int j = (i > S ? i - S : 0); j < i; ++j)
+          mbar_wait_bounded(&m.full[j & smask], (unsigned)((j >> lgS) & 1), kWaitTimeoutNs);
+      }
+    }
+    return;
+  }
+
+  // ---- consumers
+  const int cw = warp - 1;
+  pdl_wait();
+
+  // activation prologue: this warp's own super-blocks b = cw (mod kConsumers)
+  if constexpr (IN == kInQ8K) {
+    const uint32_t* src = static_cast<const uint32_t*>(p.x);
+    for (int b = cw; b < nb; b += kConsumers) {
+#pragma unroll 1
+      for (int t = 0; t < T; ++t) {
+        const uint32_t* blk = src + ((int64_t)t * nb + b) * Q8K_BLOCK_WORDS;
+        const int slot = t * nb + b;
+        const uint32_t w0 = blk[lane], w1 = blk[lane + 32];
+        const uint32_t w2 = lane + 64 < Q8K_BLOCK_WORDS ? blk[lane + 64] : 0u;
+        uint32_t* q = reinterpret_cast<uint32_t*>(m.qs) + (size_t)slot * 64;
+        // words: 0 = d, 1..64 = qs, 65..72 = bsums
+        if (lane == 0) m.d[slot] = __uint_as_float(w0);
+        else q[lane - 1] = w0;
+        q[lane + 31] = w1;
+        if (lane + 64 < Q8K_BLOCK_WORDS) {
+          if (lane == 0) q[63] = w2;
+          else m.bs[slot * 8 + (lane - 1)] = (int)w2;
+        }
+      }
+    }
+  } else {
+    const float* x = static_cast<const float*>(p.x);
+    if constexpr (IN == kInF32Rms) {
+      for (int i = cw; i < T * nb; i += kConsumers) {
+        const int t = i / nb, b = i - t * nb;
+        float v[8];
+        load8(x + t * p.ld_x + b * QK_K + lane * 8, v);
+        const float s = block_sumsq_warp(v);
+        if (lane == 0) m.rsum[t * (nb + 1) + b] = s;
+      }
+      mbar_arrive(&m.rms[0]);
+      if (cw == 0) {
+        if (!mbar_wait_bounded(&m.rms[0], 0, kWaitTimeoutNs)) {
+          raise_device_error(p.err, kDevErrTimeout);
+          return;
+        }
+        if (lane < T) {
+          float* rs = m.rsum + lane * (nb + 1);
+          float total = 0.f;
+          for (int b = 0; b < nb; ++b) total = __fadd_rn(total, rs[b]);
+          rs[nb] = rms_inv_from_sum(total, nb * QK_K, p.eps);
+        }
+        mbar_arrive(&m.rms[1]);
+      }
+      if (!mbar_wait_bounded(&m.rms[1], 0, kWaitTimeoutNs)) {
+        raise_device_error(p.err, kDevErrTimeout);
+        return;
+      }
+    }
+    for (int b = cw; b < nb; b += kConsumers) {
+#pragma unroll 1
+      for (int t = 0; t < T; ++t) {
+        float v[8];
+        load8(x + t * p.ld_x + b * QK_K + lane * 8, v);
+        if constexpr (IN == kInF32Rms) {
+          const float inv = m.rsum[t * (nb + 1) + nb];
+#pragma unroll
+          for (int k = 0; k < 8; ++k) v[k] = __fmul_rn(v[k], inv);
+        }
+        store_q8k_smem(q8k_quantize_lane(v), m, t * nb + b);
+      }
+    }
+  }
+  __syncwarp();
+
+  // main loop over this CTA's row groups
+  for (int j = 0; j < ng; ++j) {
+    const int buf = j & 1;
+    float* terms = m.terms + (size_t)buf * T * nb * 32;
+    if (!SUMS && j >= 2 && !mbar_wait_bounded(&m.tfree[buf], (unsigned)(((j >> 1) - 1) & 1), kWaitTimeoutNs)) {
+      raise_device_error(p.err, kDevErrTimeout);
+      return;
+    }
+    const int64_t group = g0 + j;
+    const int64_t row = group * 32 + lane;
+    for (int b = cw; b < nb; b += kConsumers) {
+      const int i = j * nb + b;
+      const int s = i & smask;
+      if (!mbar_wait_bounded(&m.full[s], (unsigned)((i >> lgS) & 1), kWaitTimeoutNs)) {
+        raise_device_error(p.err, kDevErrTimeout);
+        return;
+      }
+      const uint8_t* tile = m.ring + (size_t)s * kTileBytes;
+      const uint4* t4 = reinterpret_cast<const uint4*>(tile);
+      WBlock wb;
+      wb.q[0] = t4[0 * 32 + lane];
+      wb.q[1] = t4[1 * 32 + lane];
+      wb.q[2] = t4[2 * 32 + lane];
+      wb.q[3] = t4[3 * 32 + lane];
+      wb.s = t4[4 * 32 + lane];
+      wb.dm = reinterpret_cast<const unsigned*>(tile + 5 * 512)[lane];
+      mbar_arrive(&m.empty[s]);
+      block_terms<T, SUMS>(wb, m, nb, b, terms, lane, row, p.n_rows, p.isum_out, p.summs_out);
+    }
+    if constexpr (!SUMS) {
+      mbar_arrive(&m.grp[buf]);
+      if (cw == (j % kConsumers)) {
+        if (!mbar_wait_bounded(&m.grp[buf], (unsigned)((j >> 1) & 1), kWaitTimeoutNs)) {
+          raise_device_error(p.err, kDevErrTimeout);
+          return;
+        }
+        finish_group<T, EPI>(terms, nb, group, lane, p);
+        mbar_arrive(&m.tfree[buf]);
       }
     }
   }
@@ -239,38 +431,124 @@ __global__ void q2k_repack_kernel(const uint8_t* __restrict__ src, int64_t n_row
   reinterpret_cast<uint32_t*>(tile + 5 * 512)[lane] = w[20];
 }
 
-size_t gemv_smem_bytes(int T, int nb) { return (size_t)T * nb * (256 + 32 + 4 + 128); }
+constexpr int kSmemLimit = 227 * 1024;
 
-template <int T, int EPI, bool SUMS>
-int launch_gemv(const Q2KWeight& w, const uint8_t* xq, float* y, int64_t ldy, const float* resid,
-                int64_t ld_resid, int32_t* isum, int32_t* summs, cudaStream_t stream) {
-  auto kern = q2k_gemv_kernel<T, EPI, SUMS>;
-  const size_t smem = gemv_smem_bytes(T, w.nb);
+int num_sms() {
+  static int cached[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return 148;
+  if (!cached[dev]) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) {
+      cudaGetLastError();
+      n = 148;
+    }
+    cached[dev] = n;
+  }
+  return cached[dev];
+}
+
+struct Plan {
+  int ctas_per_sm;
+  int consumers;
+  int stages;
+};
+
+// Launch shape of the GEMV for T tokens, nb super-blocks per row and
+// n_groups 32-row groups (measured on B200, graph-timed, batch 1):
+//   <= 1 CTA per SM of work  : 1 CTA/SM, 16 consumer warps, deep ring
+//   <= ~4 groups per SM      : 3 CTAs/SM, 8 consumer warps
+//   more                     : 4 CTAs/SM, 4 consumer warps
+// More resident warps per SM is what lifts throughput: the integer core is
+// issue-latency bound.  The ring takes the deepest power of two (4..64
+// stages) that fits in the CTA's share of shared memory.  The override
+// SMEAI_GEMV_PLAN="ctas_per_sm,consumers,stages" exists for tuning sweeps.
+Plan plan_for(int T, int nb, int64_t n_groups) {
+  const int sms = num_sms();
+  Plan pl;
+  if (n_groups <= sms) pl = {1, 16, 0};
+  else if (n_groups <= 4 * sms) pl = {3, 8, 0};
+  else pl = {4, 4, 0};
+  static int ov[3] = {-1, -1, -1};
+  static bool read = false;
+  if (!read) {
+    read = true;
+    const char* e = getenv("SMEAI_GEMV_PLAN");
+    if (e) sscanf(e, "%d,%d,%d", &ov[0], &ov[1], &ov[2]);
+  }
+  if (ov[0] > 0) pl.ctas_per_sm = ov[0];
+  if (ov[1] > 0 && ov[1] <= kMaxConsumers) pl.consumers = ov[1];
+  const size_t fixed = smem_fixed_bytes(T, nb);
+  const size_t budget = (size_t)kSmemLimit / (size_t)(pl.ctas_per_sm < 2 ? 2 : pl.ctas_per_sm);
+  const int cap = pl.ctas_per_sm == 1 ? 64 : 16;
+  for (int s = cap; s >= 4; s >>= 1)
+    if ((ov[2] <= 0 || s <= ov[2]) && fixed + (size_t)s * (kTileBytes + 16) <= budget) {
+      pl.stages = s;
+      break;
+    }
+  if (!pl.stages)
+    for (int s = 32; s >= 4; s >>= 1)
+      if (fixed + (size_t)s * (kTileBytes + 16) <= (size_t)kSmemLimit) {
+        pl.stages = s;
+        pl.ctas_per_sm = 1;
+        break;
+      }
+  return pl;
+}
+
+int plan_stages(int T, int nb) { return plan_for(T, nb, 1).stages; }
+
+template <int T, int EPI, int IN, bool SUMS>
+int launch_gemv(const Q2KWeight& w, GemvParams p, cudaStream_t stream) {
+  auto kern = q2k_gemv_kernel<T, EPI, IN, SUMS>;
+  const Plan pl = plan_for(T, w.nb, w.n_groups);
+  if (pl.stages <= 0) {
+    set_last_error("q2k_gemv: k=%lld too large for %d tokens per launch", (long long)w.k, T);
+    return kBadArgument;
+  }
+  p.stages = pl.stages;
+  p.log2_stages = 31 - __builtin_clz((unsigned)pl.stages);
+  p.n_groups = w.n_groups;
+  p.err = device_error_ptr();
+  if (!p.err) {
+    set_last_error("q2k_gemv: device error word unavailable");
+    return kCudaError;
+  }
+  const size_t smem = smem_total_bytes(T, w.nb, pl.stages);
   static unsigned configured = 0;  // per template instance, one bit per device
   int dev = 0;
   SMEAI_CUDA_TRY(cudaGetDevice(&dev));
   if (!(configured & (1u << (dev & 31)))) {
-    SMEAI_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024));
+    SMEAI_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit));
     configured |= 1u << (dev & 31);
   }
-  SMEAI_CUDA_TRY(launch(kern, dim3((unsigned)w.n_groups), dim3(kThreads), smem, stream,
-                        (const uint8_t*)w.tiles, w.nb, w.n_rows, xq, y, ldy, resid, ld_resid, isum, summs));
+  const int64_t max_ctas = (int64_t)num_sms() * pl.ctas_per_sm;
+  const int64_t ctas = w.n_groups < max_ctas ? w.n_groups : max_ctas;
+  SMEAI_CUDA_TRY(launch(kern, dim3((unsigned)ctas), dim3((pl.consumers + 1) * 32), smem, stream, p));
   return kOk;
 }
 
-template <int EPI>
-int dispatch_t(int T, const Q2KWeight& w, const uint8_t* xq, float* y, int64_t ldy, const float* resid,
-               int64_t ld_resid, cudaStream_t s) {
+template <int EPI, int IN>
+int dispatch_t(int T, const Q2KWeight& w, const GemvParams& p, cudaStream_t s) {
   switch (T) {
-    case 1: return launch_gemv<1, EPI, false>(w, xq, y, ldy, resid, ld_resid, nullptr, nullptr, s);
-    case 2: return launch_gemv<2, EPI, false>(w, xq, y, ldy, resid, ld_resid, nullptr, nullptr, s);
-    case 3: return launch_gemv<3, EPI, false>(w, xq, y, ldy, resid, ld_resid, nullptr, nullptr, s);
-    case 4: return launch_gemv<4, EPI, false>(w, xq, y, ldy, resid, ld_resid, nullptr, nullptr, s);
-    case 5: return launch_gemv<5, EPI, false>(w, xq, y, ldy, resid, ld_resid, nullptr, nullptr, s);
-    case 6: return launch_gemv<6, EPI, false>(w, xq, y, ldy, resid, ld_resid, nullptr, nullptr, s);
-    case 7: return launch_gemv<7, EPI, false>(w, xq, y, ldy, resid, ld_resid, nullptr, nullptr, s);
-    case 8: return launch_gemv<8, EPI, false>(w, xq, y, ldy, resid, ld_resid, nullptr, nullptr, s);
+    case 1: return launch_gemv<1, EPI, IN, false>(w, p, s);
+    case 2: return launch_gemv<2, EPI, IN, false>(w, p, s);
+    case 4: return launch_gemv<4, EPI, IN, false>(w, p, s);
+    case 8: return launch_gemv<8, EPI, IN, false>(w, p, s);
     default: return kBadArgument;
+  }
+}
+
+template <int IN>
+int dispatch_epi(int epi, int T, const Q2KWeight& w, const GemvParams& p, cudaStream_t s) {
+  switch (epi) {
+    case kEpiStore: return dispatch_t<kEpiStore, IN>(T, w, p, s);
+    case kEpiResidual: return dispatch_t<kEpiResidual, IN>(T, w, p, s);
+    case kEpiSiluMul: return dispatch_t<kEpiSiluMul, IN>(T, w, p, s);
+    default:
+      set_last_error("q2k_gemv: unknown epilogue %d", epi);
+      return kBadArgument;
   }
 }
 
@@ -323,14 +601,18 @@ int q2k_repack(const void* w_blocks_dev, int64_t n_rows, int64_t k, Q2KWeight* o
   return st;
 }
 
-int q2k_gemv(const Q2KWeight& w, const void* xq, int64_t n_cols, float* y, int64_t ldy, int epilogue,
-             const float* resid, int64_t ld_resid, cudaStream_t stream) {
-  if (!w.tiles || !xq || !y || n_cols <= 0) {
+int q2k_gemv_any(const Q2KWeight& w, int in_mode, const void* x, int64_t ld_x, float eps, int64_t n_cols,
+                 float* y, int64_t ldy, int epilogue, const float* resid, int64_t ld_resid, cudaStream_t stream) {
+  if (!w.tiles || !x || !y || n_cols <= 0) {
     set_last_error("q2k_gemv: bad arguments");
     return kBadArgument;
   }
-  if (reinterpret_cast<uintptr_t>(xq) & 3) {
+  if (in_mode == kInQ8K && (reinterpret_cast<uintptr_t>(x) & 3)) {
     set_last_error("q2k_gemv: Q8_K activations must be 4-byte aligned");
+    return kBadArgument;
+  }
+  if (in_mode != kInQ8K && ((reinterpret_cast<uintptr_t>(x) & 3) || ld_x < w.k)) {
+    set_last_error("q2k_gemv: fp32 activations must be 4-byte aligned with ld_x >= k");
     return kBadArgument;
   }
   if (epilogue == kEpiResidual && !resid) {
@@ -346,24 +628,30 @@ int q2k_gemv(const Q2KWeight& w, const void* xq, int64_t n_cols, float* y, int64
     set_last_error("q2k_gemv: leading dimension smaller than the output rows");
     return kBadArgument;
   }
-  const size_t q8_row_bytes = (size_t)w.nb * Q8K_BLOCK_BYTES;
   for (int64_t c0 = 0; c0 < n_cols;) {
-    int T = (int)((n_cols - c0) > 8 ? 8 : (n_cols - c0));
-    while (T > 1 && gemv_smem_bytes(T, w.nb) > 227 * 1024) --T;
-    if (gemv_smem_bytes(T, w.nb) > 227 * 1024) {
-      set_last_error("q2k_gemv: k=%lld too large for the shared-memory staging", (long long)w.k);
-      return kBadArgument;
-    }
-    const uint8_t* xc = static_cast<const uint8_t*>(xq) + c0 * q8_row_bytes;
-    float* yc = y + c0 * ldy;
-    const float* rc = resid ? resid + c0 * ld_resid : nullptr;
+    const int64_t rem = n_cols - c0;
+    int T = rem >= 8 ? 8 : (rem >= 4 ? 4 : (rem >= 2 ? 2 : 1));
+    while (T > 1 && plan_stages(T, w.nb) <= 0) T >>= 1;
+    GemvParams p = {};
+    p.tiles = w.tiles;
+    p.nb = w.nb;
+    p.n_rows = w.n_rows;
+    p.x = in_mode == kInQ8K ? static_cast<const void*>(static_cast<const uint8_t*>(x) +
+                                                       c0 * (int64_t)w.nb * Q8K_BLOCK_BYTES)
+                            : static_cast<const void*>(static_cast<const float*>(x) + c0 * ld_x);
+    p.ld_x = ld_x;
+    p.eps = eps;
+    p.y = y + c0 * ldy;
+    p.ldy = ldy;
+    p.resid = resid ? resid + c0 * ld_resid : nullptr;
+    p.ld_resid = ld_resid;
     int st;
-    switch (epilogue) {
-      case kEpiStore: st = dispatch_t<kEpiStore>(T, w, xc, yc, ldy, rc, ld_resid, stream); break;
-      case kEpiResidual: st = dispatch_t<kEpiResidual>(T, w, xc, yc, ldy, rc, ld_resid, stream); break;
-      case kEpiSiluMul: st = dispatch_t<kEpiSiluMul>(T, w, xc, yc, ldy, rc, ld_resid, stream); break;
+    switch (in_mode) {
+      case kInQ8K: st = dispatch_epi<kInQ8K>(epilogue, T, w, p, stream); break;
+      case kInF32: st = dispatch_epi<kInF32>(epilogue, T, w, p, stream); break;
+      case kInF32Rms: st = dispatch_epi<kInF32Rms>(epilogue, T, w, p, stream); break;
       default:
-        set_last_error("q2k_gemv: unknown epilogue %d", epilogue);
+        set_last_error("q2k_gemv: unknown input mode %d", in_mode);
         return kBadArgument;
     }
     if (st != kOk) return st;
@@ -372,13 +660,24 @@ int q2k_gemv(const Q2KWeight& w, const void* xq, int64_t n_cols, float* y, int64
   return kOk;
 }
 
+int q2k_gemv(const Q2KWeight& w, const void* xq, int64_t n_cols, float* y, int64_t ldy, int epilogue,
+             const float* resid, int64_t ld_resid, cudaStream_t stream) {
+  return q2k_gemv_any(w, kInQ8K, xq, 0, 0.f, n_cols, y, ldy, epilogue, resid, ld_resid, stream);
+}
+
 int q2k_block_sums(const Q2KWeight& w, const void* xq, int32_t* isum, int32_t* summs, cudaStream_t stream) {
   if (!w.tiles || !xq || !isum || !summs) {
     set_last_error("q2k_block_sums: bad arguments");
     return kBadArgument;
   }
-  return launch_gemv<1, kEpiStore, true>(w, static_cast<const uint8_t*>(xq), nullptr, 0, nullptr, 0, isum, summs,
-                                          stream);
+  GemvParams p = {};
+  p.tiles = w.tiles;
+  p.nb = w.nb;
+  p.n_rows = w.n_rows;
+  p.x = xq;
+  p.isum_out = isum;
+  p.summs_out = summs;
+  return launch_gemv<1, kEpiStore, kInQ8K, true>(w, p, stream);
 }
 
 }  // namespace smeai

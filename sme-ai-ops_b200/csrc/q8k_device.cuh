@@ -1,0 +1,106 @@
+// q8k_device.cuh -- warp-level Q8_K quantization core shared by the standalone
+// quantizer (q8k_quant.cu) and the GEMV prologue (q2k_gemv.cu), so both
+// produce identical blocks.
+//
+// Restates ggml's quantize_row_q8_K (generic C, ggml 0.9.8): per 256 values,
+// the value of largest magnitude (first on ties) gives iscale = -127/max;
+// q = nearest(iscale*x) capped at 127 (ggml's nearest_int as one fused
+// multiply-add with 1.5*2^23, the form GCC's default contraction produces on
+// an FMA target); d = 1/iscale; bsums = sums of 16 consecutive q.  An
+// all-zero block gives d = 0 and zero quants and sums.
+#pragma once
+
+#include "common.cuh"
+
+namespace smeai {
+
+// What one lane contributes to its block: qs bytes 8l..8l+7 as two words;
+// on lanes with l % 4 == 0, the bsums pair (2*(l/4), 2*(l/4)+1) as one word;
+// d (same on every lane).
+struct Q8KLane {
+  uint32_t w0, w1;
+  uint32_t bsum_pair;
+  float d;
+};
+
+// RMS partial of one 256-value block: lane sums of 8 fused squares, folded at
+// distances 16, 8, 4, 2, 1 (the fixed order the CPU restatement follows).
+__device__ __forceinline__ float block_sumsq_warp(const float (&v)[8]) {
+  float s = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) s = __fmaf_rn(v[i], v[i], s);
+#pragma unroll
+  for (int off = 16; off >= 1; off >>= 1) s = __fadd_rn(s, __shfl_xor_sync(0xffffffffu, s, off));
+  return s;
+}
+
+// inv = 1/sqrt(sum/k + eps), each step rounded once.
+__device__ __forceinline__ float rms_inv_from_sum(float total, int k, float eps) {
+  const float mean = __fdiv_rn(total, (float)k);
+  return __fdiv_rn(1.f, __fsqrt_rn(__fadd_rn(mean, eps)));
+}
+
+__device__ __forceinline__ Q8KLane q8k_quantize_lane(const float (&v)[8]) {
+  const int lane = threadIdx.x & 31;
+  float amax = 0.f, vmax = 0.f;
+  int idx = 0x7fffffff;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const float a = fabsf(v[i]);
+    if (a > amax) { amax = a; vmax = v[i]; idx = lane * 8 + i; }
+  }
+#pragma unroll
+  for (int off = 16; off >= 1; off >>= 1) {
+    const float a2 = __shfl_xor_sync(0xffffffffu, amax, off);
+    const float v2 = __shfl_xor_sync(0xffffffffu, vmax, off);
+    const int i2 = __shfl_xor_sync(0xffffffffu, idx, off);
+    if (a2 > amax || (a2 == amax && i2 < idx)) { amax = a2; vmax = v2; idx = i2; }
+  }
+  Q8KLane r;
+  if (amax == 0.f) {
+    r.w0 = r.w1 = r.bsum_pair = 0u;
+    r.d = 0.f;
+    return r;
+  }
+  const float iscale = __fdiv_rn(-127.f, vmax);
+  int part = 0;
+  uint32_t w[2] = {0u, 0u};
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    int q = magic_round_bits(__fmaf_rn(iscale, v[i], kMagic));
+    q = q > 127 ? 127 : q;
+    part += q;
+    w[i >> 2] |= (uint32_t)(q & 0xff) << (8 * (i & 3));
+  }
+  r.w0 = w[0];
+  r.w1 = w[1];
+  const int gsum = part + __shfl_xor_sync(0xffffffffu, part, 1);      // group l/2
+  const int other = __shfl_down_sync(0xffffffffu, gsum, 2);          // group l/2 + 1
+  r.bsum_pair = (uint32_t)(gsum & 0xffff) | ((uint32_t)other << 16);
+  r.d = __fdiv_rn(1.f, iscale);
+  return r;
+}
+
+// Write one lane's share as a ggml block_q8_K (292 bytes, 4-byte aligned).
+__device__ __forceinline__ void q8k_store_global(const Q8KLane& r, uint8_t* out) {
+  const int lane = threadIdx.x & 31;
+  uint32_t* ow = reinterpret_cast<uint32_t*>(out);
+  ow[1 + 2 * lane] = r.w0;
+  ow[2 + 2 * lane] = r.w1;
+  if ((lane & 3) == 0) ow[65 + (lane >> 2)] = r.bsum_pair;
+  if (lane == 0) ow[0] = __float_as_uint(r.d);
+}
+
+__device__ __forceinline__ void load8(const float* p, float (&v)[8]) {
+  if ((reinterpret_cast<uintptr_t>(p) & 15) == 0) {
+    const float4 a = *reinterpret_cast<const float4*>(p);
+    const float4 b = *reinterpret_cast<const float4*>(p + 4);
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+    v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+  } else {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] = p[i];
+  }
+}
+
+}  // namespace smeai

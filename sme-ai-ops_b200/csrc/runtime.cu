@@ -31,6 +31,33 @@ bool pdl_enabled() {
   return enabled == 1;
 }
 
+namespace {
+__device__ unsigned g_device_error = 0;
+}
+
+unsigned* device_error_ptr() {
+  static unsigned* cached[64] = {nullptr};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+  if (!cached[dev]) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_device_error) != cudaSuccess) {
+      cudaGetLastError();
+      return nullptr;
+    }
+    cached[dev] = static_cast<unsigned*>(p);
+  }
+  return cached[dev];
+}
+
+int device_error_take(unsigned* code) {
+  unsigned v = 0, zero = 0;
+  SMEAI_CUDA_TRY(cudaMemcpyFromSymbol(&v, g_device_error, sizeof(v)));
+  if (v) SMEAI_CUDA_TRY(cudaMemcpyToSymbol(g_device_error, &zero, sizeof(zero)));
+  *code = v;
+  return kOk;
+}
+
 bool device_ready() {
   int n = 0;
   if (cudaGetDeviceCount(&n) != cudaSuccess || n <= 0) {

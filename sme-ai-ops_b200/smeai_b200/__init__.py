@@ -60,6 +60,7 @@ def _declare(L: ctypes.CDLL) -> None:
         "ggml_vec_dot_q2_K_q8_K": (None, [I, P, SZ, P, SZ, P, SZ, I]),
         "smeai_device_ready": (I, []),
         "smeai_last_error": (ctypes.c_char_p, []),
+        "smeai_take_device_error": (I, [ctypes.POINTER(ctypes.c_uint)]),
         "smeai_q2k_repack": (I, [P, I64, I64, ctypes.POINTER(ctypes.c_void_p)]),
         "smeai_q2k_free": (None, [P]),
         "smeai_q2k_weight_bytes": (SZ, [P]),
@@ -68,6 +69,7 @@ def _declare(L: ctypes.CDLL) -> None:
         "smeai_q2k_mul_mat": (I, [P, I64, I64, P, I64, P, SZ, P]),
         "smeai_q2k_mul_mat_ex": (I, [P, P, I64, P, SZ, I, P, SZ, P]),
         "smeai_q2k_mul_mat_f32": (I, [P, P, I64, P, SZ, P]),
+        "smeai_q2k_mul_mat_f32_ex": (I, [P, P, SZ, I64, P, SZ, I, P, SZ, F, P]),
         "smeai_q2k_block_sums": (I, [P, P, P, P, P]),
         "smeai_q2k_quantize_device": (I, [P, I64, P, P]),
         "smeai_q2k_dequantize_device": (I, [P, I64, P, P]),

@@ -105,6 +105,24 @@ class Q2KMatrix:
               "q2k_mul_mat_f32")
         return out
 
+    def mul_mat_f32_ex(self, x: torch.Tensor, n_cols: int, out: torch.Tensor | None = None,
+                       epilogue: int = EPI_STORE, resid: torch.Tensor | None = None,
+                       rms_eps: float | None = None) -> torch.Tensor:
+        """fp32 activations [n_cols, >=k] (row stride x.stride(0)), quantized to
+        Q8_K (after an RMSNorm when rms_eps is given) inside the GEMV."""
+        out_rows = self.n_rows // 2 if epilogue == EPI_SILU_MUL else self.n_rows
+        if out is None:
+            out = torch.empty((n_cols, out_rows), dtype=torch.float32, device=x.device)
+        assert x.dtype == torch.float32 and x.stride(-1) == 1
+        ld_x = x.stride(0) if x.dim() == 2 else self.k
+        ldy = out.stride(0) if out.dim() == 2 else out_rows
+        ldr = 0 if resid is None else (resid.stride(0) if resid.dim() == 2 else out_rows)
+        eps = -1.0 if rms_eps is None else float(rms_eps)
+        check(lib().smeai_q2k_mul_mat_f32_ex(self.handle, _ptr(x), ld_x, n_cols, _ptr(out), ldy, epilogue,
+                                             _ptr(resid), ldr, ctypes.c_float(eps), cur_stream()),
+              "q2k_mul_mat_f32_ex")
+        return out
+
     def block_sums(self, xq: torch.Tensor):
         isum = torch.empty((self.n_rows, self.nb), dtype=torch.int32, device=xq.device)
         summs = torch.empty_like(isum)

@@ -47,9 +47,16 @@ def gemv_bytes(rows: int, k: int, cols: int, out_rows: int | None = None) -> int
 
 class Q2KDecodeStack:
     def __init__(self, n_layers=32, hidden=4096, ffn=11008, vocab=32000, batch=1, rank=0, world=1,
-                 device=None, seed=0, std=0.02, eps=1e-5, group=None):
+                 device=None, seed=0, std=0.02, eps=1e-5, group=None, keep_blocks=False, quant="separate"):
         self.L, self.H, self.F, self.V = n_layers, hidden, ffn, vocab
         self.B, self.rank, self.world, self.eps, self.group = batch, rank, world, eps, group
+        # where each linear's input is quantized to Q8_K: "fused" = inside the
+        # GEMV's prologue; "separate" = a quantizer kernel before the GEMV;
+        # "mixed" = fused where an RMSNorm comes first (qkv, gate/up, lm_head),
+        # separate for the plain re-quantizations (o, down).  All three give
+        # bit-identical results.
+        assert quant in ("fused", "separate", "mixed")
+        self.quant = quant
         self.dev = device or torch.device("cuda", torch.cuda.current_device())
         assert hidden % QK_K == 0 and ffn % QK_K == 0
         self.h_lo, self.h_hi = shard_range(hidden, rank, world)
@@ -58,21 +65,27 @@ class Q2KDecodeStack:
         hs, fs, vs = self.h_hi - self.h_lo, self.f_hi - self.f_lo, self.v_hi - self.v_lo
         self.hs, self.fs, self.vs = hs, fs, vs
         self.layers = []
+        self.blocks = [] if keep_blocks else None   # raw ggml blocks per layer (tests)
         self.weight_bytes = 0
         for li in range(n_layers):
             wq, wk, wv = (self._draw(seed, li, m, hidden, hidden, self.h_lo, self.h_hi, std) for m in range(3))
             wqkv = Q.Q2KMatrix(torch.cat([wq, wk, wv], 0), 3 * hs, hidden)
-            del wq, wk, wv
-            wo = Q.Q2KMatrix(self._draw(seed, li, 3, hidden, hidden, self.h_lo, self.h_hi, std), hs, hidden)
+            wo_b = self._draw(seed, li, 3, hidden, hidden, self.h_lo, self.h_hi, std)
+            wo = Q.Q2KMatrix(wo_b, hs, hidden)
             wg = self._draw(seed, li, 4, ffn, hidden, self.f_lo, self.f_hi, std)
             wu = self._draw(seed, li, 5, ffn, hidden, self.f_lo, self.f_hi, std)
             wgu = Q.Q2KMatrix(torch.stack([wg, wu], 1).reshape(2 * fs, -1), 2 * fs, hidden)
-            del wg, wu
-            wd = Q.Q2KMatrix(self._draw(seed, li, 6, hidden, ffn, self.h_lo, self.h_hi, std), hs, ffn)
+            wd_b = self._draw(seed, li, 6, hidden, ffn, self.h_lo, self.h_hi, std)
+            wd = Q.Q2KMatrix(wd_b, hs, ffn)
+            if keep_blocks:
+                self.blocks.append(dict(q=wq, k=wk, v=wv, o=wo_b, g=wg, u=wu, d=wd_b))
+            del wq, wk, wv, wg, wu
             self.layers.append((wqkv, wo, wgu, wd))
             self.weight_bytes += wqkv.n_rows * wqkv.nb * 84 + wo.n_rows * wo.nb * 84 + \
                 wgu.n_rows * wgu.nb * 84 + wd.n_rows * wd.nb * 84
-        self.lm = Q.Q2KMatrix(self._draw(seed, n_layers, 7, vocab, hidden, self.v_lo, self.v_hi, std), vs, hidden)
+        lm_b = self._draw(seed, n_layers, 7, vocab, hidden, self.v_lo, self.v_hi, std)
+        self.lm = Q.Q2KMatrix(lm_b, vs, hidden)
+        self.lm_blocks = lm_b if keep_blocks else None
         self.weight_bytes += self.lm.n_rows * self.lm.nb * 84
         torch.cuda.synchronize()
         B, d, f32, u8 = batch, self.dev, torch.float32, torch.uint8
@@ -123,52 +136,55 @@ class Q2KDecodeStack:
         full.copy_(buf.permute(1, 0, 2).reshape(self.B, -1)[:, :n])
 
     # --------------------------------------------------------------- one token
+    def _lin(self, m, x, out, epilogue=EPI_STORE, resid=None, rms=False, qbuf=None):
+        """One linear: y = W Q8_K([rmsnorm] x) with the stack's quantization placement."""
+        fused = self.quant == "fused" or (self.quant == "mixed" and rms)
+        if fused:
+            m.mul_mat_f32_ex(x, self.B, out=out, epilogue=epilogue, resid=resid,
+                             rms_eps=self.eps if rms else None)
+        else:
+            if rms:
+                Q.rms_quantize_q8k(x, self.eps, out=qbuf)
+            else:
+                Q.quantize_q8k(x, out=qbuf)
+            m.mul_mat(qbuf, self.B, out=out, epilogue=epilogue, resid=resid)
+
     def step(self, x_in: torch.Tensor | None = None):
         """Enqueue one pass of the stack on the current stream; returns logits."""
         B, H, hs = self.B, self.H, self.hs
         self.x.copy_(self.x0 if x_in is None else x_in)
         one = self.world == 1
+        L = self._lin
         for wqkv, wo, wgu, wd in self.layers:
-            Q.rms_quantize_q8k(self.x, self.eps, out=self.xq)
-            wqkv.mul_mat(self.xq, B, out=self.qkv)
+            L(wqkv, self.x, self.qkv, rms=True, qbuf=self.xq)
             v_loc = self.qkv[:, 2 * hs:3 * hs]
             if one:
-                Q.quantize_q8k(v_loc, out=self.vq)
+                L(wo, v_loc, self.x, EPI_RESIDUAL, self.x, qbuf=self.vq)
+                L(wgu, self.x, self.h_full, EPI_SILU_MUL, rms=True, qbuf=self.xq)
+                L(wd, self.h_full, self.x, EPI_RESIDUAL, self.x, qbuf=self.hq)
             else:
                 self._gather(self.v_full, v_loc.contiguous(), self.h_lo, self.h_hi)
-                Q.quantize_q8k(self.v_full, out=self.vq)
-            if one:
-                wo.mul_mat(self.vq, B, out=self.x, epilogue=EPI_RESIDUAL, resid=self.x)
-            else:
-                wo.mul_mat(self.vq, B, out=self.x_loc, epilogue=EPI_RESIDUAL,
-                           resid=self.x[:, self.h_lo:self.h_hi])
+                L(wo, self.v_full, self.x_loc, EPI_RESIDUAL, self.x[:, self.h_lo:self.h_hi], qbuf=self.vq)
                 self._gather(self.x, self.x_loc, self.h_lo, self.h_hi)
-            Q.rms_quantize_q8k(self.x, self.eps, out=self.xq)
-            if one:
-                wgu.mul_mat(self.xq, B, out=self.h_full, epilogue=EPI_SILU_MUL)
-            else:
-                wgu.mul_mat(self.xq, B, out=self.h_loc, epilogue=EPI_SILU_MUL)
+                L(wgu, self.x, self.h_loc, EPI_SILU_MUL, rms=True, qbuf=self.xq)
                 self._gather(self.h_full, self.h_loc, self.f_lo, self.f_hi)
-            Q.quantize_q8k(self.h_full, out=self.hq)
-            if one:
-                wd.mul_mat(self.hq, B, out=self.x, epilogue=EPI_RESIDUAL, resid=self.x)
-            else:
-                wd.mul_mat(self.hq, B, out=self.x_loc, epilogue=EPI_RESIDUAL,
-                           resid=self.x[:, self.h_lo:self.h_hi])
+                L(wd, self.h_full, self.x_loc, EPI_RESIDUAL, self.x[:, self.h_lo:self.h_hi], qbuf=self.hq)
                 self._gather(self.x, self.x_loc, self.h_lo, self.h_hi)
-        Q.rms_quantize_q8k(self.x, self.eps, out=self.xq)
         if one:
-            self.lm.mul_mat(self.xq, B, out=self.logits)
+            L(self.lm, self.x, self.logits, rms=True, qbuf=self.xq)
         else:
-            self.lm.mul_mat(self.xq, B, out=self.lg_loc)
+            L(self.lm, self.x, self.lg_loc, rms=True, qbuf=self.xq)
             self._gather(self.logits, self.lg_loc, self.v_lo, self.v_hi)
         return self.logits
 
     # --------------------------------------------------------------- accounting
     def launches_per_step(self) -> int:
-        """Kernels of this library per step (quantizers + GEMVs, chunks of 8 tokens)."""
-        g = math.ceil(self.B / 8)
-        return self.L * (4 + 4 * g) + 1 + g
+        """Kernels of this library per step: one GEMV per linear (the batch is
+        split into launches of 8, 4, 2, 1 tokens) plus one quantizer per
+        linear whose quantization is not fused."""
+        chunks = self.B // 8 + bin(self.B % 8).count("1")
+        per_layer = {"fused": 0, "separate": 4, "mixed": 2}[self.quant]
+        return (self.L * 4 + 1) * chunks + self.L * per_layer + (1 if self.quant == "separate" else 0)
 
     def gemv_list(self):
         """(name, matrix, k, cols, out_rows) of every GEMV in a step."""

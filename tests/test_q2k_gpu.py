@@ -264,3 +264,54 @@ def test_coarse_api_errors(cuda):
     assert st == S.SME_AI_BAD_ARGUMENT
     m.free()
     torch.cuda.synchronize()
+
+
+# ------------------------------------------------------------------ fused fp32-input GEMV
+@pytest.mark.parametrize("rows,k,cols", [(4096, 4096, 1), (128, 11008, 3), (300, 2048, 8), (64, 256, 5)])
+def test_fused_prologue_bit_identical(cuda, rows, k, cols):
+    """Quantizing in the GEMV prologue (with and without RMSNorm, strided rows)
+    gives exactly the two-kernel result; the cluster split (4096 rows -> 128
+    groups) and the unsplit path agree too."""
+    wb = gpu_q2k_weights(cuda, rows, k, rows + cols)
+    m = Q.Q2KMatrix(wb, rows, k)
+    g = torch.Generator(device=cuda).manual_seed(cols)
+    xs = torch.randn((cols, k + 64), generator=g, device=cuda) * 3
+    x = xs[:, :k]                                  # row stride k + 64
+    y_two = m.mul_mat(Q.quantize_q8k(x.contiguous()), cols)
+    y_one = m.mul_mat_f32_ex(x, cols)
+    assert torch.equal(y_one, y_two)
+    y_two = m.mul_mat(Q.rms_quantize_q8k(x.contiguous(), 1e-5), cols)
+    y_one = m.mul_mat_f32_ex(x, cols, rms_eps=1e-5)
+    assert torch.equal(y_one, y_two)
+    r = torch.randn((cols, rows), generator=g, device=cuda)
+    y_res = m.mul_mat_f32_ex(x, cols, out=r.clone(), epilogue=S.EPI_RESIDUAL, resid=r, rms_eps=1e-5)
+    assert torch.equal(y_res, r + y_two)
+    assert torch.equal(m.mul_mat_f32(x.contiguous()), m.mul_mat(Q.quantize_q8k(x.contiguous()), cols))
+
+
+def test_fused_silu_epilogue_matches_two_kernel(cuda):
+    hidden, k = 1000, 4096
+    wg = gpu_q2k_weights(cuda, hidden, k, 41)
+    wu = gpu_q2k_weights(cuda, hidden, k, 42)
+    m = Q.Q2KMatrix(torch.stack([wg, wu], 1).reshape(2 * hidden, -1), 2 * hidden, k)
+    x = torch.randn((2, k), generator=torch.Generator(device=cuda).manual_seed(4), device=cuda)
+    h1 = m.mul_mat_f32_ex(x, 2, epilogue=S.EPI_SILU_MUL, rms_eps=1e-5)
+    h2 = m.mul_mat(Q.rms_quantize_q8k(x, 1e-5), 2, epilogue=S.EPI_SILU_MUL)
+    assert torch.equal(h1, h2)
+
+
+@pytest.mark.parametrize("rows,k,cols", [(148 * 4 * 32 + 40, 512, 1), (148 * 3 * 32, 256, 4), (600 * 32, 768, 2)])
+def test_mul_mat_many_row_groups_per_cta(cuda, oracle, rows, k, cols):
+    """More 32-row groups than SMs: each persistent CTA walks several groups
+    through the double-buffered terms (and a ring shorter than its stages)."""
+    y, exp = _check_mul_mat(cuda, oracle, rows, k, cols, seed=rows % 97, threads=16)
+    assert np.array_equal(y.view(np.uint32), exp.view(np.uint32))
+
+
+def test_no_device_error_recorded(cuda):
+    """Every bounded wait in the GEMV completed: the device error word is clear."""
+    import ctypes as C
+    L = S.lib()
+    code = C.c_uint(0)
+    assert L.smeai_take_device_error(C.byref(code)) == 0
+    assert code.value == 0

@@ -1,0 +1,77 @@
+"""The Llama-shape Q2_K decode stack (the benchmark workload) against the CPU
+oracle run step by step on the same blocks, at reduced sizes."""
+import numpy as np
+import pytest
+import torch
+
+import smeai_b200 as S
+from smeai_b200.stack import Q2KDecodeStack, shard_range
+
+pytestmark = pytest.mark.gpu
+
+
+def oracle_stack(O, st: Q2KDecodeStack, x0: np.ndarray):
+    """Same computation on the CPU: rmsnorm+Q8_K, Q2_K GEMVs, silu*mul, residuals."""
+    B2 = lambda t: t.cpu().numpy().reshape(-1).view(O.BLOCK_Q2_K)
+    H, F, V = st.H, st.F, st.V
+    x = x0.astype(np.float32).copy()
+    for blk in st.blocks:
+        xq = O.rmsnorm_quantize_q8_K(x, st.eps)
+        v = O.q2k_mul_mat(B2(blk["v"]), H, H, xq, 1, n_threads=8)[0]
+        x = (x + O.q2k_mul_mat(B2(blk["o"]), H, H, O.quantize_q8_K(v), 1, n_threads=8)[0]).astype(np.float32)
+        xq = O.rmsnorm_quantize_q8_K(x, st.eps)
+        g = O.q2k_mul_mat(B2(blk["g"]), F, H, xq, 1, n_threads=8)[0]
+        u = O.q2k_mul_mat(B2(blk["u"]), F, H, xq, 1, n_threads=8)[0]
+        h = O.silu_mul(g, u)
+        x = (x + O.q2k_mul_mat(B2(blk["d"]), H, F, O.quantize_q8_K(h), 1, n_threads=8)[0]).astype(np.float32)
+    xq = O.rmsnorm_quantize_q8_K(x, st.eps)
+    return O.q2k_mul_mat(B2(st.lm_blocks), V, H, xq, 1, n_threads=8)[0]
+
+
+def test_stack_matches_oracle(cuda, oracle):
+    st = Q2KDecodeStack(n_layers=2, hidden=1024, ffn=2816, vocab=4000, device=cuda, seed=3, keep_blocks=True)
+    logits = st.step().clone()
+    torch.cuda.synchronize()
+    exp = oracle_stack(oracle, st, st.x0.cpu().numpy()[0])
+    got = logits.cpu().numpy()[0]
+    assert np.isfinite(got).all()
+    # silu uses CUDA expf vs glibc expf; a last-bit difference can move one
+    # Q8_K code, so the stack is held to a relative bar, not bit identity
+    scale = np.abs(exp).max()
+    assert np.abs(got - exp).max() <= 1e-3 * scale
+
+
+@pytest.mark.parametrize("quant", ["fused", "separate", "mixed"])
+def test_stack_quant_placements_identical(cuda, quant):
+    """Fused, separate and mixed Q8_K placement give bit-identical logits."""
+    ref = Q2KDecodeStack(n_layers=2, hidden=1024, ffn=2816, vocab=2048, device=cuda, seed=9, quant="fused")
+    a = ref.step().clone()
+    st = Q2KDecodeStack(n_layers=2, hidden=1024, ffn=2816, vocab=2048, device=cuda, seed=9, quant=quant)
+    assert torch.equal(st.step(), a)
+
+
+def test_stack_graph_replay_is_deterministic(cuda):
+    st = Q2KDecodeStack(n_layers=3, hidden=1024, ffn=2816, vocab=2048, device=cuda, seed=5)
+    eager = st.step().clone()
+    stream = torch.cuda.Stream()
+    with torch.cuda.stream(stream):
+        st.step()
+    stream.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=stream):
+        st.step()
+    for _ in range(3):
+        with torch.cuda.stream(stream):
+            g.replay()
+    stream.synchronize()
+    assert torch.equal(st.logits, eager)
+    assert st.launches_per_step() == 3 * 4 + 1 + 3 * 4 + 1
+
+
+def test_shard_ranges_partition_rows():
+    for n in (4096, 11008, 32000, 12288):
+        for world in (1, 2, 4, 8):
+            spans = [shard_range(n, r, world) for r in range(world)]
+            assert spans[0][0] == 0 and spans[-1][1] == n
+            assert all(a[1] == b[0] for a, b in zip(spans, spans[1:]))
+            assert all((hi - lo) % 32 == 0 for lo, hi in spans[:-1])
