@@ -207,6 +207,32 @@ sme_ai_status sme_ai_linear_packed_f16f32_device(const sme_ai_fp16 *input, uint6
                                                  const sme_ai_packed_linear_weight *packed_weight,
                                                  const float *bias, int act, float *output, void *stream);
 
+/* SwiGLU on packed weights for callers that cannot allocate device memory.
+ * No counterpart in the reference.  Some callers may not call cudaMalloc at
+ * all: code running under a framework that owns the whole device heap
+ * through its own pool allocator, or a steady-state loop that must never make
+ * an allocation (which may synchronize the device).  This entry point
+ * allocates nothing: every pointer is device memory supplied by the caller
+ * (input [batch][in], biases, output [batch][out]); the fp16 hidden state
+ * lives in a fixed device array built into the library, 1 MiB
+ * (batch * hidden_features <= 524288; larger requests return
+ * SME_AI_WORKSPACE_TOO_SMALL with the reason in smeai_last_error()), held on
+ * every GPU that loads the library until the process exits.  Work is queued
+ * on `stream` (a cudaStream_t, NULL = legacy default) and the call returns
+ * without waiting; results equal sme_ai_swiglu_sme_packed_f16f32's.
+ * The first call on each device looks up the array's device address (a
+ * one-time set-up), so make that first call before any stream capture.  All
+ * calls share the one array: calls whose work overlaps on the GPU (different
+ * streams, or different host threads on one device) race on it and must be
+ * serialized by the caller.  Nothing in the array needs to start at zero:
+ * each call writes every hidden value before reading it. */
+sme_ai_status sme_ai_swiglu_packed_f16f32_noalloc(const sme_ai_fp16 *input, uint64_t batch,
+                                                  const sme_ai_packed_linear_weight *gate_weight,
+                                                  const float *gate_bias,
+                                                  const sme_ai_packed_linear_weight *up_weight, const float *up_bias,
+                                                  const sme_ai_packed_linear_weight *down_weight,
+                                                  const float *down_bias, float *output, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -7,6 +7,8 @@
 // the calling thread); device pointers are used in place.
 #include <string.h>
 
+#include <mutex>
+
 #include "common.cuh"
 #include "elementwise.h"
 #include "linear.h"
@@ -250,6 +252,42 @@ void ew_act(float* data, uint64_t count, int act) {
   if (!r) r = c.o.finish(c.stream);
   if (!r) sync(c.stream);
   c.o.host = nullptr;
+}
+
+// ---- fixed scratch for sme_ai_swiglu_packed_f16f32_noalloc ------------------
+// The fp16 hidden state of that entry point lives in this file-scope device
+// array, not in a workspace, so the entry point never allocates.  Its size is
+// fixed: batch * hidden_features must not exceed kNoAllocHiddenElems
+// (524288 fp16 values = 1 MiB).  Every GPU that loads the library holds the
+// array until the process exits.  In host code `g_noalloc_hidden` is only a
+// stand-in symbol, not a device address: the address is fetched once per
+// device with cudaGetSymbolAddress and passed to the kernels.
+constexpr uint64_t kNoAllocHiddenElems = 512u * 1024u;
+static __device__ __align__(256) __half g_noalloc_hidden[kNoAllocHiddenElems];
+
+std::mutex g_noalloc_mu;
+__half* g_noalloc_ptr[64] = {nullptr};
+
+// Device address of the scratch on the current device (set up on first use).
+int noalloc_scratch(__half** out) {
+  int dev = 0;
+  SMEAI_CUDA_TRY(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64) {
+    set_last_error("device ordinal %d out of range", dev);
+    return kUnsupported;
+  }
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (!g_noalloc_ptr[dev]) {
+    void* p = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_hidden);
+    if (e != cudaSuccess || !p) {
+      set_last_error("cudaGetSymbolAddress of the fixed scratch failed: %s", cudaGetErrorString(e));
+      return kCudaError;
+    }
+    g_noalloc_ptr[dev] = static_cast<__half*>(p);
+  }
+  *out = g_noalloc_ptr[dev];
+  return kOk;
 }
 
 }  // namespace
@@ -604,6 +642,42 @@ sme_ai_status sme_ai_linear_packed_f16f32_device(const sme_ai_fp16* input, uint6
   if (!p || p->is_f32 || act < kActNone || act > kActSilu) return SME_AI_BAD_ARGUMENT;
   return st(packed_linear_dev(reinterpret_cast<const __half*>(input), batch, pw, bias, act, output,
                               static_cast<cudaStream_t>(stream)));
+}
+
+
+// SwiGLU on packed weights that allocates nothing (see sme_ai_ops.h).  Same
+// kernels and same results as sme_ai_swiglu_sme_packed_f16f32; the hidden
+// state goes to the fixed device array above instead of ws->tmp_f16.
+sme_ai_status sme_ai_swiglu_packed_f16f32_noalloc(const sme_ai_fp16* input, uint64_t batch,
+                                                  const sme_ai_packed_linear_weight* gate_weight,
+                                                  const float* gate_bias,
+                                                  const sme_ai_packed_linear_weight* up_weight, const float* up_bias,
+                                                  const sme_ai_packed_linear_weight* down_weight,
+                                                  const float* down_bias, float* output, void* stream) {
+  if (!input || !gate_weight || !up_weight || !down_weight || !output || !batch) return SME_AI_BAD_ARGUMENT;
+  if (!gate_weight->packed_weight || !up_weight->packed_weight || !down_weight->packed_weight)
+    return SME_AI_BAD_ARGUMENT;
+  if (gate_weight->out_features != up_weight->out_features ||
+      gate_weight->out_features != down_weight->in_features || gate_weight->in_features != up_weight->in_features)
+    return SME_AI_BAD_ARGUMENT;
+  const PackedPriv *pg = ppriv(gate_weight), *pu = ppriv(up_weight), *pd = ppriv(down_weight);
+  if (!pg || !pu || !pd || pg->is_f32 || pu->is_f32 || pd->is_f32) return SME_AI_BAD_ARGUMENT;
+  const uint64_t M = batch, K = gate_weight->in_features, H = gate_weight->out_features,
+                 N = down_weight->out_features;
+  if (H > kNoAllocHiddenElems || M > kNoAllocHiddenElems / H) {
+    set_last_error("sme_ai_swiglu_packed_f16f32_noalloc: batch*hidden_features = %llu exceeds the fixed "
+                   "scratch of %llu fp16 values",
+                   (unsigned long long)(M * H), (unsigned long long)kNoAllocHiddenElems);
+    return SME_AI_WORKSPACE_TOO_SMALL;
+  }
+  if (!device_ready()) return SME_AI_UNSUPPORTED;
+  __half* hid = nullptr;
+  int r = noalloc_scratch(&hid);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (!r) r = swiglu_gate_up_f16(reinterpret_cast<const __half*>(input), M, K, static_cast<const __half*>(pg->dev),
+                                 static_cast<const __half*>(pu->dev), pg->ldb, H, gate_bias, up_bias, hid, s);
+  if (!r) r = linear_f16(hid, M, H, static_cast<const __half*>(pd->dev), pd->ldb, N, down_bias, kActNone, output, s);
+  return st(r);
 }
 
 }  // extern "C"
