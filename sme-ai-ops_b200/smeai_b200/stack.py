@@ -31,11 +31,38 @@ LLAMA7B = dict(n_layers=32, hidden=4096, ffn=11008, vocab=32000)
 
 
 def shard_range(n: int, rank: int, world: int, align: int = 32):
-    """Contiguous row slice of rank `rank`: multiples of `align` except the last."""
-    per = int(math.ceil(n / world / align)) * align
+    """Contiguous row slice [lo, hi) of rank `rank`: every slice but the last is
+    ceil(n / world / align) * align rows (the last may be shorter or empty)."""
+    per = shard_stride(n, world, align)
     lo = min(n, rank * per)
     hi = min(n, lo + per)
     return lo, hi
+
+
+def shard_stride(n: int, world: int, align: int = 32) -> int:
+    return int(math.ceil(n / world / align)) * align
+
+
+def gather_rows(full, local, n: int, world: int, group=None, scratch=None):
+    """full[:, :n] <- the ranks' row slices in rank order (torch.distributed).
+
+    `local` is this rank's [B, hi-lo] slice; slices follow shard_range(n, ., world).
+    When every slice has the same length and B == 1 the gather lands in `full`
+    directly; otherwise the slices are padded to the common stride, gathered into
+    `scratch` ([world * B, stride], allocated if None) and copied out."""
+    import torch.distributed as dist
+    B, have = local.shape
+    stride = shard_stride(n, world)
+    if B == 1 and stride * world == n and have == stride and full.is_contiguous():
+        dist.all_gather_into_tensor(full.view(-1)[:n], local.reshape(-1), group=group)
+        return full
+    if scratch is None:
+        scratch = local.new_empty((world * B, stride))
+    send = local.new_zeros((B, stride))
+    send[:, :have].copy_(local)
+    dist.all_gather_into_tensor(scratch, send, group=group)
+    full[:, :n].copy_(scratch.view(world, B, stride).permute(1, 0, 2).reshape(B, world * stride)[:, :n])
+    return full
 
 
 def gemv_bytes(rows: int, k: int, cols: int, out_rows: int | None = None) -> int:
@@ -125,15 +152,7 @@ class Q2KDecodeStack:
             if full.data_ptr() != local.data_ptr():
                 full.copy_(local)
             return
-        import torch.distributed as dist
-        per = local.shape[1]
-        n = full.shape[1]
-        if self.B == 1 and per * self.world == n:
-            dist.all_gather_into_tensor(full.view(-1), local.view(-1), group=self.group)
-            return
-        buf = torch.empty((self.world, self.B, per), dtype=local.dtype, device=local.device)
-        dist.all_gather_into_tensor(buf, local.contiguous(), group=self.group)
-        full.copy_(buf.permute(1, 0, 2).reshape(self.B, -1)[:, :n])
+        gather_rows(full, local, full.shape[1], self.world, self.group)
 
     # --------------------------------------------------------------- one token
     def _lin(self, m, x, out, epilogue=EPI_STORE, resid=None, rms=False, qbuf=None):

@@ -1,0 +1,66 @@
+"""Row-sharded decode stack on 2 GPUs (NCCL all-gathers) against the
+single-GPU stack: logits must be bit-identical (sharding only moves rows
+between GPUs; every row's arithmetic is unchanged).  Skips with < 2 GPUs."""
+import datetime
+import os
+import socket
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+
+DIMS = dict(n_layers=2, hidden=1024, ffn=2816, vocab=4096, seed=11)
+
+
+def _port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _rank(rank, world, port, results):
+    import sys
+    root = os.path.abspath(os.path.join(os.path.dirname(__file__), ".."))
+    for p in (root, os.path.join(root, "sme-ai-ops_b200")):
+        if p not in sys.path:
+            sys.path.insert(0, p)
+    import torch.distributed as dist
+    from smeai_b200.stack import Q2KDecodeStack
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=dev)
+    try:
+        st = Q2KDecodeStack(rank=rank, world=world, device=dev, **DIMS)
+        eager = st.step().clone()
+        stream = torch.cuda.Stream()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            st.step()
+        with torch.cuda.stream(stream):
+            g.replay()
+        stream.synchronize()
+        results[rank] = (eager.cpu(), st.logits.cpu().clone())
+        del g
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+def test_two_gpu_sharded_stack_matches_single_gpu(cuda):
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    from smeai_b200.stack import Q2KDecodeStack
+    ref = Q2KDecodeStack(device=cuda, **DIMS).step().cpu().clone()
+    torch.cuda.synchronize()
+    results = mp.get_context("spawn").Manager().dict()
+    mp.start_processes(_rank, args=(2, _port(), results), nprocs=2, start_method="spawn")
+    for r in range(2):
+        eager, graphed = results[r]
+        assert torch.equal(eager, ref), r
+        assert torch.equal(graphed, ref), r
