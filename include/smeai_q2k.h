@@ -93,9 +93,15 @@ int smeai_rms_q8k_quantize(const float *x_dev, int64_t ld_x, int64_t n_cols, int
 
 /* y[c*ldy + r] = sum_k W[r,k] * X[c,k]  for r < n_rows, c < n_cols: the
  * result of ggml's mul_mat for a Q2_K src0 and Q8_K-quantized src1 (dst
- * rows contiguous).  n_rows and k must match the handle. */
+ * rows contiguous).  n_rows and k must match the handle.  Up to 15 activation
+ * rows run on the decode GEMV, 16 or more on the tensor-core GEMM (the
+ * analogue of ggml_gemv_ / ggml_gemm_q2_K_8x8_q8_K); both give identical bits.
+ * The GEMM keeps a library-owned device scratch per (device, stream). */
 int smeai_q2k_mul_mat(const void *w_dev, int64_t n_rows, int64_t k, const void *x_q8k_dev, int64_t n_cols,
                       float *y_dev, size_t ldy, void *stream);
+/* The tensor-core GEMM for any n_cols >= 1 (tcgen05.mma, TMEM accumulators). */
+int smeai_q2k_mul_mat_tc(const void *w_dev, const void *x_q8k_dev, int64_t n_cols, float *y_dev, size_t ldy,
+                         void *stream);
 
 /* Fused epilogues of the decode GEMV (n_cols <= 8 per launch, larger counts
  * are split):

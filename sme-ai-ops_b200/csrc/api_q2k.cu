@@ -1,6 +1,10 @@
 // api_q2k.cu -- the C-ABI of include/smeai_q2k.h.
 #include <string.h>
 
+#include <map>
+#include <mutex>
+#include <utility>
+
 #include "common.cuh"
 #include "kernels.h"
 #include "runtime.h"
@@ -43,6 +47,34 @@ struct ThreadCtx {
 ThreadCtx& tctx() {
   thread_local ThreadCtx ctx;
   return ctx;
+}
+
+// Library-owned scratch of the tensor-core GEMM (activation operands in UMMA
+// order), one growable buffer per (device, stream).
+std::mutex g_gemm_mu;
+std::map<std::pair<int, cudaStream_t>, DeviceBuffer*> g_gemm_scratch;
+
+int gemm_scratch(cudaStream_t s, size_t bytes, void** out) {
+  int dev = 0;
+  SMEAI_CUDA_TRY(cudaGetDevice(&dev));
+  std::lock_guard<std::mutex> lock(g_gemm_mu);
+  DeviceBuffer*& b = g_gemm_scratch[{dev, s}];
+  if (!b) b = new DeviceBuffer();
+  const int st = b->reserve(bytes);
+  if (st) return st;
+  *out = b->ptr;
+  return kOk;
+}
+
+// Activation rows at which mul_mat switches from the GEMV to the tensor cores.
+constexpr int64_t kGemmMinCols = 16;
+
+int mul_mat_tc(const Q2KWeight& w, const void* xq, int64_t n_cols, float* y, int64_t ldy, cudaStream_t s) {
+  const size_t need = q2k_gemm_scratch_bytes(n_cols, w.nb);
+  void* scratch = nullptr;
+  const int st = gemm_scratch(s, need, &scratch);
+  if (st) return st;
+  return q2k_gemm_tc(w, xq, n_cols, y, ldy, scratch, need, s);
 }
 
 }  // namespace
@@ -199,7 +231,15 @@ int smeai_q2k_mul_mat(const void* w_dev, int64_t n_rows, int64_t k, const void* 
                    (long long)n_rows, (long long)k, (long long)h->w.n_rows, (long long)h->w.k);
     return kBadArgument;
   }
+  if (n_cols >= kGemmMinCols) return mul_mat_tc(h->w, x_q8k_dev, n_cols, y_dev, (int64_t)ldy, as_stream(stream));
   return q2k_gemv(h->w, x_q8k_dev, n_cols, y_dev, (int64_t)ldy, kEpiStore, nullptr, 0, as_stream(stream));
+}
+
+int smeai_q2k_mul_mat_tc(const void* w_dev, const void* x_q8k_dev, int64_t n_cols, float* y_dev, size_t ldy,
+                         void* stream) {
+  const Handle* h = as_handle(w_dev);
+  if (!h) return kBadArgument;
+  return mul_mat_tc(h->w, x_q8k_dev, n_cols, y_dev, (int64_t)ldy, as_stream(stream));
 }
 
 int smeai_q2k_mul_mat_ex(const void* w_dev, const void* x_q8k_dev, int64_t n_cols, float* y_dev, size_t ldy,

@@ -57,6 +57,13 @@ int q2k_gemv_any(const Q2KWeight& w, int in_mode, const void* x, int64_t ld_x, f
 int q2k_gemv(const Q2KWeight& w, const void* xq, int64_t n_cols, float* y, int64_t ldy, int epilogue,
              const float* resid, int64_t ld_resid, cudaStream_t stream);
 
+// Tensor-core GEMM for many activation rows (prefill): y = W x for n_cols
+// Q8_K rows, store epilogue, bit-identical to q2k_gemv.  Needs a 256-byte
+// aligned scratch of q2k_gemm_scratch_bytes(n_cols, nb) bytes.
+size_t q2k_gemm_scratch_bytes(int64_t n_cols, int nb);
+int q2k_gemm_tc(const Q2KWeight& w, const void* xq, int64_t n_cols, float* y, int64_t ldy, void* scratch,
+                size_t scratch_bytes, cudaStream_t stream);
+
 // Per-(row, super-block) integer sums (isum, summs), [n_rows][nb] each, for a
 // single activation row -- the exactness check of the GEMV's integer core.
 int q2k_block_sums(const Q2KWeight& w, const void* xq, int32_t* isum, int32_t* summs, cudaStream_t stream);

@@ -96,6 +96,14 @@ class Q2KMatrix:
         check(st, "q2k_mul_mat")
         return out
 
+    def mul_mat_tc(self, xq: torch.Tensor, n_cols: int, out: torch.Tensor | None = None) -> torch.Tensor:
+        """The tensor-core GEMM path (any number of activation rows)."""
+        if out is None:
+            out = torch.empty((n_cols, self.n_rows), dtype=torch.float32, device=xq.device)
+        check(lib().smeai_q2k_mul_mat_tc(self.handle, _ptr(xq), n_cols, _ptr(out), out.stride(0), cur_stream()),
+              "q2k_mul_mat_tc")
+        return out
+
     def mul_mat_f32(self, x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
         x2 = x.reshape(-1, self.k).contiguous()
         n_cols = x2.shape[0]
