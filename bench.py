@@ -47,7 +47,8 @@ def parse_args():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["decode", "gemv"], default="decode")
+    ap.add_argument("--workload", choices=["decode", "gemv", "prefill"], default="decode")
+    ap.add_argument("--prefill-tokens", type=int, default=512, help="prefill workload: activation rows")
     ap.add_argument("--layers", type=int, default=32)
     ap.add_argument("--quant", choices=["fused", "separate", "mixed"], default="separate",
                     help="where each linear's Q8_K quantization runs (results are identical)")
@@ -231,6 +232,60 @@ def run_reference(args):
     return 0
 
 
+def tensor_peak():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            return float(json.load(f)["bf16_tflops"]), "measured"
+    except Exception:
+        return 1590.0, "fallback"
+
+
+def gemv_roofline(gemvs, stream, dev, peak, peak_kind):
+    """Every GEMV of a step timed alone: events around each launch, queued
+    behind a sleep kernel so launch gaps do not count; consecutive GEMVs read
+    distinct weights, so nothing sits in L2."""
+    import torch
+    from smeai_b200 import q2k as Q
+    from smeai_b200.stack import gemv_bytes
+    per = {}
+    with torch.cuda.stream(stream):
+        xq_by_k = {}
+        for name, m in gemvs:
+            if m.k not in xq_by_k:
+                xq_by_k[m.k] = Q.quantize_q8k(torch.randn((1, m.k), device=dev))
+        outs = {name: torch.empty((1, m.n_rows), device=dev) for name, m in gemvs}
+        evs = []
+        torch.cuda._sleep(20_000_000)
+        for name, m in gemvs:
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            m.mul_mat(xq_by_k[m.k], 1, out=outs[name])
+            b.record(stream)
+            evs.append((name, m, a, b))
+    stream.synchronize()
+    tot_b, tot_ms = 0, 0.0
+    for name, m, a, b in evs:
+        d = a.elapsed_time(b)
+        nbytes = gemv_bytes(m.n_rows, m.k, 1)
+        agg = per.setdefault(name, [0, 0.0, 0])
+        agg[0] += nbytes
+        agg[1] += d
+        agg[2] += 1
+        tot_b += nbytes
+        tot_ms += d
+    achieved = tot_b / (tot_ms / 1e3) / 1e9
+    ratio = traffic_ratio()
+    launch_avg_bytes = tot_b / len(evs)
+    return {"bound": "hbm", "kernel": "q2k_gemv_kernel", "achieved": achieved, "peak": peak,
+            "unit": "GB/s", "frac": achieved / peak, "peak_kind": peak_kind,
+            "traffic": (ratio * launch_avg_bytes) if ratio else None,
+            "algorithmic_bytes_per_launch": launch_avg_bytes,
+            "avg_launch_us": tot_ms / len(evs) * 1e3,
+            "per_matrix": {n: {"GB/s": v[0] / (v[1] / 1e3) / 1e9, "us": v[1] / v[2] * 1e3, "launches": v[2]}
+                           for n, v in per.items()}}
+
+
 # ---------------------------------------------------------------------------- GPU side
 def run_ours(args):
     import torch
@@ -307,7 +362,36 @@ def run_ours(args):
                     f"{copies} rotating weight copies ({copies * mbytes / 2**20:.0f} MB > L2)")
         gemvs = [("gemv", m) for m in mats]
 
-    total_bytes = local_bytes * world if args.workload == "decode" else local_bytes * world
+    if args.workload == "prefill":
+        # config 4: activations [512, 4096] (Q8_K per row) x W[11008, 4096] Q2_K -> [512, 11008]
+        rows, k, cols = 11008, 4096, args.prefill_tokens
+        mbytes = rows * (k // 256) * 84
+        copies = max(2, min(48, -(-4 * 126 * 2**20 // mbytes)))
+        g = torch.Generator(device=dev).manual_seed(0)
+        mats = [Q.Q2KMatrix(Q.quantize_q2k(torch.randn((rows, k), generator=g, device=dev) * 0.02), rows, k)
+                for _ in range(copies)]
+        x_in = torch.randn((cols, k), generator=g, device=dev)
+        xq = Q.quantize_q8k(x_in)
+        y = torch.empty((cols, rows), device=dev)
+        it = {"i": 0}
+
+        def step():
+            m = mats[it["i"] % copies]
+            it["i"] += 1
+            Q.quantize_q8k(x_in, out=xq)
+            m.mul_mat_tc(xq, cols, out=y)
+            return y
+
+        launches_per_step = 4   # quantizer, operand prepass, GEMM (+ a memset of the operand padding)
+        local_bytes = gemv_bytes(rows, k, cols)
+        h2d, d2h = cols * k * 4, cols * rows * 4
+        out_buf = y
+        workload = (f"Q2_K prefill mul_mat: activations [{cols},{k}] ~N(0,1) (Q8_K per row) x W[{rows},{k}] "
+                    f"~N(0,0.02) Q2_K -> fp32 [{cols},{rows}] on tcgen05; {copies} rotating weight copies")
+        gemvs = []
+        prefill_ops = 2 * rows * k * cols
+
+    total_bytes = local_bytes * world
 
     # ---- warm-up, then capture into a CUDA graph: one step (decode) or one
     # pass over every rotating weight copy (gemv; a step is then one GEMV)
@@ -315,7 +399,8 @@ def run_ours(args):
         step()
     stream.synchronize()
     barrier()
-    steps_per_replay = 1 if args.workload == "decode" else len(gemvs)
+    steps_per_replay = {"decode": 1, "gemv": len(gemvs), "prefill": len(mats) if args.workload == "prefill"
+                        else 0}[args.workload]
     graph = torch.cuda.CUDAGraph()
     with torch.cuda.graph(graph, stream=stream):
         for _ in range(steps_per_replay):
@@ -374,45 +459,31 @@ def run_ours(args):
     e2e_ms = max_over_ranks(e2e_ms)
     e2e_value = total_bytes / (e2e_ms / 1e3) / 1e9
 
+    if args.workload == "prefill":
+        # roofline of the GEMM kernel: events around each launch (distinct weights)
+        evs = []
+        with torch.cuda.stream(stream):
+            torch.cuda._sleep(20_000_000)
+            for m in mats[:8]:
+                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a.record(stream)
+                m.mul_mat_tc(xq, cols, out=y)
+                b.record(stream)
+                evs.append((a, b))
+        stream.synchronize()
+        gemm_ms = sorted(a.elapsed_time(b) for a, b in evs)[len(evs) // 2]
+        tpeak, tkind = tensor_peak()
+        achieved = prefill_ops / (gemm_ms / 1e3) / 1e12
+        roofline = {"bound": "tensor", "kernel": "q2k_gemm_tc_kernel (+ operand prepass)", "achieved": achieved,
+                    "peak": tpeak, "unit": "TFLOP/s", "frac": achieved / tpeak, "peak_kind": tkind,
+                    "traffic": None, "ops_per_launch": prefill_ops, "median_launch_us": gemm_ms * 1e3,
+                    "note": "fp16 tensor-core MMAs on exact integer operands; peak is the measured dense bf16 "
+                            "GEMM rate (same tensor throughput as fp16)"}
     # ---- roofline of the dominant kernel: every GEMV of a step timed alone
     # (events around each launch, queued behind a sleep so launch gaps do not
     # count; consecutive GEMVs read distinct weights, so nothing sits in L2)
-    per = {}
-    with torch.cuda.stream(stream):
-        xq_by_k = {}
-        for name, m in gemvs:
-            if m.k not in xq_by_k:
-                xq_by_k[m.k] = Q.quantize_q8k(torch.randn((1, m.k), device=dev))
-        outs = {name: torch.empty((1, m.n_rows), device=dev) for name, m in gemvs}
-        evs = []
-        torch.cuda._sleep(20_000_000)
-        for name, m in gemvs:
-            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            a.record(stream)
-            m.mul_mat(xq_by_k[m.k], 1, out=outs[name])
-            b.record(stream)
-            evs.append((name, m, a, b))
-    stream.synchronize()
-    tot_b, tot_ms = 0, 0.0
-    for name, m, a, b in evs:
-        d = a.elapsed_time(b)
-        nbytes = gemv_bytes(m.n_rows, m.k, 1)
-        agg = per.setdefault(name, [0, 0.0, 0])
-        agg[0] += nbytes
-        agg[1] += d
-        agg[2] += 1
-        tot_b += nbytes
-        tot_ms += d
-    achieved = tot_b / (tot_ms / 1e3) / 1e9
-    ratio = traffic_ratio()
-    launch_avg_bytes = tot_b / len(evs)
-    roofline = {"bound": "hbm", "kernel": "q2k_gemv_kernel", "achieved": achieved, "peak": peak,
-                "unit": "GB/s", "frac": achieved / peak, "peak_kind": peak_kind,
-                "traffic": (ratio * launch_avg_bytes) if ratio else None,
-                "algorithmic_bytes_per_launch": launch_avg_bytes,
-                "avg_launch_us": tot_ms / len(evs) * 1e3,
-                "per_matrix": {n: {"GB/s": v[0] / (v[1] / 1e3) / 1e9, "us": v[1] / v[2] * 1e3, "launches": v[2]}
-                               for n, v in per.items()}}
+    if gemvs:
+        roofline = gemv_roofline(gemvs, stream, dev, peak, peak_kind)
 
     # ---- CPU baseline (rank 0, one GPU only)
     cpu = None
@@ -430,12 +501,16 @@ def run_ours(args):
             "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "int8xu2", "data": "synthetic",
-            "tokens_per_s": (1e3 / ms) if args.workload == "decode" else None,
+            "tokens_per_s": (1e3 / ms) if args.workload == "decode" else
+            ((args.prefill_tokens * 1e3 / ms) if args.workload == "prefill" else None),
             "pct_of_hbm_peak": value / (peak * world) * 100,
-            "config": {"workload": workload, "global_batch": 1, "seq_len": 1,
+            "config": {"workload": workload,
+                       "global_batch": args.prefill_tokens if args.workload == "prefill" else 1, "seq_len": 1,
                        "parallelism": f"row-shard tp{world}" if world > 1 else "single GPU",
                        "l2": "inputs larger than L2 (2.17 GB of weights per step)" if args.workload == "decode"
                        else "inputs larger than L2 (rotating distinct weight copies)",
+                       **({"prefill_ops_per_step": prefill_ops, "tops": prefill_ops / (ms / 1e3) / 1e12}
+                          if args.workload == "prefill" else {}),
                        "cuda_graph": use_graph, "pdl": os.environ.get("SMEAI_PDL", "1") != "0",
                        "q8k_placement": args.quant},
             "clocks": clocks,
