@@ -92,15 +92,15 @@ __host__ __device__ __forceinline__ size_t smem_fixed_bytes(int T, int nb) {
   return align16((size_t)T * nb * 256) + align16((size_t)T * nb * 32) + align16((size_t)T * nb * 4) +
          align16((size_t)T * (nb + 1) * 4) + align16((size_t)2 * T * nb * 128) + 8 * 6;
 }
-__host__ __device__ __forceinline__ size_t smem_total_bytes(int T, int nb, int stages) {
-  return (size_t)stages * kTileBytes + smem_fixed_bytes(T, nb) + (size_t)stages * 16;
+__host__ __device__ __forceinline__ size_t smem_total_bytes(int T, int nb, int stages, int consumers) {
+  return (size_t)stages * consumers * kTileBytes + smem_fixed_bytes(T, nb) + (size_t)stages * 16;
 }
 
-__device__ __forceinline__ Smem carve(uint8_t* base, int T, int nb, int stages) {
+__device__ __forceinline__ Smem carve(uint8_t* base, int T, int nb, int stages, int consumers) {
   Smem m;
   size_t o = 0;
   m.ring = base;
-  o += (size_t)stages * kTileBytes;
+  o += (size_t)stages * consumers * kTileBytes;
   m.qs = reinterpret_cast<int4*>(base + o);
   o += align16((size_t)T * nb * 256);
   m.bs = reinterpret_cast<int*>(base + o);
@@ -247,13 +247,17 @@ __global__ void __launch_bounds__(kMaxThreads) q2k_gemv_kernel(const GemvParams 
   const int64_t C = gridDim.x;
   const int64_t g0 = (int64_t)blockIdx.x * p.n_groups / C, g1 = ((int64_t)blockIdx.x + 1) * p.n_groups / C;
   const int ng = (int)(g1 - g0);
-  const int n_stages = ng * nb;
-  const Smem m = carve(smem, T, nb, S);
+  // a stage is one bulk copy of kConsumers consecutive super-blocks of one row
+  // group (fewer in the group's last chunk); consumer warp w takes block w of it
+  const int nchunks = (nb + kConsumers - 1) / kConsumers;
+  const int n_stages = ng * nchunks;
+  const int stage_bytes = kConsumers * kTileBytes;
+  const Smem m = carve(smem, T, nb, S, kConsumers);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
       mbar_init(&m.full[s], 1);
-      mbar_init(&m.empty[s], 32);
+      mbar_init(&m.empty[s], kConsumers * 32);
     }
     mbar_init(&m.grp[0], kConsumers * 32);
     mbar_init(&m.grp[1], kConsumers * 32);
@@ -278,8 +282,11 @@ __global__ void __launch_bounds__(kMaxThreads) q2k_gemv_kernel(const GemvParams 
           ok = false;
           break;
         }
-        mbar_arrive_expect_tx(&m.full[s], kTileBytes);
-        bulk_copy_g2s(m.ring + (size_t)s * kTileBytes, src + (size_t)i * kTileBytes, kTileBytes, &m.full[s]);
+        const int j = i / nchunks, c = i - j * nchunks;
+        const int nblk = min(kConsumers, nb - c * kConsumers);
+        mbar_arrive_expect_tx(&m.full[s], (unsigned)(nblk * kTileBytes));
+        bulk_copy_g2s(m.ring + (size_t)s * stage_bytes, src + ((size_t)j * nb + (size_t)c * kConsumers) * kTileBytes,
+                      (unsigned)(nblk * kTileBytes), &m.full[s]);
       }
       if (!ok) {
         raise_device_error(p.err, kDevErrTimeout);
@@ -370,14 +377,19 @@ __global__ void __launch_bounds__(kMaxThreads) q2k_gemv_kernel(const GemvParams 
     }
     const int64_t group = g0 + j;
     const int64_t row = group * 32 + lane;
-    for (int b = cw; b < nb; b += kConsumers) {
-      const int i = j * nb + b;
+    for (int c = 0; c < nchunks; ++c) {
+      const int i = j * nchunks + c;
       const int s = i & smask;
+      const int b = c * kConsumers + cw;
       if (!mbar_wait_bounded(&m.full[s], (unsigned)((i >> lgS) & 1), kWaitTimeoutNs)) {
         raise_device_error(p.err, kDevErrTimeout);
         return;
       }
-      const uint8_t* tile = m.ring + (size_t)s * kTileBytes;
+      if (b >= nb) {  // the group's last chunk is short: nothing for this warp
+        mbar_arrive(&m.empty[s]);
+        continue;
+      }
+      const uint8_t* tile = m.ring + (size_t)s * stage_bytes + (size_t)cw * kTileBytes;
       const uint4* t4 = reinterpret_cast<const uint4*>(tile);
       WBlock wb;
       wb.q[0] = t4[0 * 32 + lane];
@@ -456,20 +468,18 @@ struct Plan {
 };
 
 // Launch shape of the GEMV for T tokens, nb super-blocks per row and
-// n_groups 32-row groups (measured on B200, graph-timed, batch 1):
-//   <= 1 CTA per SM of work  : 1 CTA/SM, 16 consumer warps, deep ring
-//   <= ~4 groups per SM      : 3 CTAs/SM, 8 consumer warps
-//   more                     : 4 CTAs/SM, 4 consumer warps
-// More resident warps per SM is what lifts throughput: the integer core is
-// issue-latency bound.  The ring takes the deepest power of two (4..64
-// stages) that fits in the CTA's share of shared memory.  The override
+// n_groups 32-row groups (measured on B200, graph-timed, batch 1): below ~6
+// groups per SM one CTA per SM with 16 consumer warps (a stage is then one
+// 43 KB bulk copy -- large copies keep the TMA engine ahead); above it four
+// CTAs per SM with 8 consumer warps.  The ring takes the deepest power of
+// two that fits in the CTA's share of shared memory (half the SM for one CTA,
+// so the next kernel's CTA can be resident during the tail).  The override
 // SMEAI_GEMV_PLAN="ctas_per_sm,consumers,stages" exists for tuning sweeps.
 Plan plan_for(int T, int nb, int64_t n_groups) {
   const int sms = num_sms();
   Plan pl;
-  if (n_groups <= sms) pl = {1, 16, 0};
-  else if (n_groups <= 4 * sms) pl = {3, 8, 0};
-  else pl = {4, 4, 0};
+  if (n_groups < 6 * sms) pl = {1, 16, 0};
+  else pl = {4, 8, 0};
   static int ov[3] = {-1, -1, -1};
   static bool read = false;
   if (!read) {
@@ -481,15 +491,16 @@ Plan plan_for(int T, int nb, int64_t n_groups) {
   if (ov[1] > 0 && ov[1] <= kMaxConsumers) pl.consumers = ov[1];
   const size_t fixed = smem_fixed_bytes(T, nb);
   const size_t budget = (size_t)kSmemLimit / (size_t)(pl.ctas_per_sm < 2 ? 2 : pl.ctas_per_sm);
-  const int cap = pl.ctas_per_sm == 1 ? 64 : 16;
-  for (int s = cap; s >= 4; s >>= 1)
-    if ((ov[2] <= 0 || s <= ov[2]) && fixed + (size_t)s * (kTileBytes + 16) <= budget) {
+  const size_t stage = (size_t)pl.consumers * kTileBytes + 16;
+  const int cap = pl.ctas_per_sm == 1 ? 16 : 8;
+  for (int s = cap; s >= 2; s >>= 1)
+    if ((ov[2] <= 0 || s <= ov[2]) && fixed + (size_t)s * stage <= budget) {
       pl.stages = s;
       break;
     }
   if (!pl.stages)
-    for (int s = 32; s >= 4; s >>= 1)
-      if (fixed + (size_t)s * (kTileBytes + 16) <= (size_t)kSmemLimit) {
+    for (int s = 8; s >= 2; s >>= 1)
+      if (fixed + (size_t)s * stage <= (size_t)kSmemLimit) {
         pl.stages = s;
         pl.ctas_per_sm = 1;
         break;
@@ -515,7 +526,7 @@ int launch_gemv(const Q2KWeight& w, GemvParams p, cudaStream_t stream) {
     set_last_error("q2k_gemv: device error word unavailable");
     return kCudaError;
   }
-  const size_t smem = smem_total_bytes(T, w.nb, pl.stages);
+  const size_t smem = smem_total_bytes(T, w.nb, pl.stages, pl.consumers);
   static unsigned configured = 0;  // per template instance, one bit per device
   int dev = 0;
   SMEAI_CUDA_TRY(cudaGetDevice(&dev));
