@@ -115,6 +115,48 @@ int smeai_q2k_mul_mat_tc(const void *w_dev, const void *x_q8k_dev, int64_t n_col
 int smeai_q2k_mul_mat_ex(const void *w_dev, const void *x_q8k_dev, int64_t n_cols, float *y_dev, size_t ldy,
                          int epilogue, const float *resid_dev, size_t ld_resid, void *stream);
 
+/* smeai_q2k_mul_mat_ex, then the next linear's input in the same kernel: once
+ * every output row is written, rows [q_row0, q_row0 + q_rows) of each
+ * activation row's result (q_rows a multiple of 256) are quantized to Q8_K
+ * into y_q8k_dev (n_cols rows of q_rows/256 blocks) -- RMS-normalized first
+ * when rms_eps >= 0 -- bit-identical to smeai_rms_q8k_quantize /
+ * smeai_q8k_quantize of that slice.  The last CTA of the grid to finish does
+ * it, so a decode step needs no separate quantizer kernels. */
+int smeai_q2k_mul_mat_chain(const void *w_dev, const void *x_q8k_dev, int64_t n_cols, float *y_dev, size_t ldy,
+                            int epilogue, const float *resid_dev, size_t ld_resid, int64_t q_row0, int64_t q_rows,
+                            float rms_eps, void *y_q8k_dev, void *stream);
+
+/* ---- decode program: a chain of dependent GEMVs as ONE persistent kernel ----
+ * Phase p reads the complete output of phase p-1 (its input buffer is, or
+ * contains, that output); each phase is one smeai_q2k_mul_mat_ex /
+ * smeai_q2k_mul_mat_f32_ex call and gives the same bits.  One CTA per SM
+ * streams every phase's weights back to back while the phases wait on one
+ * another through completion counters in device memory, so a decode step is
+ * one launch instead of one per linear (ggml's graph of MUL_MAT nodes over a
+ * layer stack, run as a single kernel).  n_cols (tokens) is 1, 2, 4 or 8.
+ * The launch is cooperative; a run that hits a bounded-wait timeout (never
+ * expected; reported by smeai_take_device_error) needs
+ * smeai_q2k_program_reset before the next run. */
+#define SMEAI_IN_Q8K 0     /* x: contiguous Q8_K rows */
+#define SMEAI_IN_F32 1     /* x: fp32 rows (stride ld_x), quantized to Q8_K in the kernel */
+#define SMEAI_IN_F32_RMS 2 /* the same after an RMSNorm of each row (rms_eps) */
+typedef struct smeai_q2k_phase {
+  const void *w;       /* handle from smeai_q2k_repack */
+  int input;           /* SMEAI_IN_* */
+  const void *x;
+  size_t ld_x;
+  float *y;
+  size_t ldy;
+  int epilogue;        /* SMEAI_EPI_* */
+  const float *resid;  /* SMEAI_EPI_RESIDUAL; may alias y */
+  size_t ld_resid;
+} smeai_q2k_phase;
+int smeai_q2k_program_create(const smeai_q2k_phase *phases, int n_phases, int64_t n_cols, float rms_eps,
+                             void **prog_out);
+int smeai_q2k_program_run(void *prog, void *stream);
+int smeai_q2k_program_reset(void *prog, void *stream);
+void smeai_q2k_program_free(void *prog);
+
 /* fp32 activations in, fp32 out: each CTA quantizes the activation rows to
  * Q8_K in its prologue (bit-identical to smeai_q8k_quantize), then runs the
  * GEMV -- one kernel, no intermediate buffer.  x: n_cols rows of k floats. */

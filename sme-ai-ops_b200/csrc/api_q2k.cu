@@ -4,6 +4,7 @@
 #include <map>
 #include <mutex>
 #include <utility>
+#include <vector>
 
 #include "common.cuh"
 #include "kernels.h"
@@ -249,6 +250,62 @@ int smeai_q2k_mul_mat_ex(const void* w_dev, const void* x_q8k_dev, int64_t n_col
   return q2k_gemv(h->w, x_q8k_dev, n_cols, y_dev, (int64_t)ldy, epilogue, resid_dev, (int64_t)ld_resid,
                   as_stream(stream));
 }
+
+int smeai_q2k_mul_mat_chain(const void* w_dev, const void* x_q8k_dev, int64_t n_cols, float* y_dev, size_t ldy,
+                            int epilogue, const float* resid_dev, size_t ld_resid, int64_t q_row0, int64_t q_rows,
+                            float rms_eps, void* y_q8k_dev, void* stream) {
+  const Handle* h = as_handle(w_dev);
+  if (!h) return kBadArgument;
+  if (!y_q8k_dev) {
+    set_last_error("smeai_q2k_mul_mat_chain: NULL Q8_K output");
+    return kBadArgument;
+  }
+  Q8KChain chain;
+  chain.q8 = y_q8k_dev;
+  chain.row0 = q_row0;
+  chain.rows = q_rows;
+  chain.rms_eps = rms_eps;
+  return q2k_gemv_any(h->w, kInQ8K, x_q8k_dev, 0, 0.f, n_cols, y_dev, (int64_t)ldy, epilogue, resid_dev,
+                      (int64_t)ld_resid, as_stream(stream), &chain);
+}
+
+int smeai_q2k_program_create(const smeai_q2k_phase* phases, int n_phases, int64_t n_cols, float rms_eps,
+                             void** prog_out) {
+  if (!phases || !prog_out || n_phases <= 0 || n_cols <= 0 || n_cols > 8) {
+    set_last_error("smeai_q2k_program_create: bad arguments");
+    return kBadArgument;
+  }
+  *prog_out = nullptr;
+  std::vector<ProgPhase> ph((size_t)n_phases);
+  for (int p = 0; p < n_phases; ++p) {
+    const Handle* h = as_handle(phases[p].w);
+    if (!h) return kBadArgument;
+    ProgPhase& d = ph[(size_t)p];
+    d.w = &h->w;
+    d.in_mode = phases[p].input;
+    d.x = phases[p].x;
+    d.ld_x = (int64_t)phases[p].ld_x;
+    d.y = phases[p].y;
+    d.ldy = (int64_t)phases[p].ldy;
+    d.epi = phases[p].epilogue;
+    d.resid = phases[p].resid;
+    d.ld_resid = (int64_t)phases[p].ld_resid;
+  }
+  Q2KProgram* pr = nullptr;
+  const int st = q2k_program_create(ph.data(), n_phases, (int)n_cols, rms_eps, &pr);
+  if (st == kOk) *prog_out = pr;
+  return st;
+}
+
+int smeai_q2k_program_run(void* prog, void* stream) {
+  return q2k_program_run(static_cast<Q2KProgram*>(prog), as_stream(stream));
+}
+
+int smeai_q2k_program_reset(void* prog, void* stream) {
+  return q2k_program_reset(static_cast<Q2KProgram*>(prog), as_stream(stream));
+}
+
+void smeai_q2k_program_free(void* prog) { q2k_program_free(static_cast<Q2KProgram*>(prog)); }
 
 int smeai_q2k_mul_mat_f32(const void* w_dev, const float* x_dev, int64_t n_cols, float* y_dev, size_t ldy,
                           void* stream) {

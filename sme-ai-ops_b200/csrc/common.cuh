@@ -131,6 +131,16 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, unsigned by
 __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
 }
+// One arrival for the whole warp (barriers initialised with a count of warps):
+// the lanes meet at __syncwarp, which orders their earlier shared-memory
+// accesses before lane 0's release arrive.  `dep` must be computed from every
+// register the lanes loaded from the guarded buffer, so those loads have
+// completed when the warp arrives (use 0 when nothing was loaded).
+__device__ __forceinline__ void mbar_arrive_warp(uint64_t* bar, unsigned dep = 0u) {
+  asm volatile("" ::"r"(dep));
+  __syncwarp();
+  if ((threadIdx.x & 31) == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, unsigned parity) {
   uint32_t ok;
   asm volatile(
@@ -176,6 +186,9 @@ enum DeviceError : unsigned { kDevErrTimeout = 1u };
 __device__ __forceinline__ void raise_device_error(unsigned* err, unsigned code) { atomicOr(err, code); }
 unsigned* device_error_ptr();
 int device_error_take(unsigned* code);
+// Zero-initialised grid-completion counter of the GEMV's chained Q8_K output
+// for this (device, stream); device_error_take() resets all of them.
+unsigned* chain_counter(cudaStream_t stream);
 
 __device__ __forceinline__ void pdl_wait() {
   asm volatile("griddepcontrol.wait;" ::: "memory");

@@ -50,12 +50,47 @@ enum Epilogue : int {
 // rows quantized to Q8_K in the kernel's prologue, optionally after an RMSNorm.
 enum InMode : int { kInQ8K = 0, kInF32 = 1, kInF32Rms = 2 };
 
+// Chained output quantization: after the GEMV's last row is written, output
+// rows [row0, row0 + rows) of every token (rows a multiple of 256) are
+// quantized to Q8_K -- RMS-normalized first when rms_eps >= 0 -- into q8
+// (n_cols rows of rows/256 blocks), bit-identical to q8k_quantize /
+// rms_q8k_quantize of that slice.  The last CTA of the grid does it.
+struct Q8KChain {
+  void* q8 = nullptr;
+  int64_t row0 = 0;
+  int64_t rows = 0;
+  float rms_eps = -1.f;
+};
+
 int q2k_gemv_any(const Q2KWeight& w, int in_mode, const void* x, int64_t ld_x, float eps, int64_t n_cols,
-                 float* y, int64_t ldy, int epilogue, const float* resid, int64_t ld_resid, cudaStream_t stream);
+                 float* y, int64_t ldy, int epilogue, const float* resid, int64_t ld_resid, cudaStream_t stream,
+                 const Q8KChain* chain = nullptr);
 
 // y = W x for n_cols Q8_K activation rows (ggml layout, contiguous rows).
 int q2k_gemv(const Q2KWeight& w, const void* xq, int64_t n_cols, float* y, int64_t ldy, int epilogue,
              const float* resid, int64_t ld_resid, cudaStream_t stream);
+
+// A decode step as one persistent cooperative kernel (q2k_program.cu): the
+// phases run in order, phase p reading the complete output of phase p-1;
+// every output is bit-identical to running the phases as separate q2k_gemv_any
+// launches (same input modes, epilogues and quantizers).
+struct ProgPhase {
+  const Q2KWeight* w = nullptr;
+  int in_mode = kInQ8K;        // kInQ8K: x = contiguous Q8_K rows; kInF32 / kInF32Rms: fp32 rows
+  const void* x = nullptr;
+  int64_t ld_x = 0;            // fp32 row stride (floats)
+  float* y = nullptr;
+  int64_t ldy = 0;
+  int epi = kEpiStore;
+  const float* resid = nullptr;
+  int64_t ld_resid = 0;
+};
+struct Q2KProgram;
+int q2k_program_create(const ProgPhase* phases, int n_phases, int n_cols, float rms_eps, Q2KProgram** out);
+int q2k_program_run(Q2KProgram* prog, cudaStream_t stream);
+int q2k_program_reset(Q2KProgram* prog, cudaStream_t stream);
+void q2k_program_free(Q2KProgram* prog);
+void q2k_program_shape(const Q2KProgram* prog, int* grid, int* consumers, int* stages, size_t* smem);
 
 // Tensor-core GEMM for many activation rows (prefill): y = W x for n_cols
 // Q8_K rows, store epilogue, bit-identical to q2k_gemv.  Needs a 256-byte

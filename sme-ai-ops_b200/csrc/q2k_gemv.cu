@@ -33,6 +33,7 @@
 #include "common.cuh"
 #include "kernels.h"
 #include "q8k_device.cuh"
+#include "q2k_core.cuh"
 
 #include <stdio.h>
 #include <stdlib.h>
@@ -41,15 +42,9 @@ namespace smeai {
 
 namespace {
 
-struct WBlock {
-  uint4 q[4];
-  uint4 s;
-  unsigned dm;
-};
 
 constexpr int kMaxConsumers = 16;
 constexpr int kMaxThreads = (kMaxConsumers + 1) * 32;
-constexpr int kMaxStages = 64;
 constexpr uint64_t kWaitTimeoutNs = 2000000000ull;  // 2 s
 
 struct GemvParams {
@@ -69,6 +64,16 @@ struct GemvParams {
   unsigned* err;
   int stages;        // ring depth (a power of two)
   int log2_stages;
+  // chained quantization: when chain_q8 is set, the grid's last CTA to finish
+  // quantizes output rows [chain_row0, chain_row0 + 256 * chain_nb) of every
+  // token to Q8_K blocks at chain_q8 (RMS-normalized first when chain_rms),
+  // so the next linear's input is ready when this kernel completes
+  uint8_t* chain_q8;
+  int64_t chain_row0;
+  int chain_nb;
+  int chain_rms;
+  float chain_eps;
+  unsigned* chain_ctr;  // zero between launches; the last CTA resets it
 };
 
 // Shared-memory carve-up for T tokens (16-byte aligned pieces).
@@ -84,13 +89,17 @@ struct Smem {
   uint64_t* grp;   // [2] all consumer lanes finished a row group
   uint64_t* tfree; // [2] the finisher has consumed the terms buffer
   uint64_t* rms;   // [2] block sums written / 1/rms ready
+  uint64_t* done;  // all consumer lanes finished their row groups
+  uint64_t* verdict;  // the completion count has been taken
+  uint64_t* fin;   // [2] chained RMS: block sums written / 1/rms ready
+  unsigned* last;  // this CTA finished last
 };
 
 __host__ __device__ __forceinline__ size_t align16(size_t v) { return (v + 15) & ~(size_t)15; }
 
 __host__ __device__ __forceinline__ size_t smem_fixed_bytes(int T, int nb) {
   return align16((size_t)T * nb * 256) + align16((size_t)T * nb * 32) + align16((size_t)T * nb * 4) +
-         align16((size_t)T * (nb + 1) * 4) + align16((size_t)2 * T * nb * 128) + 8 * 6;
+         align16((size_t)T * (nb + 1) * 4) + align16((size_t)2 * T * nb * 128) + 8 * 11 + 8;
 }
 __host__ __device__ __forceinline__ size_t smem_total_bytes(int T, int nb, int stages, int consumers) {
   return (size_t)stages * consumers * kTileBytes + smem_fixed_bytes(T, nb) + (size_t)stages * 16;
@@ -116,82 +125,11 @@ __device__ __forceinline__ Smem carve(uint8_t* base, int T, int nb, int stages, 
   m.grp = m.empty + stages;
   m.tfree = m.grp + 2;
   m.rms = m.tfree + 2;
+  m.done = m.rms + 2;
+  m.verdict = m.done + 1;
+  m.fin = m.verdict + 1;
+  m.last = reinterpret_cast<unsigned*>(m.fin + 2);
   return m;
-}
-
-__device__ __forceinline__ void store_q8k_smem(const Q8KLane& r, const Smem& m, int slot) {
-  const int lane = threadIdx.x & 31;
-  uint32_t* q = reinterpret_cast<uint32_t*>(m.qs) + (size_t)slot * 64;
-  q[2 * lane] = r.w0;
-  q[2 * lane + 1] = r.w1;
-  if ((lane & 3) == 0) m.bs[slot * 8 + (lane >> 2)] = (int)r.bsum_pair;
-  if (lane == 0) m.d[slot] = r.d;
-}
-
-// Integer core + float term of super-block b for this lane's row.
-template <int T, bool SUMS>
-__device__ __forceinline__ void block_terms(const WBlock& wb, const Smem& m, int nb, int b, float* terms,
-                                            int lane, int64_t row, int64_t n_rows, int32_t* isum_out,
-                                            int32_t* summs_out) {
-  const unsigned sl[4] = {wb.s.x & 0x0F0F0F0Fu, wb.s.y & 0x0F0F0F0Fu, wb.s.z & 0x0F0F0F0Fu, wb.s.w & 0x0F0F0F0Fu};
-  const unsigned mh[4] = {(wb.s.x >> 4) & 0x0F0F0F0Fu, (wb.s.y >> 4) & 0x0F0F0F0Fu, (wb.s.z >> 4) & 0x0F0F0F0Fu,
-                          (wb.s.w >> 4) & 0x0F0F0F0Fu};
-  int plane[T][4];
-#pragma unroll
-  for (int t = 0; t < T; ++t)
-#pragma unroll
-    for (int s = 0; s < 4; ++s) plane[t][s] = 0;
-#pragma unroll
-  for (int c = 0; c < 4; ++c) {
-    const unsigned q0 = wb.q[c].x, q1 = wb.q[c].y, q2 = wb.q[c].z, q3 = wb.q[c].w;
-    const int h = c >> 1, hf = c & 1;
-#pragma unroll
-    for (int s = 0; s < 4; ++s) {
-      const unsigned mask = 0x03030303u << (2 * s);
-      const unsigned m0 = q0 & mask, m1 = q1 & mask, m2 = q2 & mask, m3 = q3 & mask;
-      const int j = 8 * h + 2 * s + hf;  // sub-block of these 16 quants
-      const int sc = (int)__byte_perm(sl[j >> 2], 0u, 0x4440u | (unsigned)(j & 3));
-      const int chunk = h * 8 + s * 2 + hf;  // 16-byte activation chunk within the block
-#pragma unroll
-      for (int t = 0; t < T; ++t) {
-        const int4 av = m.qs[(t * nb + b) * 16 + chunk];
-        int acc = dp4a_us(m0, av.x, 0);
-        acc = dp4a_us(m1, av.y, acc);
-        acc = dp4a_us(m2, av.z, acc);
-        acc = dp4a_us(m3, av.w, acc);
-        plane[t][s] += sc * acc;
-      }
-    }
-  }
-  const float dw = __half2float(__ushort_as_half((unsigned short)(wb.dm & 0xffffu)));
-  const float dmw = __half2float(__ushort_as_half((unsigned short)(wb.dm >> 16)));
-#pragma unroll
-  for (int t = 0; t < T; ++t) {
-    const int isum = plane[t][0] + (plane[t][1] >> 2) + (plane[t][2] >> 4) + (plane[t][3] >> 6);
-    const int* bsp = m.bs + (t * nb + b) * 8;
-    const int4 bs0 = *reinterpret_cast<const int4*>(bsp);
-    const int4 bs1 = *reinterpret_cast<const int4*>(bsp + 4);
-    int mm = dp2a_lo_su(bs0.x, mh[0], 0);
-    mm = dp2a_hi_su(bs0.y, mh[0], mm);
-    mm = dp2a_lo_su(bs0.z, mh[1], mm);
-    mm = dp2a_hi_su(bs0.w, mh[1], mm);
-    mm = dp2a_lo_su(bs1.x, mh[2], mm);
-    mm = dp2a_hi_su(bs1.y, mh[2], mm);
-    mm = dp2a_lo_su(bs1.z, mh[3], mm);
-    mm = dp2a_hi_su(bs1.w, mh[3], mm);
-    if constexpr (SUMS) {
-      if (row < n_rows) {
-        isum_out[row * nb + b] = isum;
-        summs_out[row * nb + b] = mm;
-      }
-    } else {
-      const float dx = m.d[t * nb + b];
-      const float dall = __fmul_rn(dx, dw);
-      const float dmn = __fmul_rn(dx, dmw);
-      terms[(t * nb + b) * 32 + lane] =
-          __fmaf_rn(dall, __int2float_rn(isum), -__fmul_rn(dmn, __int2float_rn(mm)));
-    }
-  }
 }
 
 // Ordered sum over super-blocks of one row group, then the epilogue.
@@ -238,6 +176,81 @@ __device__ __forceinline__ void finish_group(const float* terms, int nb, int64_t
   }
 }
 
+// Chained quantization (consumer warps, after the main loop).  Every lane
+// fences its output stores; the CTA's completion is counted once all its
+// lanes have arrived; the CTA that brings the count to gridDim.x owns the
+// whole output and quantizes the slice exactly as rms_q8k_quantize_kernel /
+// q8k_quantize_kernel would (same helpers, same summation order).
+template <int T>
+__device__ __forceinline__ void chain_quantize(const Smem& m, const GemvParams& p, int cw, int W, int lane) {
+  __threadfence();
+  mbar_arrive_warp(m.done);
+  if (cw == 0) {
+    const bool ok = mbar_wait_bounded(m.done, 0, kWaitTimeoutNs);
+    if (lane == 0) {
+      unsigned last = 0;
+      if (ok) {
+        const unsigned old = atomicAdd(p.chain_ctr, 1u);
+        last = old == gridDim.x - 1 ? 1u : 0u;
+        if (last) atomicExch(p.chain_ctr, 0u);
+      } else {
+        raise_device_error(p.err, kDevErrTimeout);
+      }
+      *m.last = last;
+    }
+    __syncwarp();
+    mbar_arrive_warp(m.verdict);
+  }
+  if (!mbar_wait_bounded(m.verdict, 0, kWaitTimeoutNs)) {
+    raise_device_error(p.err, kDevErrTimeout);
+    return;
+  }
+  if (!*m.last) return;
+  __threadfence();
+  const int cnb = p.chain_nb, nq = T * cnb;
+  const float* ysl = p.y + p.chain_row0;
+  float* rs = m.terms;  // [T][cnb + 1]; the terms are consumed by now
+  if (p.chain_rms) {
+    for (int i = cw; i < nq; i += W) {
+      const int t = i / cnb, b = i - t * cnb;
+      float v[8];
+      load8_cg(ysl + t * p.ldy + b * QK_K + lane * 8, v);
+      const float s = block_sumsq_warp(v);
+      if (lane == 0) rs[t * (cnb + 1) + b] = s;
+    }
+    mbar_arrive_warp(&m.fin[0]);
+    if (cw == 0) {
+      if (!mbar_wait_bounded(&m.fin[0], 0, kWaitTimeoutNs)) {
+        raise_device_error(p.err, kDevErrTimeout);
+        return;
+      }
+      if (lane < T) {
+        float* r = rs + lane * (cnb + 1);
+        float total = 0.f;
+        for (int b = 0; b < cnb; ++b) total = __fadd_rn(total, r[b]);
+        r[cnb] = rms_inv_from_sum(total, cnb * QK_K, p.chain_eps);
+      }
+      __syncwarp();
+      mbar_arrive_warp(&m.fin[1]);
+    }
+    if (!mbar_wait_bounded(&m.fin[1], 0, kWaitTimeoutNs)) {
+      raise_device_error(p.err, kDevErrTimeout);
+      return;
+    }
+  }
+  for (int i = cw; i < nq; i += W) {
+    const int t = i / cnb, b = i - t * cnb;
+    float v[8];
+    load8_cg(ysl + t * p.ldy + b * QK_K + lane * 8, v);
+    if (p.chain_rms) {
+      const float inv = rs[t * (cnb + 1) + cnb];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) v[k] = __fmul_rn(v[k], inv);
+    }
+    q8k_store_global(q8k_quantize_lane(v), p.chain_q8 + (int64_t)i * Q8K_BLOCK_BYTES);
+  }
+}
+
 template <int T, int EPI, int IN, bool SUMS>
 __global__ void __launch_bounds__(kMaxThreads) q2k_gemv_kernel(const GemvParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
@@ -253,18 +266,23 @@ __global__ void __launch_bounds__(kMaxThreads) q2k_gemv_kernel(const GemvParams 
   const int n_stages = ng * nchunks;
   const int stage_bytes = kConsumers * kTileBytes;
   const Smem m = carve(smem, T, nb, S, kConsumers);
+  const ActSmem act = {m.qs, m.bs, m.d};
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
       mbar_init(&m.full[s], 1);
-      mbar_init(&m.empty[s], kConsumers * 32);
+      mbar_init(&m.empty[s], kConsumers);
     }
-    mbar_init(&m.grp[0], kConsumers * 32);
-    mbar_init(&m.grp[1], kConsumers * 32);
-    mbar_init(&m.tfree[0], 32);
-    mbar_init(&m.tfree[1], 32);
-    mbar_init(&m.rms[0], kConsumers * 32);
-    mbar_init(&m.rms[1], 32);
+    mbar_init(&m.grp[0], kConsumers);
+    mbar_init(&m.grp[1], kConsumers);
+    mbar_init(&m.tfree[0], 1);
+    mbar_init(&m.tfree[1], 1);
+    mbar_init(&m.rms[0], kConsumers);
+    mbar_init(&m.rms[1], 1);
+    mbar_init(m.done, kConsumers);
+    mbar_init(m.verdict, 1);
+    mbar_init(&m.fin[0], kConsumers);
+    mbar_init(&m.fin[1], 1);
     mbar_fence_init();
   }
   __syncthreads();
@@ -306,21 +324,8 @@ __global__ void __launch_bounds__(kMaxThreads) q2k_gemv_kernel(const GemvParams 
     const uint32_t* src = static_cast<const uint32_t*>(p.x);
     for (int b = cw; b < nb; b += kConsumers) {
 #pragma unroll 1
-      for (int t = 0; t < T; ++t) {
-        const uint32_t* blk = src + ((int64_t)t * nb + b) * Q8K_BLOCK_WORDS;
-        const int slot = t * nb + b;
-        const uint32_t w0 = blk[lane], w1 = blk[lane + 32];
-        const uint32_t w2 = lane + 64 < Q8K_BLOCK_WORDS ? blk[lane + 64] : 0u;
-        uint32_t* q = reinterpret_cast<uint32_t*>(m.qs) + (size_t)slot * 64;
-        // words: 0 = d, 1..64 = qs, 65..72 = bsums
-        if (lane == 0) m.d[slot] = __uint_as_float(w0);
-        else q[lane - 1] = w0;
-        q[lane + 31] = w1;
-        if (lane + 64 < Q8K_BLOCK_WORDS) {
-          if (lane == 0) q[63] = w2;
-          else m.bs[slot * 8 + (lane - 1)] = (int)w2;
-        }
-      }
+      for (int t = 0; t < T; ++t)
+        copy_q8k_smem(src + ((int64_t)t * nb + b) * Q8K_BLOCK_WORDS, act, t * nb + b, lane);
     }
   } else {
     const float* x = static_cast<const float*>(p.x);
@@ -332,7 +337,7 @@ __global__ void __launch_bounds__(kMaxThreads) q2k_gemv_kernel(const GemvParams 
         const float s = block_sumsq_warp(v);
         if (lane == 0) m.rsum[t * (nb + 1) + b] = s;
       }
-      mbar_arrive(&m.rms[0]);
+      mbar_arrive_warp(&m.rms[0]);
       if (cw == 0) {
         if (!mbar_wait_bounded(&m.rms[0], 0, kWaitTimeoutNs)) {
           raise_device_error(p.err, kDevErrTimeout);
@@ -344,7 +349,7 @@ __global__ void __launch_bounds__(kMaxThreads) q2k_gemv_kernel(const GemvParams 
           for (int b = 0; b < nb; ++b) total = __fadd_rn(total, rs[b]);
           rs[nb] = rms_inv_from_sum(total, nb * QK_K, p.eps);
         }
-        mbar_arrive(&m.rms[1]);
+        mbar_arrive_warp(&m.rms[1]);
       }
       if (!mbar_wait_bounded(&m.rms[1], 0, kWaitTimeoutNs)) {
         raise_device_error(p.err, kDevErrTimeout);
@@ -361,7 +366,7 @@ __global__ void __launch_bounds__(kMaxThreads) q2k_gemv_kernel(const GemvParams 
 #pragma unroll
           for (int k = 0; k < 8; ++k) v[k] = __fmul_rn(v[k], inv);
         }
-        store_q8k_smem(q8k_quantize_lane(v), m, t * nb + b);
+        store_q8k_smem(q8k_quantize_lane(v), act, t * nb + b);
       }
     }
   }
@@ -386,32 +391,28 @@ __global__ void __launch_bounds__(kMaxThreads) q2k_gemv_kernel(const GemvParams 
         return;
       }
       if (b >= nb) {  // the group's last chunk is short: nothing for this warp
-        mbar_arrive(&m.empty[s]);
+        mbar_arrive_warp(&m.empty[s]);
         continue;
       }
       const uint8_t* tile = m.ring + (size_t)s * stage_bytes + (size_t)cw * kTileBytes;
-      const uint4* t4 = reinterpret_cast<const uint4*>(tile);
-      WBlock wb;
-      wb.q[0] = t4[0 * 32 + lane];
-      wb.q[1] = t4[1 * 32 + lane];
-      wb.q[2] = t4[2 * 32 + lane];
-      wb.q[3] = t4[3 * 32 + lane];
-      wb.s = t4[4 * 32 + lane];
-      wb.dm = reinterpret_cast<const unsigned*>(tile + 5 * 512)[lane];
-      mbar_arrive(&m.empty[s]);
-      block_terms<T, SUMS>(wb, m, nb, b, terms, lane, row, p.n_rows, p.isum_out, p.summs_out);
+      const WBlock wb = load_wblock(tile, lane);
+      mbar_arrive_warp(&m.empty[s], wblock_dep(wb));
+      block_terms<T, SUMS>(wb, act, nb, b, terms, lane, row, p.n_rows, p.isum_out, p.summs_out);
     }
     if constexpr (!SUMS) {
-      mbar_arrive(&m.grp[buf]);
+      mbar_arrive_warp(&m.grp[buf]);
       if (cw == (j % kConsumers)) {
         if (!mbar_wait_bounded(&m.grp[buf], (unsigned)((j >> 1) & 1), kWaitTimeoutNs)) {
           raise_device_error(p.err, kDevErrTimeout);
           return;
         }
         finish_group<T, EPI>(terms, nb, group, lane, p);
-        mbar_arrive(&m.tfree[buf]);
+        mbar_arrive_warp(&m.tfree[buf]);
       }
     }
+  }
+  if constexpr (!SUMS) {
+    if (p.chain_q8) chain_quantize<T>(m, p, cw, kConsumers, lane);
   }
 }
 
@@ -613,7 +614,8 @@ int q2k_repack(const void* w_blocks_dev, int64_t n_rows, int64_t k, Q2KWeight* o
 }
 
 int q2k_gemv_any(const Q2KWeight& w, int in_mode, const void* x, int64_t ld_x, float eps, int64_t n_cols,
-                 float* y, int64_t ldy, int epilogue, const float* resid, int64_t ld_resid, cudaStream_t stream) {
+                 float* y, int64_t ldy, int epilogue, const float* resid, int64_t ld_resid, cudaStream_t stream,
+                 const Q8KChain* chain) {
   if (!w.tiles || !x || !y || n_cols <= 0) {
     set_last_error("q2k_gemv: bad arguments");
     return kBadArgument;
@@ -639,6 +641,24 @@ int q2k_gemv_any(const Q2KWeight& w, int in_mode, const void* x, int64_t ld_x, f
     set_last_error("q2k_gemv: leading dimension smaller than the output rows");
     return kBadArgument;
   }
+  unsigned* ctr = nullptr;
+  int cnb = 0;
+  if (chain && chain->q8) {
+    if (chain->rows <= 0 || chain->rows % QK_K || chain->row0 < 0 || chain->row0 + chain->rows > out_rows ||
+        (reinterpret_cast<uintptr_t>(chain->q8) & 3)) {
+      set_last_error("q2k_gemv: chained quantization needs a slice of the output whose length is a multiple "
+                     "of 256 and a 4-byte aligned Q8_K buffer");
+      return kBadArgument;
+    }
+    cnb = (int)(chain->rows / QK_K);
+    if (cnb + 1 > 64 * w.nb) {  // the RMS block sums reuse the terms buffer
+      set_last_error("q2k_gemv: chained slice of %lld rows too long for k=%lld", (long long)chain->rows,
+                     (long long)w.k);
+      return kBadArgument;
+    }
+    ctr = chain_counter(stream);
+    if (!ctr) return kCudaError;
+  }
   for (int64_t c0 = 0; c0 < n_cols;) {
     const int64_t rem = n_cols - c0;
     int T = rem >= 8 ? 8 : (rem >= 4 ? 4 : (rem >= 2 ? 2 : 1));
@@ -656,6 +676,14 @@ int q2k_gemv_any(const Q2KWeight& w, int in_mode, const void* x, int64_t ld_x, f
     p.ldy = ldy;
     p.resid = resid ? resid + c0 * ld_resid : nullptr;
     p.ld_resid = ld_resid;
+    if (ctr) {
+      p.chain_q8 = static_cast<uint8_t*>(chain->q8) + c0 * (int64_t)cnb * Q8K_BLOCK_BYTES;
+      p.chain_row0 = chain->row0;
+      p.chain_nb = cnb;
+      p.chain_rms = chain->rms_eps >= 0.f ? 1 : 0;
+      p.chain_eps = chain->rms_eps;
+      p.chain_ctr = ctr;
+    }
     int st;
     switch (in_mode) {
       case kInQ8K: st = dispatch_epi<kInQ8K>(epilogue, T, w, p, stream); break;

@@ -103,4 +103,18 @@ __device__ __forceinline__ void load8(const float* p, float (&v)[8]) {
   }
 }
 
+// load8 through L2 only (ld.global.cg): for data other CTAs of the running
+// grid wrote, which this SM's L1 may hold stale.
+__device__ __forceinline__ void load8_cg(const float* p, float (&v)[8]) {
+  if ((reinterpret_cast<uintptr_t>(p) & 15) == 0) {
+    const float4 a = __ldcg(reinterpret_cast<const float4*>(p));
+    const float4 b = __ldcg(reinterpret_cast<const float4*>(p + 4));
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+    v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+  } else {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] = __ldcg(p + i);
+  }
+}
+
 }  // namespace smeai

@@ -48,6 +48,16 @@ class PackedWeight(ctypes.Structure):
                 ("k_pad", ctypes.c_uint64), ("n_pad", ctypes.c_uint64), ("packed_weight", ctypes.c_void_p)]
 
 
+IN_Q8K, IN_F32, IN_F32_RMS = 0, 1, 2
+
+
+class Q2KPhase(ctypes.Structure):
+    """smeai_q2k_phase: one GEMV of a decode program."""
+    _fields_ = [("w", ctypes.c_void_p), ("input", ctypes.c_int), ("x", ctypes.c_void_p),
+                ("ld_x", ctypes.c_size_t), ("y", ctypes.c_void_p), ("ldy", ctypes.c_size_t),
+                ("epilogue", ctypes.c_int), ("resid", ctypes.c_void_p), ("ld_resid", ctypes.c_size_t)]
+
+
 def _declare(L: ctypes.CDLL) -> None:
     P, U64, I64, I, F, SZ = (ctypes.c_void_p, ctypes.c_uint64, ctypes.c_int64, ctypes.c_int,
                              ctypes.c_float, ctypes.c_size_t)
@@ -68,10 +78,15 @@ def _declare(L: ctypes.CDLL) -> None:
         "smeai_rms_q8k_quantize": (I, [P, I64, I64, I64, F, P, P]),
         "smeai_q2k_mul_mat": (I, [P, I64, I64, P, I64, P, SZ, P]),
         "smeai_q2k_mul_mat_ex": (I, [P, P, I64, P, SZ, I, P, SZ, P]),
+        "smeai_q2k_mul_mat_chain": (I, [P, P, I64, P, SZ, I, P, SZ, I64, I64, F, P, P]),
         "smeai_q2k_mul_mat_tc": (I, [P, P, I64, P, SZ, P]),
         "smeai_q2k_mul_mat_f32": (I, [P, P, I64, P, SZ, P]),
         "smeai_q2k_mul_mat_f32_ex": (I, [P, P, SZ, I64, P, SZ, I, P, SZ, F, P]),
         "smeai_q2k_block_sums": (I, [P, P, P, P, P]),
+        "smeai_q2k_program_create": (I, [ctypes.POINTER(Q2KPhase), I, I64, F, ctypes.POINTER(ctypes.c_void_p)]),
+        "smeai_q2k_program_run": (I, [P, P]),
+        "smeai_q2k_program_reset": (I, [P, P]),
+        "smeai_q2k_program_free": (None, [P]),
         "smeai_q2k_quantize_device": (I, [P, I64, P, P]),
         "smeai_q2k_dequantize_device": (I, [P, I64, P, P]),
         # sme_ai_ops.h

@@ -96,6 +96,22 @@ class Q2KMatrix:
         check(st, "q2k_mul_mat")
         return out
 
+    def mul_mat_chain(self, xq: torch.Tensor, n_cols: int, out: torch.Tensor, q_out: torch.Tensor,
+                      q_row0: int = 0, q_rows: int | None = None, epilogue: int = EPI_STORE,
+                      resid: torch.Tensor | None = None, rms_eps: float | None = None) -> torch.Tensor:
+        """mul_mat with the result's rows [q_row0, q_row0 + q_rows) quantized to
+        Q8_K into q_out by the same kernel (RMS-normalized first when rms_eps is
+        given) -- the next linear's input."""
+        out_rows = self.n_rows // 2 if epilogue == EPI_SILU_MUL else self.n_rows
+        q_rows = out_rows - q_row0 if q_rows is None else q_rows
+        ldy = out.stride(0) if out.dim() == 2 else out_rows
+        ldr = 0 if resid is None else (resid.stride(0) if resid.dim() == 2 else out_rows)
+        eps = -1.0 if rms_eps is None else float(rms_eps)
+        check(lib().smeai_q2k_mul_mat_chain(self.handle, _ptr(xq), n_cols, _ptr(out), ldy, epilogue, _ptr(resid),
+                                            ldr, q_row0, q_rows, ctypes.c_float(eps), _ptr(q_out), cur_stream()),
+              "q2k_mul_mat_chain")
+        return out
+
     def mul_mat_tc(self, xq: torch.Tensor, n_cols: int, out: torch.Tensor | None = None) -> torch.Tensor:
         """The tensor-core GEMM path (any number of activation rows)."""
         if out is None:
@@ -152,3 +168,54 @@ class Q2KMatrix:
 
 __all__ = ["quantize_q8k", "rms_quantize_q8k", "quantize_q2k", "dequantize_q2k", "Q2KMatrix", "as_bytes",
            "EPI_STORE", "EPI_RESIDUAL", "EPI_SILU_MUL"]
+
+
+class Q2KProgram:
+    """A chain of GEMV phases run as one persistent kernel
+    (smeai_q2k_program_*).  phases: dicts with keys w (Q2KMatrix), x (tensor),
+    input (IN_Q8K / IN_F32 / IN_F32_RMS), y (tensor), epilogue, resid.  Phase p
+    must read phase p-1's complete output.  The tensors must stay alive (and
+    in place) while the program exists."""
+
+    def __init__(self, phases, n_cols: int, rms_eps: float = 1e-5):
+        from . import Q2KPhase, IN_Q8K
+        arr = (Q2KPhase * len(phases))()
+        self._keep = []
+        for i, ph in enumerate(phases):
+            w, x, y = ph["w"], ph["x"], ph["y"]
+            epi = ph.get("epilogue", EPI_STORE)
+            resid = ph.get("resid")
+            mode = ph.get("input", IN_Q8K)
+            out_rows = w.n_rows // 2 if epi == EPI_SILU_MUL else w.n_rows
+            arr[i].w = w.handle
+            arr[i].input = mode
+            arr[i].x = x.data_ptr()
+            arr[i].ld_x = 0 if mode == IN_Q8K else (x.stride(0) if x.dim() == 2 else w.k)
+            arr[i].y = y.data_ptr()
+            arr[i].ldy = y.stride(0) if y.dim() == 2 else out_rows
+            arr[i].epilogue = epi
+            arr[i].resid = 0 if resid is None else resid.data_ptr()
+            arr[i].ld_resid = 0 if resid is None else (resid.stride(0) if resid.dim() == 2 else out_rows)
+            self._keep += [w, x, y, resid]
+        h = ctypes.c_void_p()
+        check(lib().smeai_q2k_program_create(arr, len(phases), n_cols, ctypes.c_float(rms_eps), ctypes.byref(h)),
+              "q2k_program_create")
+        self.handle = h
+        self.n_phases = len(phases)
+
+    def run(self):
+        check(lib().smeai_q2k_program_run(self.handle, cur_stream()), "q2k_program_run")
+
+    def reset(self):
+        check(lib().smeai_q2k_program_reset(self.handle, cur_stream()), "q2k_program_reset")
+
+    def free(self):
+        if getattr(self, "handle", None) and self.handle.value:
+            lib().smeai_q2k_program_free(self.handle)
+            self.handle = ctypes.c_void_p()
+
+    def __del__(self):
+        try:
+            self.free()
+        except Exception:
+            pass

@@ -41,13 +41,18 @@ def test_stack_matches_oracle(cuda, oracle):
     assert np.abs(got - exp).max() <= 1e-3 * scale
 
 
-@pytest.mark.parametrize("quant", ["fused", "separate", "mixed"])
-def test_stack_quant_placements_identical(cuda, quant):
-    """Fused, separate and mixed Q8_K placement give bit-identical logits."""
-    ref = Q2KDecodeStack(n_layers=2, hidden=1024, ffn=2816, vocab=2048, device=cuda, seed=9, quant="fused")
+@pytest.mark.parametrize("quant", ["fused", "separate", "mixed", "chain", "program"])
+@pytest.mark.parametrize("batch", [1, 2, 3, 4, 8])
+def test_stack_quant_placements_identical(cuda, quant, batch):
+    """Fused, separate, mixed and chained Q8_K placement, and the whole step as
+    one persistent kernel, give bit-identical logits."""
+    ref = Q2KDecodeStack(n_layers=2, hidden=1024, ffn=2816, vocab=2048, batch=batch, device=cuda, seed=9,
+                         quant="fused")
     a = ref.step().clone()
-    st = Q2KDecodeStack(n_layers=2, hidden=1024, ffn=2816, vocab=2048, device=cuda, seed=9, quant=quant)
+    st = Q2KDecodeStack(n_layers=2, hidden=1024, ffn=2816, vocab=2048, batch=batch, device=cuda, seed=9,
+                        quant=quant)
     assert torch.equal(st.step(), a)
+    assert torch.equal(st.step(), a)   # again: the chained counters reset themselves
 
 
 def test_stack_graph_replay_is_deterministic(cuda):
@@ -75,3 +80,55 @@ def test_shard_ranges_partition_rows():
             assert spans[0][0] == 0 and spans[-1][1] == n
             assert all(a[1] == b[0] for a, b in zip(spans, spans[1:]))
             assert all((hi - lo) % 32 == 0 for lo, hi in spans[:-1])
+
+
+def test_program_phase_inputs_and_graph_capture(cuda):
+    """A program whose first phase takes Q8_K rows and whose later phases take
+    fp32 rows (plain and RMS-normalized), against the separate GEMV launches,
+    eagerly and replayed from a CUDA graph."""
+    from smeai_b200 import IN_F32, IN_F32_RMS, IN_Q8K
+    from smeai_b200 import q2k as Q
+    g = torch.Generator(device=cuda).manual_seed(4)
+    mk = lambda rows, k: Q.Q2KMatrix(Q.quantize_q2k(torch.randn((rows, k), generator=g, device=cuda) * 0.02),
+                                     rows, k)
+    B = 2
+    a, b, c = mk(768, 512), mk(2 * 512, 768), mk(300, 512)
+    xq = Q.quantize_q8k(torch.randn((B, 512), generator=g, device=cuda))
+    r = torch.randn((B, 768), generator=g, device=cuda)
+    y0, y1, y2 = torch.empty((B, 768), device=cuda), torch.empty((B, 512), device=cuda), \
+        torch.empty((B, 300), device=cuda)
+    prog = Q.Q2KProgram([dict(w=a, x=xq, input=IN_Q8K, y=y0, epilogue=S.EPI_RESIDUAL, resid=r),
+                         dict(w=b, x=y0, input=IN_F32_RMS, y=y1, epilogue=S.EPI_SILU_MUL),
+                         dict(w=c, x=y1, input=IN_F32, y=y2)], B, rms_eps=1e-5)
+    e0 = a.mul_mat(xq, B, epilogue=S.EPI_RESIDUAL, resid=r)
+    e1 = b.mul_mat_f32_ex(e0, B, epilogue=S.EPI_SILU_MUL, rms_eps=1e-5)
+    e2 = c.mul_mat_f32_ex(e1, B)
+    prog.run()
+    torch.cuda.synchronize()
+    assert torch.equal(y0, e0) and torch.equal(y1, e1) and torch.equal(y2, e2)
+    stream = torch.cuda.Stream()
+    y2.zero_()
+    torch.cuda.synchronize()
+    gr = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(gr, stream=stream):
+        prog.run()
+    for _ in range(3):
+        with torch.cuda.stream(stream):
+            gr.replay()
+    stream.synchronize()
+    assert torch.equal(y2, e2)
+    del gr
+    prog.free()
+
+
+def test_program_rejects_bad_phases(cuda):
+    from smeai_b200 import IN_F32
+    from smeai_b200 import q2k as Q
+    m = Q.Q2KMatrix(Q.quantize_q2k(torch.randn((64, 512), device=cuda)), 64, 512)
+    x, y = torch.zeros((3, 512), device=cuda), torch.zeros((3, 64), device=cuda)
+    with pytest.raises(RuntimeError):      # 3 tokens: not 1, 2, 4 or 8
+        Q.Q2KProgram([dict(w=m, x=x, input=IN_F32, y=y)], 3)
+    with pytest.raises(RuntimeError):      # residual epilogue without a residual
+        Q.Q2KProgram([dict(w=m, x=x[:2], input=IN_F32, y=y[:2], epilogue=S.EPI_RESIDUAL)], 2)
+    with pytest.raises(RuntimeError):      # input rows shorter than k
+        Q.Q2KProgram([dict(w=m, x=torch.zeros((2, 256), device=cuda), input=IN_F32, y=y[:2])], 2)
