@@ -115,17 +115,6 @@ int smeai_q2k_mul_mat_tc(const void *w_dev, const void *x_q8k_dev, int64_t n_col
 int smeai_q2k_mul_mat_ex(const void *w_dev, const void *x_q8k_dev, int64_t n_cols, float *y_dev, size_t ldy,
                          int epilogue, const float *resid_dev, size_t ld_resid, void *stream);
 
-/* smeai_q2k_mul_mat_ex, then the next linear's input in the same kernel: once
- * every output row is written, rows [q_row0, q_row0 + q_rows) of each
- * activation row's result (q_rows a multiple of 256) are quantized to Q8_K
- * into y_q8k_dev (n_cols rows of q_rows/256 blocks) -- RMS-normalized first
- * when rms_eps >= 0 -- bit-identical to smeai_rms_q8k_quantize /
- * smeai_q8k_quantize of that slice.  The last CTA of the grid to finish does
- * it, so a decode step needs no separate quantizer kernels. */
-int smeai_q2k_mul_mat_chain(const void *w_dev, const void *x_q8k_dev, int64_t n_cols, float *y_dev, size_t ldy,
-                            int epilogue, const float *resid_dev, size_t ld_resid, int64_t q_row0, int64_t q_rows,
-                            float rms_eps, void *y_q8k_dev, void *stream);
-
 /* ---- decode program: a chain of dependent GEMVs as ONE persistent kernel ----
  * Phase p reads the complete output of phase p-1 (its input buffer is, or
  * contains, that output); each phase is one smeai_q2k_mul_mat_ex /

@@ -62,6 +62,7 @@ def lib() -> ctypes.CDLL:
             "orc_vec_dot_q2_K_q8_K": (F, [I, P, P, I]),
             "orc_q2k_mul_mat": (None, [P, I64, I64, P, I64, P, I64, I, I]),
             "orc_rms_inv": (F, [P, I64, F]),
+            "orc_rms_sumsq": (F, [P, I64]),
             "orc_rmsnorm_quantize_q8_K": (None, [P, P, I64, F, I]),
             "orc_silu_mul": (None, [P, P, P, I64]),
         }
@@ -182,6 +183,12 @@ def q2k_mul_mat(w: np.ndarray, n_rows: int, k: int, xq: np.ndarray, n_cols: int,
 def rms_inv(x, eps):
     x = np.ascontiguousarray(x, np.float32)
     return lib().orc_rms_inv(_p(x), x.size, eps)
+
+
+def rms_sumsq(x):
+    """Sum of squares in the fixed order of the RMSNorm (group sums, then the fold)."""
+    x = np.ascontiguousarray(x, np.float32)
+    return lib().orc_rms_sumsq(_p(x), x.size)
 
 
 def rmsnorm_quantize_q8_K(x, eps, rounding=ROUND_FUSED):

@@ -528,29 +528,40 @@ void orc_q2k_mul_mat(const orc_block_q2_K *w, int64_t n_rows, int64_t k,
 /* ======================================================================== */
 /* Decode-stack helpers (RMSNorm is the reference's sme_ai_rmsnorm_f32,      */
 /* sme_ai_ops.c:1060-1092: y = x / sqrt(mean(x^2) + eps)).  The sum of       */
-/* squares is taken in the fixed order the GPU kernel uses, so both sides    */
-/* round identically: per 256-value block, 32 partial sums of 8 consecutive  */
-/* squares (fused, ascending), folded pairwise at distances 16, 8, 4, 2, 1;  */
-/* then the block sums added in ascending block order.                       */
+/* squares is taken in the fixed order the GPU kernels use, so both sides    */
+/* round identically:                                                        */
+/*   1. per 32-value group g (values 32g .. 32g+31): the squares x*x, each   */
+/*      rounded, folded pairwise at distances 16, 8, 4, 2, 1 -> s_g;         */
+/*   2. 32 accumulators a_l = s_l + s_{l+32} + s_{l+64} + ... (ascending,    */
+/*      starting from 0), folded pairwise at distances 16, 8, 4, 2, 1.       */
+/* Step 1 is what one warp computes from one value per lane (the GEMV's row  */
+/* group), step 2 what one warp computes from all the group sums.            */
 /* ======================================================================== */
-float orc_rms_inv(const float *x, int64_t k, float eps) {
-    int64_t nb = k / ORC_QK_K;
-    float total = 0.0f;
-    for (int64_t b = 0; b < nb; ++b) {
-        float part[32];
-        for (int l = 0; l < 32; ++l) {
-            float s = 0.0f;
-            for (int i = 0; i < 8; ++i) {
-                float v = x[b * ORC_QK_K + l * 8 + i];
-                s = fmaf(v, v, s);
-            }
-            part[l] = s;
-        }
-        for (int width = 16; width >= 1; width /= 2)
-            for (int l = 0; l < width; ++l) part[l] = part[l] + part[l + width];
-        total = total + part[0];
+static float orc_fold32(float *a) {
+    for (int width = 16; width >= 1; width /= 2)
+        for (int l = 0; l < width; ++l) a[l] = a[l] + a[l + width];
+    return a[0];
+}
+
+float orc_rms_group_sumsq(const float *x) {
+    float a[32];
+    for (int l = 0; l < 32; ++l) a[l] = x[l] * x[l];
+    return orc_fold32(a);
+}
+
+float orc_rms_sumsq(const float *x, int64_t k) {
+    int64_t groups = k / 32;
+    float a[32];
+    for (int l = 0; l < 32; ++l) {
+        float acc = 0.0f;
+        for (int64_t g = l; g < groups; g += 32) acc = acc + orc_rms_group_sumsq(x + 32 * g);
+        a[l] = acc;
     }
-    float mean = total / (float) k;
+    return orc_fold32(a);
+}
+
+float orc_rms_inv(const float *x, int64_t k, float eps) {
+    float mean = orc_rms_sumsq(x, k) / (float) k;
     return 1.0f / sqrtf(mean + eps);
 }
 

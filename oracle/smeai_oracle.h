@@ -97,6 +97,8 @@ void orc_q2k_mul_mat(const orc_block_q2_K *w, int64_t n_rows, int64_t k,
                      int combine, int n_threads);
 
 /* ---------------- decode-stack helpers ---------------- */
+float orc_rms_group_sumsq(const float *x);      /* one 32-value group */
+float orc_rms_sumsq(const float *x, int64_t k);  /* k a multiple of 32 */
 float orc_rms_inv(const float *x, int64_t k, float eps);
 void orc_rmsnorm_quantize_q8_K(const float *x, orc_block_q8_K *y, int64_t k, float eps, int rounding);
 void orc_silu_mul(const float *g, const float *u, float *h, int64_t n);

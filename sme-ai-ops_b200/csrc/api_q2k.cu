@@ -251,24 +251,6 @@ int smeai_q2k_mul_mat_ex(const void* w_dev, const void* x_q8k_dev, int64_t n_col
                   as_stream(stream));
 }
 
-int smeai_q2k_mul_mat_chain(const void* w_dev, const void* x_q8k_dev, int64_t n_cols, float* y_dev, size_t ldy,
-                            int epilogue, const float* resid_dev, size_t ld_resid, int64_t q_row0, int64_t q_rows,
-                            float rms_eps, void* y_q8k_dev, void* stream) {
-  const Handle* h = as_handle(w_dev);
-  if (!h) return kBadArgument;
-  if (!y_q8k_dev) {
-    set_last_error("smeai_q2k_mul_mat_chain: NULL Q8_K output");
-    return kBadArgument;
-  }
-  Q8KChain chain;
-  chain.q8 = y_q8k_dev;
-  chain.row0 = q_row0;
-  chain.rows = q_rows;
-  chain.rms_eps = rms_eps;
-  return q2k_gemv_any(h->w, kInQ8K, x_q8k_dev, 0, 0.f, n_cols, y_dev, (int64_t)ldy, epilogue, resid_dev,
-                      (int64_t)ld_resid, as_stream(stream), &chain);
-}
-
 int smeai_q2k_program_create(const smeai_q2k_phase* phases, int n_phases, int64_t n_cols, float rms_eps,
                              void** prog_out) {
   if (!phases || !prog_out || n_phases <= 0 || n_cols <= 0 || n_cols > 8) {

@@ -168,6 +168,11 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, unsigned parity
     if (global_timer_ns() - t0 > timeout_ns) return false;
   }
 }
+// Ask the TMA engine to bring [src, src + bytes) into L2 (a hint: nothing
+// completes, nothing is written).  src 16-byte aligned; bytes a multiple of 16.
+__device__ __forceinline__ void bulk_prefetch_l2(const void* src, unsigned bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
 // Contiguous global -> shared copy by the TMA engine, completing on `bar`.
 // dst, src 16-byte aligned; bytes a multiple of 16.  No multicast.
 __device__ __forceinline__ void bulk_copy_g2s(void* dst, const void* src, unsigned bytes, uint64_t* bar) {
@@ -186,9 +191,6 @@ enum DeviceError : unsigned { kDevErrTimeout = 1u };
 __device__ __forceinline__ void raise_device_error(unsigned* err, unsigned code) { atomicOr(err, code); }
 unsigned* device_error_ptr();
 int device_error_take(unsigned* code);
-// Zero-initialised grid-completion counter of the GEMV's chained Q8_K output
-// for this (device, stream); device_error_take() resets all of them.
-unsigned* chain_counter(cudaStream_t stream);
 
 __device__ __forceinline__ void pdl_wait() {
   asm volatile("griddepcontrol.wait;" ::: "memory");

@@ -50,21 +50,8 @@ enum Epilogue : int {
 // rows quantized to Q8_K in the kernel's prologue, optionally after an RMSNorm.
 enum InMode : int { kInQ8K = 0, kInF32 = 1, kInF32Rms = 2 };
 
-// Chained output quantization: after the GEMV's last row is written, output
-// rows [row0, row0 + rows) of every token (rows a multiple of 256) are
-// quantized to Q8_K -- RMS-normalized first when rms_eps >= 0 -- into q8
-// (n_cols rows of rows/256 blocks), bit-identical to q8k_quantize /
-// rms_q8k_quantize of that slice.  The last CTA of the grid does it.
-struct Q8KChain {
-  void* q8 = nullptr;
-  int64_t row0 = 0;
-  int64_t rows = 0;
-  float rms_eps = -1.f;
-};
-
 int q2k_gemv_any(const Q2KWeight& w, int in_mode, const void* x, int64_t ld_x, float eps, int64_t n_cols,
-                 float* y, int64_t ldy, int epilogue, const float* resid, int64_t ld_resid, cudaStream_t stream,
-                 const Q8KChain* chain = nullptr);
+                 float* y, int64_t ldy, int epilogue, const float* resid, int64_t ld_resid, cudaStream_t stream);
 
 // y = W x for n_cols Q8_K activation rows (ggml layout, contiguous rows).
 int q2k_gemv(const Q2KWeight& w, const void* xq, int64_t n_cols, float* y, int64_t ldy, int epilogue,

@@ -73,7 +73,10 @@ __device__ __forceinline__ void store_q8k_smem(const Q8KLane& r, const ActSmem& 
 
 // Integer core + float term of super-block b for this lane's row.
 template <int T, bool SUMS>
-__device__ __forceinline__ void block_terms(const WBlock& wb, const ActSmem& m, int nb, int b, float* terms,
+// The activation of token t sits in slot aslot + t * astride; the term goes
+// to terms[(t * nb + b) * 32 + lane].
+__device__ __forceinline__ void block_terms(const WBlock& wb, const ActSmem& m, int aslot, int astride, int nb,
+                                            int b, float* terms,
                                             int lane, int64_t row, int64_t n_rows, int32_t* isum_out,
                                             int32_t* summs_out) {
   const unsigned sl[4] = {wb.s.x & 0x0F0F0F0Fu, wb.s.y & 0x0F0F0F0Fu, wb.s.z & 0x0F0F0F0Fu, wb.s.w & 0x0F0F0F0Fu};
@@ -97,7 +100,7 @@ __device__ __forceinline__ void block_terms(const WBlock& wb, const ActSmem& m, 
       const int chunk = h * 8 + s * 2 + hf;  // 16-byte activation chunk within the block
 #pragma unroll
       for (int t = 0; t < T; ++t) {
-        const int4 av = m.qs[(t * nb + b) * 16 + chunk];
+        const int4 av = m.qs[(aslot + t * astride) * 16 + chunk];
         int acc = dp4a_us(m0, av.x, 0);
         acc = dp4a_us(m1, av.y, acc);
         acc = dp4a_us(m2, av.z, acc);
@@ -111,7 +114,7 @@ __device__ __forceinline__ void block_terms(const WBlock& wb, const ActSmem& m, 
 #pragma unroll
   for (int t = 0; t < T; ++t) {
     const int isum = plane[t][0] + (plane[t][1] >> 2) + (plane[t][2] >> 4) + (plane[t][3] >> 6);
-    const int* bsp = m.bs + (t * nb + b) * 8;
+    const int* bsp = m.bs + (aslot + t * astride) * 8;
     const int4 bs0 = *reinterpret_cast<const int4*>(bsp);
     const int4 bs1 = *reinterpret_cast<const int4*>(bsp + 4);
     int mm = dp2a_lo_su(bs0.x, mh[0], 0);
@@ -128,7 +131,7 @@ __device__ __forceinline__ void block_terms(const WBlock& wb, const ActSmem& m, 
         summs_out[row * nb + b] = mm;
       }
     } else {
-      const float dx = m.d[t * nb + b];
+      const float dx = m.d[aslot + t * astride];
       const float dall = __fmul_rn(dx, dw);
       const float dmn = __fmul_rn(dx, dmw);
       terms[(t * nb + b) * 32 + lane] =

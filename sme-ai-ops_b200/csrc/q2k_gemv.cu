@@ -64,16 +64,6 @@ struct GemvParams {
   unsigned* err;
   int stages;        // ring depth (a power of two)
   int log2_stages;
-  // chained quantization: when chain_q8 is set, the grid's last CTA to finish
-  // quantizes output rows [chain_row0, chain_row0 + 256 * chain_nb) of every
-  // token to Q8_K blocks at chain_q8 (RMS-normalized first when chain_rms),
-  // so the next linear's input is ready when this kernel completes
-  uint8_t* chain_q8;
-  int64_t chain_row0;
-  int chain_nb;
-  int chain_rms;
-  float chain_eps;
-  unsigned* chain_ctr;  // zero between launches; the last CTA resets it
 };
 
 // Shared-memory carve-up for T tokens (16-byte aligned pieces).
@@ -82,24 +72,20 @@ struct Smem {
   int4* qs;        // [T*nb][16]  256 int8 per block
   int* bs;         // [T*nb][8]   16 int16 bsums per block
   float* d;        // [T*nb]
-  float* rsum;     // [T][nb + 1] RMS block sums, then 1/rms
+  float* rsum;     // [T][8 nb + 1] RMS group sums (8 per super-block), then 1/rms
   float* terms;    // [2][T*nb][32]
   uint64_t* full;  // [stages]
   uint64_t* empty; // [stages]
   uint64_t* grp;   // [2] all consumer lanes finished a row group
   uint64_t* tfree; // [2] the finisher has consumed the terms buffer
-  uint64_t* rms;   // [2] block sums written / 1/rms ready
-  uint64_t* done;  // all consumer lanes finished their row groups
-  uint64_t* verdict;  // the completion count has been taken
-  uint64_t* fin;   // [2] chained RMS: block sums written / 1/rms ready
-  unsigned* last;  // this CTA finished last
+  uint64_t* rms;   // [2] group sums written / 1/rms ready
 };
 
 __host__ __device__ __forceinline__ size_t align16(size_t v) { return (v + 15) & ~(size_t)15; }
 
 __host__ __device__ __forceinline__ size_t smem_fixed_bytes(int T, int nb) {
   return align16((size_t)T * nb * 256) + align16((size_t)T * nb * 32) + align16((size_t)T * nb * 4) +
-         align16((size_t)T * (nb + 1) * 4) + align16((size_t)2 * T * nb * 128) + 8 * 11 + 8;
+         align16((size_t)T * (8 * nb + 1) * 4) + align16((size_t)2 * T * nb * 128) + 8 * 6;
 }
 __host__ __device__ __forceinline__ size_t smem_total_bytes(int T, int nb, int stages, int consumers) {
   return (size_t)stages * consumers * kTileBytes + smem_fixed_bytes(T, nb) + (size_t)stages * 16;
@@ -117,7 +103,7 @@ __device__ __forceinline__ Smem carve(uint8_t* base, int T, int nb, int stages, 
   m.d = reinterpret_cast<float*>(base + o);
   o += align16((size_t)T * nb * 4);
   m.rsum = reinterpret_cast<float*>(base + o);
-  o += align16((size_t)T * (nb + 1) * 4);
+  o += align16((size_t)T * (8 * nb + 1) * 4);
   m.terms = reinterpret_cast<float*>(base + o);
   o += align16((size_t)2 * T * nb * 128);
   m.full = reinterpret_cast<uint64_t*>(base + o);
@@ -125,10 +111,6 @@ __device__ __forceinline__ Smem carve(uint8_t* base, int T, int nb, int stages, 
   m.grp = m.empty + stages;
   m.tfree = m.grp + 2;
   m.rms = m.tfree + 2;
-  m.done = m.rms + 2;
-  m.verdict = m.done + 1;
-  m.fin = m.verdict + 1;
-  m.last = reinterpret_cast<unsigned*>(m.fin + 2);
   return m;
 }
 
@@ -176,81 +158,6 @@ __device__ __forceinline__ void finish_group(const float* terms, int nb, int64_t
   }
 }
 
-// Chained quantization (consumer warps, after the main loop).  Every lane
-// fences its output stores; the CTA's completion is counted once all its
-// lanes have arrived; the CTA that brings the count to gridDim.x owns the
-// whole output and quantizes the slice exactly as rms_q8k_quantize_kernel /
-// q8k_quantize_kernel would (same helpers, same summation order).
-template <int T>
-__device__ __forceinline__ void chain_quantize(const Smem& m, const GemvParams& p, int cw, int W, int lane) {
-  __threadfence();
-  mbar_arrive_warp(m.done);
-  if (cw == 0) {
-    const bool ok = mbar_wait_bounded(m.done, 0, kWaitTimeoutNs);
-    if (lane == 0) {
-      unsigned last = 0;
-      if (ok) {
-        const unsigned old = atomicAdd(p.chain_ctr, 1u);
-        last = old == gridDim.x - 1 ? 1u : 0u;
-        if (last) atomicExch(p.chain_ctr, 0u);
-      } else {
-        raise_device_error(p.err, kDevErrTimeout);
-      }
-      *m.last = last;
-    }
-    __syncwarp();
-    mbar_arrive_warp(m.verdict);
-  }
-  if (!mbar_wait_bounded(m.verdict, 0, kWaitTimeoutNs)) {
-    raise_device_error(p.err, kDevErrTimeout);
-    return;
-  }
-  if (!*m.last) return;
-  __threadfence();
-  const int cnb = p.chain_nb, nq = T * cnb;
-  const float* ysl = p.y + p.chain_row0;
-  float* rs = m.terms;  // [T][cnb + 1]; the terms are consumed by now
-  if (p.chain_rms) {
-    for (int i = cw; i < nq; i += W) {
-      const int t = i / cnb, b = i - t * cnb;
-      float v[8];
-      load8_cg(ysl + t * p.ldy + b * QK_K + lane * 8, v);
-      const float s = block_sumsq_warp(v);
-      if (lane == 0) rs[t * (cnb + 1) + b] = s;
-    }
-    mbar_arrive_warp(&m.fin[0]);
-    if (cw == 0) {
-      if (!mbar_wait_bounded(&m.fin[0], 0, kWaitTimeoutNs)) {
-        raise_device_error(p.err, kDevErrTimeout);
-        return;
-      }
-      if (lane < T) {
-        float* r = rs + lane * (cnb + 1);
-        float total = 0.f;
-        for (int b = 0; b < cnb; ++b) total = __fadd_rn(total, r[b]);
-        r[cnb] = rms_inv_from_sum(total, cnb * QK_K, p.chain_eps);
-      }
-      __syncwarp();
-      mbar_arrive_warp(&m.fin[1]);
-    }
-    if (!mbar_wait_bounded(&m.fin[1], 0, kWaitTimeoutNs)) {
-      raise_device_error(p.err, kDevErrTimeout);
-      return;
-    }
-  }
-  for (int i = cw; i < nq; i += W) {
-    const int t = i / cnb, b = i - t * cnb;
-    float v[8];
-    load8_cg(ysl + t * p.ldy + b * QK_K + lane * 8, v);
-    if (p.chain_rms) {
-      const float inv = rs[t * (cnb + 1) + cnb];
-#pragma unroll
-      for (int k = 0; k < 8; ++k) v[k] = __fmul_rn(v[k], inv);
-    }
-    q8k_store_global(q8k_quantize_lane(v), p.chain_q8 + (int64_t)i * Q8K_BLOCK_BYTES);
-  }
-}
-
 template <int T, int EPI, int IN, bool SUMS>
 __global__ void __launch_bounds__(kMaxThreads) q2k_gemv_kernel(const GemvParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
@@ -279,10 +186,6 @@ __global__ void __launch_bounds__(kMaxThreads) q2k_gemv_kernel(const GemvParams 
     mbar_init(&m.tfree[1], 1);
     mbar_init(&m.rms[0], kConsumers);
     mbar_init(&m.rms[1], 1);
-    mbar_init(m.done, kConsumers);
-    mbar_init(m.verdict, 1);
-    mbar_init(&m.fin[0], kConsumers);
-    mbar_init(&m.fin[1], 1);
     mbar_fence_init();
   }
   __syncthreads();
@@ -330,12 +233,13 @@ __global__ void __launch_bounds__(kMaxThreads) q2k_gemv_kernel(const GemvParams 
   } else {
     const float* x = static_cast<const float*>(p.x);
     if constexpr (IN == kInF32Rms) {
+      const int gs = 8 * nb + 1;  // group sums per token, then 1/rms
       for (int i = cw; i < T * nb; i += kConsumers) {
         const int t = i / nb, b = i - t * nb;
         float v[8];
         load8(x + t * p.ld_x + b * QK_K + lane * 8, v);
-        const float s = block_sumsq_warp(v);
-        if (lane == 0) m.rsum[t * (nb + 1) + b] = s;
+        const float s = group_sumsq_load8(v);
+        if ((lane & 3) == 0) m.rsum[t * gs + b * 8 + (lane >> 2)] = s;
       }
       mbar_arrive_warp(&m.rms[0]);
       if (cw == 0) {
@@ -343,11 +247,10 @@ __global__ void __launch_bounds__(kMaxThreads) q2k_gemv_kernel(const GemvParams 
           raise_device_error(p.err, kDevErrTimeout);
           return;
         }
-        if (lane < T) {
-          float* rs = m.rsum + lane * (nb + 1);
-          float total = 0.f;
-          for (int b = 0; b < nb; ++b) total = __fadd_rn(total, rs[b]);
-          rs[nb] = rms_inv_from_sum(total, nb * QK_K, p.eps);
+#pragma unroll 1
+        for (int t = 0; t < T; ++t) {
+          const float total = rms_fold_groups(m.rsum + t * gs, 8 * nb);
+          if (lane == 0) m.rsum[t * gs + 8 * nb] = rms_inv_from_sum(total, nb * QK_K, p.eps);
         }
         mbar_arrive_warp(&m.rms[1]);
       }
@@ -362,7 +265,7 @@ __global__ void __launch_bounds__(kMaxThreads) q2k_gemv_kernel(const GemvParams 
         float v[8];
         load8(x + t * p.ld_x + b * QK_K + lane * 8, v);
         if constexpr (IN == kInF32Rms) {
-          const float inv = m.rsum[t * (nb + 1) + nb];
+          const float inv = m.rsum[t * (8 * nb + 1) + 8 * nb];
 #pragma unroll
           for (int k = 0; k < 8; ++k) v[k] = __fmul_rn(v[k], inv);
         }
@@ -397,7 +300,7 @@ __global__ void __launch_bounds__(kMaxThreads) q2k_gemv_kernel(const GemvParams 
       const uint8_t* tile = m.ring + (size_t)s * stage_bytes + (size_t)cw * kTileBytes;
       const WBlock wb = load_wblock(tile, lane);
       mbar_arrive_warp(&m.empty[s], wblock_dep(wb));
-      block_terms<T, SUMS>(wb, act, nb, b, terms, lane, row, p.n_rows, p.isum_out, p.summs_out);
+      block_terms<T, SUMS>(wb, act, b, nb, nb, b, terms, lane, row, p.n_rows, p.isum_out, p.summs_out);
     }
     if constexpr (!SUMS) {
       mbar_arrive_warp(&m.grp[buf]);
@@ -410,9 +313,6 @@ __global__ void __launch_bounds__(kMaxThreads) q2k_gemv_kernel(const GemvParams 
         mbar_arrive_warp(&m.tfree[buf]);
       }
     }
-  }
-  if constexpr (!SUMS) {
-    if (p.chain_q8) chain_quantize<T>(m, p, cw, kConsumers, lane);
   }
 }
 
@@ -614,8 +514,7 @@ int q2k_repack(const void* w_blocks_dev, int64_t n_rows, int64_t k, Q2KWeight* o
 }
 
 int q2k_gemv_any(const Q2KWeight& w, int in_mode, const void* x, int64_t ld_x, float eps, int64_t n_cols,
-                 float* y, int64_t ldy, int epilogue, const float* resid, int64_t ld_resid, cudaStream_t stream,
-                 const Q8KChain* chain) {
+                 float* y, int64_t ldy, int epilogue, const float* resid, int64_t ld_resid, cudaStream_t stream) {
   if (!w.tiles || !x || !y || n_cols <= 0) {
     set_last_error("q2k_gemv: bad arguments");
     return kBadArgument;
@@ -641,24 +540,6 @@ int q2k_gemv_any(const Q2KWeight& w, int in_mode, const void* x, int64_t ld_x, f
     set_last_error("q2k_gemv: leading dimension smaller than the output rows");
     return kBadArgument;
   }
-  unsigned* ctr = nullptr;
-  int cnb = 0;
-  if (chain && chain->q8) {
-    if (chain->rows <= 0 || chain->rows % QK_K || chain->row0 < 0 || chain->row0 + chain->rows > out_rows ||
-        (reinterpret_cast<uintptr_t>(chain->q8) & 3)) {
-      set_last_error("q2k_gemv: chained quantization needs a slice of the output whose length is a multiple "
-                     "of 256 and a 4-byte aligned Q8_K buffer");
-      return kBadArgument;
-    }
-    cnb = (int)(chain->rows / QK_K);
-    if (cnb + 1 > 64 * w.nb) {  // the RMS block sums reuse the terms buffer
-      set_last_error("q2k_gemv: chained slice of %lld rows too long for k=%lld", (long long)chain->rows,
-                     (long long)w.k);
-      return kBadArgument;
-    }
-    ctr = chain_counter(stream);
-    if (!ctr) return kCudaError;
-  }
   for (int64_t c0 = 0; c0 < n_cols;) {
     const int64_t rem = n_cols - c0;
     int T = rem >= 8 ? 8 : (rem >= 4 ? 4 : (rem >= 2 ? 2 : 1));
@@ -676,14 +557,6 @@ int q2k_gemv_any(const Q2KWeight& w, int in_mode, const void* x, int64_t ld_x, f
     p.ldy = ldy;
     p.resid = resid ? resid + c0 * ld_resid : nullptr;
     p.ld_resid = ld_resid;
-    if (ctr) {
-      p.chain_q8 = static_cast<uint8_t*>(chain->q8) + c0 * (int64_t)cnb * Q8K_BLOCK_BYTES;
-      p.chain_row0 = chain->row0;
-      p.chain_nb = cnb;
-      p.chain_rms = chain->rms_eps >= 0.f ? 1 : 0;
-      p.chain_eps = chain->rms_eps;
-      p.chain_ctr = ctr;
-    }
     int st;
     switch (in_mode) {
       case kInQ8K: st = dispatch_epi<kInQ8K>(epilogue, T, w, p, stream); break;

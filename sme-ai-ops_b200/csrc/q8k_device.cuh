@@ -23,15 +23,66 @@ struct Q8KLane {
   float d;
 };
 
-// RMS partial of one 256-value block: lane sums of 8 fused squares, folded at
-// distances 16, 8, 4, 2, 1 (the fixed order the CPU restatement follows).
-__device__ __forceinline__ float block_sumsq_warp(const float (&v)[8]) {
-  float s = 0.f;
+// RMSNorm sum of squares, in the fixed order of the CPU restatement:
+//   1. per 32-value group: the squares (each rounded) folded pairwise at
+//      distances 16, 8, 4, 2, 1;
+//   2. the group sums: lane l adds groups l, l+32, l+64, ... in ascending
+//      order from 0, then the lanes are folded at distances 16, 8, 4, 2, 1.
+// Group sum from the load8 layout (8 consecutive values per lane; lanes
+// 4q..4q+3 hold group q of the 256-value block): distances 16 and 8 are
+// lanes xor 2 and xor 1, distances 4, 2, 1 are within the lane.  All four
+// lanes of the group return the sum.
+__device__ __forceinline__ float group_sumsq_load8(const float (&v)[8]) {
+  float a[8];
 #pragma unroll
-  for (int i = 0; i < 8; ++i) s = __fmaf_rn(v[i], v[i], s);
+  for (int b = 0; b < 8; ++b) a[b] = __fmul_rn(v[b], v[b]);
 #pragma unroll
-  for (int off = 16; off >= 1; off >>= 1) s = __fadd_rn(s, __shfl_xor_sync(0xffffffffu, s, off));
-  return s;
+  for (int b = 0; b < 8; ++b) a[b] = __fadd_rn(a[b], __shfl_xor_sync(0xffffffffu, a[b], 2));
+#pragma unroll
+  for (int b = 0; b < 8; ++b) a[b] = __fadd_rn(a[b], __shfl_xor_sync(0xffffffffu, a[b], 1));
+#pragma unroll
+  for (int b = 0; b < 4; ++b) a[b] = __fadd_rn(a[b], a[b + 4]);
+  a[0] = __fadd_rn(a[0], a[2]);
+  a[1] = __fadd_rn(a[1], a[3]);
+  return __fadd_rn(a[0], a[1]);
+}
+// Group sum with one value per lane (lane i holds value i of the group); all
+// lanes return it.
+__device__ __forceinline__ float group_sumsq_lane(float v) {
+  float a = __fmul_rn(v, v);
+#pragma unroll
+  for (int off = 16; off >= 1; off >>= 1) a = __fadd_rn(a, __shfl_xor_sync(0xffffffffu, a, off));
+  return a;
+}
+// Step 2 over G group sums at p (shared or global memory); all lanes return
+// the total.
+// The same over group sums other CTAs of the running grid wrote (read
+// through L2; each lane's loads go out together).
+__device__ __forceinline__ float rms_fold_groups_cg(const float* p, int G) {
+  const int lane = threadIdx.x & 31;
+  float acc = 0.f;
+  for (int g0 = 0; g0 < G; g0 += 32 * 8) {
+    float v[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int g = g0 + lane + 32 * j;
+      v[j] = g < G ? __ldcg(p + g) : 0.f;
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      if (g0 + lane + 32 * j < G) acc = __fadd_rn(acc, v[j]);
+  }
+#pragma unroll
+  for (int off = 16; off >= 1; off >>= 1) acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, off));
+  return acc;
+}
+__device__ __forceinline__ float rms_fold_groups(const float* p, int G) {
+  const int lane = threadIdx.x & 31;
+  float acc = 0.f;
+  for (int g = lane; g < G; g += 32) acc = __fadd_rn(acc, p[g]);
+#pragma unroll
+  for (int off = 16; off >= 1; off >>= 1) acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, off));
+  return acc;
 }
 
 // inv = 1/sqrt(sum/k + eps), each step rounded once.

@@ -27,7 +27,7 @@ __global__ void q8k_quantize_kernel(const float* __restrict__ x, int64_t ld_x, i
 // RMSNorm + quantization, one CTA per row.
 __global__ void rms_q8k_quantize_kernel(const float* __restrict__ x, int64_t ld_x, int nb, float eps,
                                         uint8_t* __restrict__ y) {
-  extern __shared__ float sm_bsum[];  // nb floats + 1
+  extern __shared__ float sm_gsum[];  // 8 group sums per block, then 1/rms
   pdl_trigger();
   pdl_wait();
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
@@ -36,17 +36,16 @@ __global__ void rms_q8k_quantize_kernel(const float* __restrict__ x, int64_t ld_
   for (int b = warp; b < nb; b += nwarps) {
     float v[8];
     load8(xr + b * QK_K + lane * 8, v);
-    const float s = block_sumsq_warp(v);
-    if (lane == 0) sm_bsum[b] = s;
+    const float s = group_sumsq_load8(v);
+    if ((lane & 3) == 0) sm_gsum[b * 8 + (lane >> 2)] = s;
   }
   __syncthreads();
-  if (threadIdx.x == 0) {
-    float total = 0.f;
-    for (int b = 0; b < nb; ++b) total = __fadd_rn(total, sm_bsum[b]);
-    sm_bsum[nb] = rms_inv_from_sum(total, nb * QK_K, eps);
+  if (warp == 0) {
+    const float total = rms_fold_groups(sm_gsum, nb * 8);
+    if (lane == 0) sm_gsum[nb * 8] = rms_inv_from_sum(total, nb * QK_K, eps);
   }
   __syncthreads();
-  const float inv = sm_bsum[nb];
+  const float inv = sm_gsum[nb * 8];
   for (int b = warp; b < nb; b += nwarps) {
     float v[8];
     load8(xr + b * QK_K + lane * 8, v);
@@ -80,7 +79,7 @@ int rms_q8k_quantize(const float* x, int64_t ld_x, int64_t n_rows, int64_t k, fl
   }
   const int nb = (int)(k / QK_K);
   const int threads = nb >= 16 ? 512 : (nb >= 8 ? 256 : 128);
-  SMEAI_CUDA_TRY(launch(rms_q8k_quantize_kernel, dim3((unsigned)n_rows), dim3(threads), (size_t)(nb + 1) * 4,
+  SMEAI_CUDA_TRY(launch(rms_q8k_quantize_kernel, dim3((unsigned)n_rows), dim3(threads), (size_t)(8 * nb + 1) * 4,
                         stream, x, ld_x, nb, eps, static_cast<uint8_t*>(y)));
   return kOk;
 }

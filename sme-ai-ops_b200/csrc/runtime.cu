@@ -4,10 +4,6 @@
 #include <stdlib.h>
 #include <string.h>
 
-#include <map>
-#include <mutex>
-#include <utility>
-
 #include "common.cuh"
 #include "runtime.h"
 
@@ -37,44 +33,6 @@ bool pdl_enabled() {
 
 namespace {
 __device__ unsigned g_device_error = 0;
-// Grid-completion counters of the GEMV's chained quantization, one per
-// (device, stream) slot; each launch's last CTA puts its counter back to 0.
-constexpr int kChainSlots = 256;
-__device__ unsigned g_chain_ctr[kChainSlots];
-std::mutex g_chain_mu;
-std::map<std::pair<int, cudaStream_t>, int> g_chain_slot;
-}
-
-unsigned* chain_counter(cudaStream_t stream) {
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess) {
-    cudaGetLastError();
-    set_last_error("chain counter: no current device");
-    return nullptr;
-  }
-  std::lock_guard<std::mutex> lock(g_chain_mu);
-  auto it = g_chain_slot.find({dev, stream});
-  int slot;
-  if (it != g_chain_slot.end()) {
-    slot = it->second;
-  } else {
-    int used = 0;
-    for (const auto& kv : g_chain_slot)
-      if (kv.first.first == dev) ++used;
-    if (used >= kChainSlots) {
-      set_last_error("chain counter: more than %d streams on device %d", kChainSlots, dev);
-      return nullptr;
-    }
-    slot = used;
-    g_chain_slot[{dev, stream}] = slot;
-  }
-  void* p = nullptr;
-  if (cudaGetSymbolAddress(&p, g_chain_ctr) != cudaSuccess) {
-    cudaGetLastError();
-    set_last_error("chain counter: symbol address unavailable");
-    return nullptr;
-  }
-  return static_cast<unsigned*>(p) + slot;
 }
 
 unsigned* device_error_ptr() {
@@ -95,12 +53,7 @@ unsigned* device_error_ptr() {
 int device_error_take(unsigned* code) {
   unsigned v = 0, zero = 0;
   SMEAI_CUDA_TRY(cudaMemcpyFromSymbol(&v, g_device_error, sizeof(v)));
-  if (v) {
-    // a kernel that gave up may have left a completion counter mid-count
-    static const unsigned zeros[kChainSlots] = {0};
-    SMEAI_CUDA_TRY(cudaMemcpyToSymbol(g_chain_ctr, zeros, sizeof(zeros)));
-    SMEAI_CUDA_TRY(cudaMemcpyToSymbol(g_device_error, &zero, sizeof(zero)));
-  }
+  if (v) SMEAI_CUDA_TRY(cudaMemcpyToSymbol(g_device_error, &zero, sizeof(zero)));
   *code = v;
   return kOk;
 }

@@ -78,7 +78,6 @@ def _declare(L: ctypes.CDLL) -> None:
         "smeai_rms_q8k_quantize": (I, [P, I64, I64, I64, F, P, P]),
         "smeai_q2k_mul_mat": (I, [P, I64, I64, P, I64, P, SZ, P]),
         "smeai_q2k_mul_mat_ex": (I, [P, P, I64, P, SZ, I, P, SZ, P]),
-        "smeai_q2k_mul_mat_chain": (I, [P, P, I64, P, SZ, I, P, SZ, I64, I64, F, P, P]),
         "smeai_q2k_mul_mat_tc": (I, [P, P, I64, P, SZ, P]),
         "smeai_q2k_mul_mat_f32": (I, [P, P, I64, P, SZ, P]),
         "smeai_q2k_mul_mat_f32_ex": (I, [P, P, SZ, I64, P, SZ, I, P, SZ, F, P]),

@@ -96,22 +96,6 @@ class Q2KMatrix:
         check(st, "q2k_mul_mat")
         return out
 
-    def mul_mat_chain(self, xq: torch.Tensor, n_cols: int, out: torch.Tensor, q_out: torch.Tensor,
-                      q_row0: int = 0, q_rows: int | None = None, epilogue: int = EPI_STORE,
-                      resid: torch.Tensor | None = None, rms_eps: float | None = None) -> torch.Tensor:
-        """mul_mat with the result's rows [q_row0, q_row0 + q_rows) quantized to
-        Q8_K into q_out by the same kernel (RMS-normalized first when rms_eps is
-        given) -- the next linear's input."""
-        out_rows = self.n_rows // 2 if epilogue == EPI_SILU_MUL else self.n_rows
-        q_rows = out_rows - q_row0 if q_rows is None else q_rows
-        ldy = out.stride(0) if out.dim() == 2 else out_rows
-        ldr = 0 if resid is None else (resid.stride(0) if resid.dim() == 2 else out_rows)
-        eps = -1.0 if rms_eps is None else float(rms_eps)
-        check(lib().smeai_q2k_mul_mat_chain(self.handle, _ptr(xq), n_cols, _ptr(out), ldy, epilogue, _ptr(resid),
-                                            ldr, q_row0, q_rows, ctypes.c_float(eps), _ptr(q_out), cur_stream()),
-              "q2k_mul_mat_chain")
-        return out
-
     def mul_mat_tc(self, xq: torch.Tensor, n_cols: int, out: torch.Tensor | None = None) -> torch.Tensor:
         """The tensor-core GEMM path (any number of activation rows)."""
         if out is None:

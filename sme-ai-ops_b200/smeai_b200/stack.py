@@ -81,13 +81,10 @@ class Q2KDecodeStack:
         # GEMV's prologue; "separate" = a quantizer kernel before the GEMV;
         # "mixed" = fused where an RMSNorm comes first (qkv, gate/up, lm_head),
         # separate for the plain re-quantizations (o, down).  All three give
-        # bit-identical results.  "chain" (one GPU): every GEMV quantizes the
-        # next linear's input itself (its last CTA, after the output is
-        # complete), so a step is one quantizer plus the GEMVs.
-        # "program" (one GPU; batch 1, 2, 4 or 8): the whole step is ONE
-        # persistent kernel (Q2KProgram) -- same bits as the others.
-        assert quant in ("fused", "separate", "mixed", "chain", "program")
-        if quant in ("chain", "program") and world > 1:
+        # bit-identical results.  "program" (one GPU; batch 1, 2, 4 or 8): the
+        # whole step is ONE persistent kernel (Q2KProgram) -- same bits again.
+        assert quant in ("fused", "separate", "mixed", "program")
+        if quant == "program" and world > 1:
             quant = "separate"   # the next input is only complete after the all-gather
         if quant == "program" and batch not in (1, 2, 4, 8):
             quant = "separate"
@@ -182,8 +179,6 @@ class Q2KDecodeStack:
         B, H, hs = self.B, self.H, self.hs
         self.x.copy_(self.x0 if x_in is None else x_in)
         one = self.world == 1
-        if self.quant == "chain":
-            return self._step_chain()
         if self.quant == "program":
             if self.prog is None:
                 self.prog = self._build_program()
@@ -227,18 +222,6 @@ class Q2KDecodeStack:
         phases.append(dict(w=self.lm, x=self.x, input=IN_F32_RMS, y=self.logits))
         return Q.Q2KProgram(phases, self.B, rms_eps=self.eps)
 
-    def _step_chain(self):
-        B, hs, eps = self.B, self.hs, self.eps
-        x, xq = self.x, self.xq
-        Q.rms_quantize_q8k(x, eps, out=xq)
-        for wqkv, wo, wgu, wd in self.layers:
-            wqkv.mul_mat_chain(xq, B, self.qkv, self.vq, q_row0=2 * hs, q_rows=hs)
-            wo.mul_mat_chain(self.vq, B, x, xq, epilogue=EPI_RESIDUAL, resid=x, rms_eps=eps)
-            wgu.mul_mat_chain(xq, B, self.h_full, self.hq, epilogue=EPI_SILU_MUL)
-            wd.mul_mat_chain(self.hq, B, x, xq, epilogue=EPI_RESIDUAL, resid=x, rms_eps=eps)
-        self.lm.mul_mat(xq, B, out=self.logits)
-        return self.logits
-
     # --------------------------------------------------------------- accounting
     def launches_per_step(self) -> int:
         """Kernels of this library per step: one GEMV per linear (the batch is
@@ -247,8 +230,8 @@ class Q2KDecodeStack:
         if self.quant == "program":
             return 1
         chunks = self.B // 8 + bin(self.B % 8).count("1")
-        per_layer = {"fused": 0, "separate": 4, "mixed": 2, "chain": 0}[self.quant]
-        return (self.L * 4 + 1) * chunks + self.L * per_layer + (1 if self.quant in ("separate", "chain") else 0)
+        per_layer = {"fused": 0, "separate": 4, "mixed": 2}[self.quant]
+        return (self.L * 4 + 1) * chunks + self.L * per_layer + (1 if self.quant == "separate" else 0)
 
     def gemv_list(self):
         """(name, matrix, k, cols, out_rows) of every GEMV in a step."""

@@ -165,3 +165,30 @@ def test_rms_inv_close_to_float64(oracle):
     inv = oracle.rms_inv(x, 1e-5)
     ref = 1.0 / np.sqrt((x.astype(np.float64) ** 2).mean() + 1e-5)
     assert abs(inv - ref) <= 1e-6 * ref
+
+
+def _fold32(a):
+    a = a.astype(np.float32).copy()
+    w = 16
+    while w >= 1:
+        a[:w] = (a[:w] + a[w:2 * w]).astype(np.float32)
+        w //= 2
+    return np.float32(a[0])
+
+
+@pytest.mark.parametrize("k", [256, 4096, 11008])
+def test_rms_sum_order_pinned(oracle, k):
+    """The RMSNorm sum of squares follows one fixed order (32-value group
+    folds, then 32 lane accumulators over the groups, folded), restated here
+    in numpy float32 steps: the oracle must give the same bits."""
+    x = np.random.default_rng(k).standard_normal(k).astype(np.float32) * 2
+    groups = [_fold32((x[32 * g:32 * g + 32] * x[32 * g:32 * g + 32]).astype(np.float32)) for g in range(k // 32)]
+    acc = np.zeros(32, np.float32)
+    for lane in range(32):
+        a = np.float32(0)
+        for g in range(lane, k // 32, 32):
+            a = np.float32(a + groups[g])
+        acc[lane] = a
+    exp = _fold32(acc)
+    got = np.float32(oracle.rms_sumsq(x))
+    assert got.view(np.uint32) == exp.view(np.uint32)

@@ -308,50 +308,6 @@ def test_mul_mat_many_row_groups_per_cta(cuda, oracle, rows, k, cols):
     assert np.array_equal(y.view(np.uint32), exp.view(np.uint32))
 
 
-@pytest.mark.parametrize("rows,k,cols,epi,rms,row0,qrows", [
-    (4096, 4096, 1, S.EPI_RESIDUAL, True, 0, 4096),        # o-proj: x += W v, then Q8_K(rmsnorm(x))
-    (3 * 1024, 1024, 3, S.EPI_STORE, False, 2048, 1024),   # qkv: the v slice
-    (2 * 2816, 1024, 2, S.EPI_SILU_MUL, False, 0, 2816),   # gate/up: Q8_K(silu(g) * u)
-    (1024, 2816, 11, S.EPI_RESIDUAL, True, 0, 1024),       # down, 11 tokens = launches of 8, 2, 1
-    (148 * 4 * 32 + 64, 256, 1, S.EPI_STORE, True, 256, 512),  # several row groups per CTA
-])
-def test_chained_quantization_bit_identical(cuda, oracle, rows, k, cols, epi, rms, row0, qrows):
-    """A GEMV whose last CTA quantizes the output slice gives the bits of the
-    GEMV followed by the standalone quantizer (and of the oracle's quantizer)."""
-    m = Q.Q2KMatrix(gpu_q2k_weights(cuda, rows, k, rows % 89), rows, k)
-    g = torch.Generator(device=cuda).manual_seed(rows + cols)
-    xq = Q.quantize_q8k(torch.randn((cols, k), generator=g, device=cuda))
-    out_rows = rows // 2 if epi == S.EPI_SILU_MUL else rows
-    r = torch.randn((cols, out_rows), generator=g, device=cuda)
-    y_ref, y = r.clone(), r.clone()
-    resid_ref, resid = (y_ref, y) if epi == S.EPI_RESIDUAL else (None, None)
-    m.mul_mat(xq, cols, out=y_ref, epilogue=epi, resid=resid_ref)
-    sl = y_ref[:, row0:row0 + qrows]
-    q_ref = Q.rms_quantize_q8k(sl, 1e-5) if rms else Q.quantize_q8k(sl)
-    q = torch.full_like(q_ref, 0x5A)
-    for _ in range(2):   # twice: the completion counter must have reset itself
-        y.copy_(r)
-        m.mul_mat_chain(xq, cols, y, q, q_row0=row0, q_rows=qrows, epilogue=epi, resid=resid,
-                        rms_eps=1e-5 if rms else None)
-        torch.cuda.synchronize()
-        assert torch.equal(y, y_ref)
-        assert torch.equal(q, q_ref)
-    sl_np = sl.cpu().numpy()
-    for c in range(cols):
-        exp = oracle.rmsnorm_quantize_q8_K(sl_np[c], 1e-5) if rms else oracle.quantize_q8_K(sl_np[c])
-        assert np.array_equal(q[c].cpu().numpy(), q8k_bytes(exp))
-
-
-def test_chained_quantization_rejects_bad_slices(cuda):
-    m = Q.Q2KMatrix(gpu_q2k_weights(cuda, 512, 256, 3), 512, 256)
-    xq = Q.quantize_q8k(torch.randn((1, 256), device=cuda))
-    y = torch.empty((1, 512), device=cuda)
-    q = torch.empty((1, 2 * 292), dtype=torch.uint8, device=cuda)
-    for row0, rows in ((0, 300), (384, 256), (-256, 256)):
-        with pytest.raises(RuntimeError):
-            m.mul_mat_chain(xq, 1, y, q, q_row0=row0, q_rows=rows)
-
-
 def test_no_device_error_recorded(cuda):
     """Every bounded wait in the GEMV completed: the device error word is clear."""
     import ctypes as C
