@@ -2,17 +2,21 @@
 """Benchmark of the Q2_K mul_mat hot path on B200 (see DESIGN.md for the metric).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload decode|gemv]
+                    [--workload decode|gemv|prefill] [--quant program|separate|fused|mixed]
 
 Workloads (one "step" each):
   decode  (default)  one token through the Llama-2-7B-shape Q2_K linear stack:
                      32 layers x {Wq,Wk,Wv,Wo 4096x4096; Wg,Wu 11008x4096;
                      Wd 4096x11008} + lm_head 32000x4096, batch 1, every linear's
                      input re-quantized to Q8_K (RMSNorm fused before the qkv,
-                     gate/up and lm_head inputs).  Row-sharded over N GPUs with
-                     NCCL all-gathers of the output slices.
+                     gate/up and lm_head inputs).  On one GPU the whole step is
+                     one persistent kernel (q2k_program_kernel); on N GPUs the
+                     weights are row-sharded and each linear is one GEMV launch
+                     followed by an NCCL all-gather of the output slices.
   gemv               one Q2_K x Q8_K GEMV W[4096,4096] x x[4096], rotating
                      over 64 distinct weight copies (352 MB > L2).
+  prefill            activations [512,4096] (Q8_K per row) x W[11008,4096] Q2_K
+                     on the tcgen05 tensor cores.
 
 Metric: "Q2_K mul_mat HBM GB/s": algorithmic bytes of every GEMV in the step
 (Q2_K weights + Q8_K activations + fp32 outputs), summed over ranks, per
@@ -50,8 +54,10 @@ def parse_args():
     ap.add_argument("--workload", choices=["decode", "gemv", "prefill"], default="decode")
     ap.add_argument("--prefill-tokens", type=int, default=512, help="prefill workload: activation rows")
     ap.add_argument("--layers", type=int, default=32)
-    ap.add_argument("--quant", choices=["fused", "separate", "mixed"], default="separate",
-                    help="where each linear's Q8_K quantization runs (results are identical)")
+    ap.add_argument("--quant", choices=["fused", "separate", "mixed", "program"], default="program",
+                    help="decode: 'program' (default) runs the whole step as one persistent kernel on one GPU; "
+                         "the others launch one GEMV per linear with the Q8_K quantization fused, separate or "
+                         "mixed (all give identical results; N > 1 GPUs always launch per linear)")
     ap.add_argument("--gemv-rows", type=int, default=4096, help="gemv workload: weight rows")
     ap.add_argument("--gemv-k", type=int, default=4096, help="gemv workload: row length")
     ap.add_argument("--gemv-epilogue", type=int, default=0, help="gemv workload: 0 store, 1 residual, 2 silu*mul")
@@ -76,10 +82,10 @@ def hbm_peak():
         return FALLBACK_HBM_GBS, "fallback"
 
 
-def traffic_ratio():
-    """DRAM bytes per algorithmic byte of the GEMV, from the committed ncu
-    summary (profiles/q2k_gemv_decode.txt, line 'traffic_ratio=<x>')."""
-    path = os.path.join(ROOT, "profiles", "q2k_gemv_decode.txt")
+def traffic_ratio(name="q2k_gemv_decode.txt"):
+    """DRAM bytes per algorithmic byte of a kernel, from its committed ncu
+    summary under profiles/ (line 'traffic_ratio=<x>')."""
+    path = os.path.join(ROOT, "profiles", name)
     try:
         for line in open(path):
             if line.startswith("traffic_ratio="):
@@ -286,6 +292,32 @@ def gemv_roofline(gemvs, stream, dev, peak, peak_kind):
                            for n, v in per.items()}}
 
 
+def program_roofline(stack, stream, peak, peak_kind, launches=8):
+    """The persistent decode kernel timed per launch (events around each
+    launch, queued behind a sleep kernel; one launch = one token, 2.17 GB of
+    distinct weights, far more than L2)."""
+    import torch
+    evs = []
+    with torch.cuda.stream(stream):
+        stack.prog.run()
+        torch.cuda._sleep(20_000_000)
+        for _ in range(launches):
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            stack.prog.run()
+            b.record(stream)
+            evs.append((a, b))
+    stream.synchronize()
+    ms = statistics.median(a.elapsed_time(b) for a, b in evs)
+    nbytes = stack.algorithmic_bytes()
+    achieved = nbytes / (ms / 1e3) / 1e9
+    ratio = traffic_ratio("q2k_program_decode.txt")
+    return {"bound": "hbm", "kernel": "q2k_program_kernel", "achieved": achieved, "peak": peak, "unit": "GB/s",
+            "frac": achieved / peak, "peak_kind": peak_kind,
+            "traffic": (ratio * nbytes) if ratio else None, "algorithmic_bytes_per_launch": nbytes,
+            "median_launch_us": ms * 1e3, "launches_timed": launches}
+
+
 # ---------------------------------------------------------------------------- GPU side
 def run_ours(args):
     import torch
@@ -482,7 +514,10 @@ def run_ours(args):
     # ---- roofline of the dominant kernel: every GEMV of a step timed alone
     # (events around each launch, queued behind a sleep so launch gaps do not
     # count; consecutive GEMVs read distinct weights, so nothing sits in L2)
-    if gemvs:
+    if args.workload == "decode" and stack.quant == "program":
+        roofline = program_roofline(stack, stream, peak, peak_kind)
+        roofline["gemv_per_launch"] = gemv_roofline(gemvs, stream, dev, peak, peak_kind)
+    elif gemvs:
         roofline = gemv_roofline(gemvs, stream, dev, peak, peak_kind)
 
     # ---- CPU baseline (rank 0, one GPU only)
@@ -512,7 +547,7 @@ def run_ours(args):
                        **({"prefill_ops_per_step": prefill_ops, "tops": prefill_ops / (ms / 1e3) / 1e12}
                           if args.workload == "prefill" else {}),
                        "cuda_graph": use_graph, "pdl": os.environ.get("SMEAI_PDL", "1") != "0",
-                       "q8k_placement": args.quant},
+                       "q8k_placement": stack.quant if args.workload == "decode" else args.quant},
             "clocks": clocks,
             "e2e": {"value": e2e_value, "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "ms_per_step": e2e_ms},

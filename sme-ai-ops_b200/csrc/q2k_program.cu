@@ -22,6 +22,8 @@
 //   * before phase p, one lane of the CTA waits (acquire loads, bounded by
 //     wall time and by the launch's abort word) until phase p-1's counter
 //     reaches its group count, while the other warps sleep on an mbarrier;
+//     meanwhile its warp copies phase p's descriptor into shared memory, so
+//     no field is read through the (then stale) L1 on the critical path;
 //     then every warp issues one round of loads -- its own activation blocks,
 //     the producer's group sums (an RMSNorm input: each warp folds them to
 //     the same 1/rms, no cross-warp barrier), the residual of the groups it
@@ -92,10 +94,11 @@ struct PSmem {
   int* bs;
   float* d;
   float* terms;
+  PhaseDev* pd;       // [2] descriptors of the CTA's current and previous phase
   uint64_t* full;
   uint64_t* empty;
-  uint64_t* grp;      // [2]
-  uint64_t* tfree;    // [2]
+  uint64_t* grp;      // [2] all consumer warps wrote a row group's terms
+  uint64_t* tfree;    // [2] the finisher has consumed them
   uint64_t* done;
   uint64_t* inready;  // the CTA's poller saw the previous phase complete
   uint64_t* invready; // the poller has put 1/rms of every token in inv[]
@@ -117,7 +120,8 @@ __host__ __device__ __forceinline__ size_t act_slots(int T, int nb_max, int W) {
 
 __host__ __device__ __forceinline__ size_t prog_fixed_bytes(int T, int nb_max, int W) {
   const size_t slots = act_slots(T, nb_max, W);
-  return al16(slots * 256) + al16(slots * 32) + al16(slots * 4) + al16((size_t)2 * T * nb_max * 128) + 8 * 7 + 16 + 32;
+  return al16(slots * 256) + al16(slots * 32) + al16(slots * 4) + al16((size_t)2 * T * nb_max * 128) +
+         al16(2 * sizeof(PhaseDev)) + 8 * 7 + 16 + 32;
 }
 __host__ __device__ __forceinline__ size_t prog_smem_bytes(int T, int nb_max, int stages, int consumers) {
   return (size_t)stages * consumers * kTileBytes + prog_fixed_bytes(T, nb_max, consumers) + (size_t)stages * 16;
@@ -137,6 +141,8 @@ __device__ __forceinline__ PSmem pcarve(uint8_t* base, int T, int nb_max, int st
   o += al16(slots * 4);
   m.terms = reinterpret_cast<float*>(base + o);
   o += al16((size_t)2 * T * nb_max * 128);
+  m.pd = reinterpret_cast<PhaseDev*>(base + o);
+  o += al16(2 * sizeof(PhaseDev));
   m.full = reinterpret_cast<uint64_t*>(base + o);
   m.empty = m.full + stages;
   m.grp = m.empty + stages;
@@ -394,10 +400,10 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1) q2k_program_kernel(const Pr
       mbar_init(&m.full[s], 1);
       mbar_init(&m.empty[s], W);
     }
-    mbar_init(&m.grp[0], W);
-    mbar_init(&m.grp[1], W);
-    mbar_init(&m.tfree[0], 1);
-    mbar_init(&m.tfree[1], 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&m.grp[b], W);
+      mbar_init(&m.tfree[b], 1);
+    }
     mbar_init(m.done, W);
     mbar_init(m.inready, 1);
     mbar_init(m.invready, 1);
@@ -444,32 +450,42 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1) q2k_program_kernel(const Pr
   const ActSmem act = {m.qs, m.bs, m.d};
   int64_t i = 0;  // ring stage, in step with the producer
   int jj = 0;     // row groups processed by this CTA (terms double buffer, finisher rota)
-  int nwait = 0;  // gates passed (inready parity)
+  int nwait = 0;  // phases this CTA took part in (inready parity, descriptor slot)
   int nrms = 0;   // RMSNorm inputs read (invready parity)
   for (int ph = 0; ph < P.n_phases; ++ph) {
-    const PhaseDev& D = P.phases[ph];  // read in place: the fields stay out of registers
-    const int nb = D.nb;
-    const int64_t g0 = cta * D.n_groups / C, g1 = (cta + 1) * D.n_groups / C;
+    const int nb = P.phases[ph].nb;
+    const int64_t ngr = P.phases[ph].n_groups;
+    const int64_t g0 = cta * ngr / C, g1 = (cta + 1) * ngr / C;
     if (g0 == g1) continue;
     const int nchunks = (nb + W - 1) / W;
 
     // phase ph reads phase ph-1's complete output (and, through it, every
-    // earlier phase's): one lane waits, the other warps sleep on inready
-    if (ph > 0) {
-      if (cw == 0) {
-        if (lane == 0 && !wait_count(P.ctr + ph - 1, (unsigned)P.phases[ph - 1].n_groups, abort_word)) {
-          fail(P);
-          *m.gate_fail = 1u;
-        }
-        mbar_arrive_warp(m.inready);
-      }
-      if (!mbar_wait_bounded(m.inready, (unsigned)(nwait & 1), kTimeoutNs)) {
+    // earlier phase's): one lane waits, the other warps sleep on inready.
+    // Meanwhile warp 0 brings the phase's descriptor into shared memory (the
+    // gate's acquire leaves this SM's L1 stale, so reading it in place would
+    // cost an L2 round trip before the first activation load and again in
+    // every finisher).  The slot alternates per phase this CTA takes part
+    // in: the slot written here was last read in the CTA's phase before the
+    // previous one, which ended before the previous gate opened.
+    PhaseDev& Ds = m.pd[nwait & 1];
+    if (cw == 0) {
+      constexpr int kWords = (int)(sizeof(PhaseDev) / 4);
+      static_assert(sizeof(PhaseDev) % 4 == 0 && kWords <= 32, "phase descriptor copy");
+      if (lane < kWords)
+        reinterpret_cast<uint32_t*>(&Ds)[lane] = __ldcg(reinterpret_cast<const uint32_t*>(P.phases + ph) + lane);
+      if (ph > 0 && lane == 0 && !wait_count(P.ctr + ph - 1, (unsigned)P.phases[ph - 1].n_groups, abort_word)) {
         fail(P);
-        return;
+        *m.gate_fail = 1u;
       }
-      ++nwait;
-      if (*reinterpret_cast<volatile unsigned*>(m.gate_fail)) return;
+      mbar_arrive_warp(m.inready);
     }
+    if (!mbar_wait_bounded(m.inready, (unsigned)(nwait & 1), kTimeoutNs)) {
+      fail(P);
+      return;
+    }
+    ++nwait;
+    if (*reinterpret_cast<volatile unsigned*>(m.gate_fail)) return;
+    const PhaseDev& D = Ds;
 
     // one round of loads: the residual of the first row group this warp will
     // finish, and the activation prologue (this warp's super-blocks)
@@ -728,10 +744,11 @@ int q2k_program_create(const ProgPhase* phases, int n_phases, int n_cols, float 
   pr->device = dev;
   pr->counter_words = (int64_t)n + 2;
   pr->parts_bytes = parts;
-  // 8 stages of up to 16 tiles ahead per SM: ~51 MB of the 126 MB L2 in
-  // flight across 148 SMs, several microseconds of HBM streaming per SM --
-  // longer than a phase boundary.  SMEAI_PROGRAM_L2_AHEAD overrides (tuning).
-  pr->l2_ahead = 8;
+  // L2 prefetch of ring stages ahead of the ring loads: off by default
+  // (measured on B200, 7B-shape decode: 0.965 ms per token without, 0.985 ms
+  // with 8 stages ahead -- the ring alone keeps the stream fed, and the extra
+  // requests cost more than they hide).  SMEAI_PROGRAM_L2_AHEAD=n sets it.
+  pr->l2_ahead = 0;
   if (const char* e = getenv("SMEAI_PROGRAM_L2_AHEAD")) pr->l2_ahead = atoi(e) < 0 ? 0 : atoi(e);
   if (cudaMalloc(&pr->d_phases, sizeof(PhaseDev) * (size_t)n) != cudaSuccess ||
       cudaMalloc(&pr->d_ctr, sizeof(unsigned) * (size_t)pr->counter_words) != cudaSuccess ||
