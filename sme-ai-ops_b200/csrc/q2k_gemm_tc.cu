@@ -606,8 +606,13 @@ int q2k_gemm_tc(const Q2KWeight& w, const void* xq, int64_t n_cols, float* y, in
   uint8_t* bq = static_cast<uint8_t*>(scratch);
   uint8_t* bs = bq + (size_t)tiles * nb * 2 * kAtomBytes;
   float* dx = reinterpret_cast<float*>(bs + (size_t)tiles * nb * kMinBytes);
-  // padding tokens of the last tile must read as zero
-  SMEAI_CUDA_TRY(cudaMemsetAsync(bq, 0, (size_t)tiles * nb * (2 * kAtomBytes + kMinBytes), stream));
+  // padding tokens of a partial last tile must read as zero (the prepass
+  // writes every byte of the real tokens' rows)
+  if (n_cols % kTN) {
+    SMEAI_CUDA_TRY(cudaMemsetAsync(bq + (size_t)(tiles - 1) * nb * 2 * kAtomBytes, 0, (size_t)nb * 2 * kAtomBytes,
+                                   stream));
+    SMEAI_CUDA_TRY(cudaMemsetAsync(bs + (size_t)(tiles - 1) * nb * kMinBytes, 0, (size_t)nb * kMinBytes, stream));
+  }
   const int64_t warps = n_cols * nb;
   SMEAI_CUDA_TRY(launch(gemm_prepass_kernel, dim3((unsigned)((warps + 7) / 8)), dim3(256), 0, stream,
                         static_cast<const uint8_t*>(xq), n_cols, nb, bq, bs, dx));
