@@ -72,6 +72,25 @@ def _declare(L: ctypes.CDLL) -> None:
         "smeai_last_error": (ctypes.c_char_p, []),
         "smeai_take_device_error": (I, [ctypes.POINTER(ctypes.c_uint)]),
         "smeai_q2k_repack": (I, [P, I64, I64, ctypes.POINTER(ctypes.c_void_p)]),
+        # smeai_gguf.h
+        "smeai_gguf_open": (I, [ctypes.c_char_p, ctypes.POINTER(ctypes.c_void_p)]),
+        "smeai_gguf_close": (None, [P]),
+        "smeai_gguf_version": (I, [P]),
+        "smeai_gguf_alignment": (U64, [P]),
+        "smeai_gguf_data_offset": (U64, [P]),
+        "smeai_gguf_n_tensors": (I64, [P]),
+        "smeai_gguf_find_tensor": (I64, [P, ctypes.c_char_p]),
+        "smeai_gguf_tensor_info": (I, [P, I64, ctypes.POINTER(ctypes.c_char_p), ctypes.POINTER(I),
+                                       ctypes.POINTER(I), ctypes.POINTER(I64), ctypes.POINTER(U64),
+                                       ctypes.POINTER(U64)]),
+        "smeai_gguf_read_tensor": (I, [P, I64, P, U64]),
+        "smeai_gguf_load_q2k": (I, [P, I64, ctypes.POINTER(ctypes.c_void_p)]),
+        "smeai_gguf_n_kv": (I64, [P]),
+        "smeai_gguf_find_key": (I64, [P, ctypes.c_char_p]),
+        "smeai_gguf_key_type": (I, [P, ctypes.c_char_p]),
+        "smeai_gguf_get_u64": (I, [P, ctypes.c_char_p, ctypes.POINTER(U64)]),
+        "smeai_gguf_get_f64": (I, [P, ctypes.c_char_p, ctypes.POINTER(ctypes.c_double)]),
+        "smeai_gguf_get_str": (I, [P, ctypes.c_char_p, ctypes.POINTER(ctypes.c_char_p)]),
         "smeai_q2k_free": (None, [P]),
         "smeai_q2k_weight_bytes": (SZ, [P]),
         "smeai_q8k_quantize": (I, [P, I64, I64, I64, P, P]),

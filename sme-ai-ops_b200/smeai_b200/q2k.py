@@ -80,6 +80,15 @@ class Q2KMatrix:
         self.handle = handle
         self.bytes = lib().smeai_q2k_weight_bytes(handle)
 
+    @classmethod
+    def from_handle(cls, handle: ctypes.c_void_p, n_rows: int, k: int) -> "Q2KMatrix":
+        """Wrap a weight already in the device tile layout (e.g. smeai_gguf_load_q2k)."""
+        self = cls.__new__(cls)
+        self.n_rows, self.k, self.nb = n_rows, k, k // QK_K
+        self.handle = handle
+        self.bytes = lib().smeai_q2k_weight_bytes(handle)
+        return self
+
     def mul_mat(self, xq: torch.Tensor, n_cols: int, out: torch.Tensor | None = None, epilogue: int = EPI_STORE,
                 resid: torch.Tensor | None = None) -> torch.Tensor:
         out_rows = self.n_rows // 2 if epilogue == EPI_SILU_MUL else self.n_rows
