@@ -169,6 +169,38 @@ int smeai_q2k_block_sums(const void *w_dev, const void *x_q8k_dev, int32_t *isum
 int smeai_q2k_quantize_device(const float *x_dev, int64_t n, void *y_q2k_dev, void *stream);
 int smeai_q2k_dequantize_device(const void *w_q2k_dev, int64_t n, float *y_dev, void *stream);
 
+/* ---------------- 3. Q3_K weights ----------------------------------------
+ * The reference leaves its Q3_K tensors (110 of the TinyLlama Q2_K file's 201,
+ * llama.cpp/doc/SME_Q2K_OPTIMIZATION.md:44-51) on ggml's generic path; these
+ * are that path's entry points on the GPU.  block_q3_K = hmask[32] qs[64]
+ * scales[12] d(fp16) = 110 bytes per 256 weights.  The per-super-block
+ * integer sums equal ggml's exactly; ggml's generic dot then accumulates
+ * floats in 8 position lanes, the GPU in one (ascending super-blocks), so
+ * outputs agree to float rounding (reordered accumulation). */
+
+/* ggml type-trait shapes (host pointers; see group 1 above). */
+void dequantize_row_q3_K(const void *x, float *y, int64_t k);
+void ggml_vec_dot_q3_K_q8_K(int n, float *s, size_t bs, const void *vx, size_t bx, const void *vy, size_t by,
+                            int nrc);
+
+/* Repack n_rows x k of block_q3_K (host or device) into the device tile
+ * layout; the handle is freed with smeai_q3k_free (or smeai_q2k_free). */
+int smeai_q3k_repack(const void *w_q3k, int64_t n_rows, int64_t k, void **w_dev_out);
+void smeai_q3k_free(void *w_dev);
+/* y[c*ldy + r] = row r . activation c for n_cols Q8_K rows (device). */
+int smeai_q3k_mul_mat(const void *w_dev, const void *x_q8k_dev, int64_t n_cols, float *y_dev, size_t ldy,
+                      void *stream);
+/* The same from fp32 activation rows (stride ld_x floats), quantized to Q8_K
+ * inside the kernel, after an RMSNorm when rms_eps >= 0. */
+int smeai_q3k_mul_mat_f32(const void *w_dev, const float *x_dev, size_t ld_x, int64_t n_cols, float *y_dev,
+                          size_t ldy, float rms_eps, void *stream);
+/* Per-(row, super-block) integer sums for one activation row: isum (ggml's
+ * integer total) and summs = sum_j (scale_j - 32) * bsums_j, [n_rows][nb]. */
+int smeai_q3k_block_sums(const void *w_dev, const void *x_q8k_dev, int32_t *isum_dev, int32_t *summs_dev,
+                         void *stream);
+/* Device decode of n weights (n/256 blocks) to fp32. */
+int smeai_q3k_dequantize_device(const void *w_q3k_dev, int64_t n, float *y_dev, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -21,11 +21,14 @@ LIB_PATH = os.path.join(HERE, "_build", "libsmeai_oracle.so")
 QK_K = 256
 BLOCK_Q2_K = np.dtype([("scales", np.uint8, 16), ("qs", np.uint8, 64),
                        ("d", np.uint16), ("dmin", np.uint16)])
+BLOCK_Q3_K = np.dtype([("hmask", np.uint8, 32), ("qs", np.uint8, 64), ("scales", np.uint8, 12),
+                       ("d", np.uint16)])
 BLOCK_Q8_K = np.dtype([("d", np.float32), ("qs", np.int8, 256), ("bsums", np.int16, 16)])
-assert BLOCK_Q2_K.itemsize == 84 and BLOCK_Q8_K.itemsize == 292
+assert BLOCK_Q2_K.itemsize == 84 and BLOCK_Q3_K.itemsize == 110 and BLOCK_Q8_K.itemsize == 292
 
 ROUND_FUSED, ROUND_SEPARATE = 0, 1
 COMBINE_FUSED, COMBINE_SEPARATE = 0, 1
+Q3K_GGML, Q3K_BLOCK_ORDER = 0, 1
 ACT_NONE, ACT_RELU, ACT_GELU, ACT_SILU = 0, 1, 2, 3
 
 _lib = None
@@ -61,6 +64,11 @@ def lib() -> ctypes.CDLL:
             "orc_q2k_block_sums": (None, [I, P, P, P, P]),
             "orc_vec_dot_q2_K_q8_K": (F, [I, P, P, I]),
             "orc_q2k_mul_mat": (None, [P, I64, I64, P, I64, P, I64, I, I]),
+            "orc_q3k_scales": (None, [P, P]),
+            "orc_dequantize_row_q3_K": (None, [P, P, I64]),
+            "orc_q3k_block_sums": (None, [I, P, P, P]),
+            "orc_vec_dot_q3_K_q8_K": (F, [I, P, P, I]),
+            "orc_q3k_mul_mat": (None, [P, I64, I64, P, I64, P, I64, I, I]),
             "orc_rms_inv": (F, [P, I64, F]),
             "orc_rms_sumsq": (F, [P, I64]),
             "orc_rmsnorm_quantize_q8_K": (None, [P, P, I64, F, I]),
@@ -169,6 +177,52 @@ def q2k_block_sums(wrow: np.ndarray, xq: np.ndarray):
 def vec_dot_q2_K_q8_K(wrow, xq, combine=COMBINE_FUSED) -> float:
     wrow, xq = np.ascontiguousarray(wrow), np.ascontiguousarray(xq)
     return lib().orc_vec_dot_q2_K_q8_K(wrow.size * QK_K, _p(wrow), _p(xq), combine)
+
+
+def random_q3_K(rng, n_blocks: int) -> np.ndarray:
+    """Valid Q3_K blocks of random bits (every bit pattern of hmask, qs and
+    scales is a valid block) with d a positive normal fp16 of the magnitude a
+    quantized N(0, 0.02) weight has (parity is defined on identical blocks,
+    so the quantizer's search is not needed)."""
+    b = rng.integers(0, 256, size=(n_blocks, 110), dtype=np.uint8)
+    d = (np.abs(rng.standard_normal(n_blocks)) * 0.0005 + 1e-5).astype(np.float16)
+    b[:, 108:110] = d.view(np.uint8).reshape(-1, 2)
+    return b.reshape(-1).view(BLOCK_Q3_K)
+
+
+def q3k_scales(block) -> np.ndarray:
+    block = np.ascontiguousarray(np.asarray(block).reshape(1))
+    out = np.empty(16, np.int8)
+    lib().orc_q3k_scales(_p(block), _p(out))
+    return out
+
+
+def dequantize_q3_K(blocks: np.ndarray) -> np.ndarray:
+    blocks = np.ascontiguousarray(blocks)
+    out = np.empty(blocks.size * QK_K, np.float32)
+    lib().orc_dequantize_row_q3_K(_p(blocks), _p(out), out.size)
+    return out
+
+
+def q3k_block_sums(wrow: np.ndarray, xq: np.ndarray) -> np.ndarray:
+    wrow, xq = np.ascontiguousarray(wrow), np.ascontiguousarray(xq)
+    isum = np.empty(wrow.size, np.int32)
+    lib().orc_q3k_block_sums(wrow.size * QK_K, _p(wrow), _p(xq), _p(isum))
+    return isum
+
+
+def vec_dot_q3_K_q8_K(wrow, xq, order=Q3K_GGML) -> float:
+    wrow, xq = np.ascontiguousarray(wrow), np.ascontiguousarray(xq)
+    return lib().orc_vec_dot_q3_K_q8_K(wrow.size * QK_K, _p(wrow), _p(xq), order)
+
+
+def q3k_mul_mat(w: np.ndarray, n_rows: int, k: int, xq: np.ndarray, n_cols: int, order=Q3K_GGML,
+                n_threads: int = 1) -> np.ndarray:
+    """Returns y[n_cols, n_rows] (ggml dst layout)."""
+    w, xq = np.ascontiguousarray(w), np.ascontiguousarray(xq)
+    y = np.empty((n_cols, n_rows), np.float32)
+    lib().orc_q3k_mul_mat(_p(w), n_rows, k, _p(xq), n_cols, _p(y), n_rows, order, n_threads)
+    return y
 
 
 def q2k_mul_mat(w: np.ndarray, n_rows: int, k: int, xq: np.ndarray, n_cols: int,

@@ -526,6 +526,113 @@ void orc_q2k_mul_mat(const orc_block_q2_K *w, int64_t n_rows, int64_t k,
 }
 
 /* ======================================================================== */
+/* Q3_K (ggml 0.9.8 generic C; the reference leaves its 110 Q3_K tensors on  */
+/* that path, llama.cpp/doc/SME_Q2K_OPTIMIZATION.md:44-51).  A weight is     */
+/* d * (scale_j - 32) * q with q = low 2 bits - (high bit clear ? 4 : 0),    */
+/* q in [-4, 3]; the 2-bit planes and sub-block order are Q2_K's, the high   */
+/* bit of quant (half h, plane s, byte l) is bit 4h+s of hmask[l].           */
+/* ======================================================================== */
+
+/* The 16 scales minus 32 from the 12 packed bytes: scales 0-7 take their low
+ * 4 bits from the nibbles of bytes 0-7 (low nibbles first), scales 8-15 from
+ * the high nibbles; the top 2 bits come from bytes 8-11, two per scale. */
+void orc_q3k_scales(const orc_block_q3_K *x, int8_t sc[16]) {
+    for (int j = 0; j < 16; ++j) {
+        int lo = (j < 8) ? (x->scales[j] & 0xF) : (x->scales[j - 8] >> 4);
+        int hi = (x->scales[8 + (j % 4)] >> (2 * (j / 4))) & 3;
+        sc[j] = (int8_t) ((lo | (hi << 4)) - 32);
+    }
+}
+
+static int orc_q3k_quant(const orc_block_q3_K *x, int i) {
+    int half = i / 128, within = i % 128, shift = within / 32, l = within % 32;
+    int q = (x->qs[half * 32 + l] >> (2 * shift)) & 3;
+    int hbit = (x->hmask[l] >> (4 * half + shift)) & 1;
+    return q - (hbit ? 0 : 4);
+}
+
+void orc_dequantize_row_q3_K(const orc_block_q3_K *x, float *y, int64_t k) {
+    int64_t nb = k / ORC_QK_K;
+    for (int64_t b = 0; b < nb; ++b) {
+        int8_t sc[16];
+        orc_q3k_scales(x + b, sc);
+        float d = orc_half_to_float(x[b].d);
+        for (int i = 0; i < ORC_QK_K; ++i) {
+            float dl = d * (float) sc[i / 16];
+            y[b * ORC_QK_K + i] = dl * (float) orc_q3k_quant(x + b, i);
+        }
+    }
+}
+
+/* Per super-block: isum = sum_j (scale_j - 32) * sum_{i in j} q_i * q8_i. */
+void orc_q3k_block_sums(int n, const orc_block_q3_K *x, const orc_block_q8_K *y, int32_t *isum) {
+    int nb = n / ORC_QK_K;
+    for (int b = 0; b < nb; ++b) {
+        int8_t sc[16];
+        orc_q3k_scales(x + b, sc);
+        int32_t acc = 0;
+        for (int j = 0; j < 16; ++j) {
+            int32_t s = 0;
+            for (int i = 16 * j; i < 16 * j + 16; ++i) s += (int32_t) y[b].qs[i] * orc_q3k_quant(x + b, i);
+            acc += (int32_t) sc[j] * s;
+        }
+        isum[b] = acc;
+    }
+}
+
+/*
+ * ggml_vec_dot_q3_K_q8_K, generic C (order = ORC_Q3K_GGML): the integer
+ * products go to 8 lanes by position mod 8, aux32[l] = sum over the block of
+ * (scale_j - 32) * q_i * q8_i for i = l (mod 8); per block
+ * d = fp32(d_x) * d_y and sums[l] += d * aux32[l] (one fused multiply-add,
+ * what GCC's default contraction forms on an FMA target); the result is
+ * sums[0] + sums[1] + ... + sums[7].  order = ORC_Q3K_BLOCK_ORDER: the GPU
+ * kernels' combine, sumf += (fp32(d_x) * d_y) * isum per block in ascending
+ * order (the same integers, one float accumulator).
+ */
+float orc_vec_dot_q3_K_q8_K(int n, const orc_block_q3_K *x, const orc_block_q8_K *y, int order) {
+    int nb = n / ORC_QK_K;
+    if (order == ORC_Q3K_BLOCK_ORDER) {
+        float sumf = 0.0f;
+        for (int b = 0; b < nb; ++b) {
+            int32_t isum;
+            orc_q3k_block_sums(ORC_QK_K, x + b, y + b, &isum);
+            const float d = orc_half_to_float(x[b].d) * y[b].d;
+            sumf = sumf + d * (float) isum;
+        }
+        return sumf;
+    }
+    float sums[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    for (int b = 0; b < nb; ++b) {
+        int8_t sc[16];
+        orc_q3k_scales(x + b, sc);
+        int32_t aux32[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+        for (int j = 0; j < 16; ++j)
+            for (int i = 16 * j; i < 16 * j + 16; ++i)
+                aux32[i % 8] += (int32_t) sc[j] * ((int32_t) y[b].qs[i] * orc_q3k_quant(x + b, i));
+        const float d = orc_half_to_float(x[b].d) * y[b].d;
+        for (int l = 0; l < 8; ++l) sums[l] = fmaf(d, (float) aux32[l], sums[l]);
+    }
+    float sumf = 0.0f;
+    for (int l = 0; l < 8; ++l) sumf += sums[l];
+    return sumf;
+}
+
+void orc_q3k_mul_mat(const orc_block_q3_K *w, int64_t n_rows, int64_t k,
+                     const orc_block_q8_K *xq, int64_t n_cols, float *y, int64_t ldy,
+                     int order, int n_threads) {
+    int64_t nb = k / ORC_QK_K;
+#ifdef _OPENMP
+    if (n_threads < 1) n_threads = 1;
+#pragma omp parallel for schedule(static) num_threads(n_threads)
+#endif
+    for (int64_t r = 0; r < n_rows; ++r)
+        for (int64_t c = 0; c < n_cols; ++c)
+            y[c * ldy + r] = orc_vec_dot_q3_K_q8_K((int) k, w + r * nb, xq + c * nb, order);
+    (void) n_threads;
+}
+
+/* ======================================================================== */
 /* Decode-stack helpers (RMSNorm is the reference's sme_ai_rmsnorm_f32,      */
 /* sme_ai_ops.c:1060-1092: y = x / sqrt(mean(x^2) + eps)).  The sum of       */
 /* squares is taken in the fixed order the GPU kernels use, so both sides    */

@@ -42,6 +42,14 @@ typedef struct {
     uint16_t dmin;      /* fp16 super-block scale for mins                 */
 } orc_block_q2_K;
 
+/* ggml block_q3_K: 110 bytes per 256 weights (gguf/constants.py, Q3_K). */
+typedef struct {
+    uint8_t hmask[32];  /* high bit of each 3-bit quant                   */
+    uint8_t qs[64];     /* low 2 bits, 4 per byte (the Q2_K bit order)     */
+    uint8_t scales[12]; /* 16 6-bit scales                                 */
+    uint16_t d;         /* fp16 super-block scale                          */
+} orc_block_q3_K;
+
 /* ggml block_q8_K: 292 bytes per 256 activations (gguf/constants.py:4246). */
 typedef struct {
     float d;
@@ -95,6 +103,17 @@ float orc_vec_dot_q2_K_q8_K(int n, const orc_block_q2_K *x, const orc_block_q8_K
 void orc_q2k_mul_mat(const orc_block_q2_K *w, int64_t n_rows, int64_t k,
                      const orc_block_q8_K *xq, int64_t n_cols, float *y, int64_t ldy,
                      int combine, int n_threads);
+
+/* Q3_K: ggml's generic decode and dot (8 float lanes over positions mod 8),
+ * the per-super-block integer sum, and the block-order combine of the GPU. */
+enum { ORC_Q3K_GGML = 0, ORC_Q3K_BLOCK_ORDER = 1 };
+void orc_q3k_scales(const orc_block_q3_K *x, int8_t sc[16]);      /* scale - 32 */
+void orc_dequantize_row_q3_K(const orc_block_q3_K *x, float *y, int64_t k);
+void orc_q3k_block_sums(int n, const orc_block_q3_K *x, const orc_block_q8_K *y, int32_t *isum);
+float orc_vec_dot_q3_K_q8_K(int n, const orc_block_q3_K *x, const orc_block_q8_K *y, int order);
+void orc_q3k_mul_mat(const orc_block_q3_K *w, int64_t n_rows, int64_t k,
+                     const orc_block_q8_K *xq, int64_t n_cols, float *y, int64_t ldy,
+                     int order, int n_threads);
 
 /* ---------------- decode-stack helpers ---------------- */
 float orc_rms_group_sumsq(const float *x);      /* one 32-value group */

@@ -24,7 +24,12 @@ int q2k_dequantize(const void* w, int64_t k_total, float* y, cudaStream_t stream
 constexpr int kRowsPerGroup = 32;
 constexpr int kTileBytes = 32 * 84;
 
+// Weight formats held in the tile layout (tile bytes per 32-row group and
+// super-block: Q2_K 2688, Q3_K 3584 -- see q3k_core.cuh).
+enum WeightFmt : int { kFmtQ2K = 0, kFmtQ3K = 1 };
+
 struct Q2KWeight {
+  int fmt = kFmtQ2K;
   int64_t n_rows = 0;
   int64_t k = 0;
   int nb = 0;           // super-blocks per row
@@ -39,6 +44,13 @@ int q2k_repack(const void* w_blocks_dev, int64_t n_rows, int64_t k, Q2KWeight* o
 size_t q2k_tile_bytes(int64_t n_rows, int64_t k);
 int q2k_repack_into(const void* w_blocks_dev, int64_t n_rows, int64_t k, uint8_t* tiles, Q2KWeight* out,
                     cudaStream_t stream);
+
+// ---- Q3_K weights (q3k_quant.cu): ggml blocks -> tiles, decode ----
+size_t q3k_tile_bytes(int64_t n_rows, int64_t k);
+int q3k_repack_into(const void* w_blocks_dev, int64_t n_rows, int64_t k, uint8_t* tiles, Q2KWeight* out,
+                    cudaStream_t stream);
+int q3k_repack(const void* w_blocks_dev, int64_t n_rows, int64_t k, Q2KWeight* out, cudaStream_t stream);
+int q3k_dequantize(const void* w, int64_t k_total, float* y, cudaStream_t stream);
 
 enum Epilogue : int {
   kEpiStore = 0,     // y[c*ldy + r] = acc

@@ -578,8 +578,8 @@ size_t q2k_gemm_scratch_bytes(int64_t n_cols, int nb) {
 
 int q2k_gemm_tc(const Q2KWeight& w, const void* xq, int64_t n_cols, float* y, int64_t ldy, void* scratch,
                 size_t scratch_bytes, cudaStream_t stream) {
-  if (!w.tiles || !xq || !y || n_cols <= 0 || ldy < w.n_rows) {
-    set_last_error("q2k_gemm_tc: bad arguments");
+  if (!w.tiles || !xq || !y || n_cols <= 0 || ldy < w.n_rows || w.fmt != kFmtQ2K) {
+    set_last_error("q2k_gemm_tc: bad arguments (a Q2_K weight is required)");
     return kBadArgument;
   }
   if (reinterpret_cast<uintptr_t>(xq) & 3) {

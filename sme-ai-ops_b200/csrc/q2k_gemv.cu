@@ -34,6 +34,7 @@
 #include "kernels.h"
 #include "q8k_device.cuh"
 #include "q2k_core.cuh"
+#include "q3k_core.cuh"
 
 #include <stdio.h>
 #include <stdlib.h>
@@ -68,7 +69,7 @@ struct GemvParams {
 
 // Shared-memory carve-up for T tokens (16-byte aligned pieces).
 struct Smem {
-  uint8_t* ring;   // [stages][kTileBytes]
+  uint8_t* ring;   // [stages][consumers][tile bytes of the weight format]
   int4* qs;        // [T*nb][16]  256 int8 per block
   int* bs;         // [T*nb][8]   16 int16 bsums per block
   float* d;        // [T*nb]
@@ -87,15 +88,15 @@ __host__ __device__ __forceinline__ size_t smem_fixed_bytes(int T, int nb) {
   return align16((size_t)T * nb * 256) + align16((size_t)T * nb * 32) + align16((size_t)T * nb * 4) +
          align16((size_t)T * (8 * nb + 1) * 4) + align16((size_t)2 * T * nb * 128) + 8 * 6;
 }
-__host__ __device__ __forceinline__ size_t smem_total_bytes(int T, int nb, int stages, int consumers) {
-  return (size_t)stages * consumers * kTileBytes + smem_fixed_bytes(T, nb) + (size_t)stages * 16;
+__host__ __device__ __forceinline__ size_t smem_total_bytes(int T, int nb, int stages, int consumers, int tile) {
+  return (size_t)stages * consumers * tile + smem_fixed_bytes(T, nb) + (size_t)stages * 16;
 }
 
-__device__ __forceinline__ Smem carve(uint8_t* base, int T, int nb, int stages, int consumers) {
+__device__ __forceinline__ Smem carve(uint8_t* base, int T, int nb, int stages, int consumers, int tile) {
   Smem m;
   size_t o = 0;
   m.ring = base;
-  o += (size_t)stages * consumers * kTileBytes;
+  o += (size_t)stages * consumers * tile;
   m.qs = reinterpret_cast<int4*>(base + o);
   o += align16((size_t)T * nb * 256);
   m.bs = reinterpret_cast<int*>(base + o);
@@ -158,7 +159,9 @@ __device__ __forceinline__ void finish_group(const float* terms, int nb, int64_t
   }
 }
 
-template <int T, int EPI, int IN, bool SUMS>
+// F: the weight format (FmtQ2K, FmtQ3K in q3k_core.cuh) -- tile size, the
+// lane's block load and the integer core; everything else is shared.
+template <class F, int T, int EPI, int IN, bool SUMS>
 __global__ void __launch_bounds__(kMaxThreads) q2k_gemv_kernel(const GemvParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -171,8 +174,9 @@ __global__ void __launch_bounds__(kMaxThreads) q2k_gemv_kernel(const GemvParams 
   // group (fewer in the group's last chunk); consumer warp w takes block w of it
   const int nchunks = (nb + kConsumers - 1) / kConsumers;
   const int n_stages = ng * nchunks;
-  const int stage_bytes = kConsumers * kTileBytes;
-  const Smem m = carve(smem, T, nb, S, kConsumers);
+  constexpr int kTile = F::kTile;
+  const int stage_bytes = kConsumers * kTile;
+  const Smem m = carve(smem, T, nb, S, kConsumers, kTile);
   const ActSmem act = {m.qs, m.bs, m.d};
 
   if (threadIdx.x == 0) {
@@ -194,7 +198,7 @@ __global__ void __launch_bounds__(kMaxThreads) q2k_gemv_kernel(const GemvParams 
   if (warp == 0) {
     // ---- producer: stream this CTA's tiles (independent of earlier kernels)
     if (lane == 0) {
-      const uint8_t* src = p.tiles + g0 * nb * (int64_t)kTileBytes;
+      const uint8_t* src = p.tiles + g0 * nb * (int64_t)kTile;
       int i = 0;
       bool ok = true;
       for (; i < n_stages; ++i) {
@@ -205,9 +209,9 @@ __global__ void __launch_bounds__(kMaxThreads) q2k_gemv_kernel(const GemvParams 
         }
         const int j = i / nchunks, c = i - j * nchunks;
         const int nblk = min(kConsumers, nb - c * kConsumers);
-        mbar_arrive_expect_tx(&m.full[s], (unsigned)(nblk * kTileBytes));
-        bulk_copy_g2s(m.ring + (size_t)s * stage_bytes, src + ((size_t)j * nb + (size_t)c * kConsumers) * kTileBytes,
-                      (unsigned)(nblk * kTileBytes), &m.full[s]);
+        mbar_arrive_expect_tx(&m.full[s], (unsigned)(nblk * kTile));
+        bulk_copy_g2s(m.ring + (size_t)s * stage_bytes, src + ((size_t)j * nb + (size_t)c * kConsumers) * kTile,
+                      (unsigned)(nblk * kTile), &m.full[s]);
       }
       if (!ok) {
         raise_device_error(p.err, kDevErrTimeout);
@@ -297,10 +301,10 @@ __global__ void __launch_bounds__(kMaxThreads) q2k_gemv_kernel(const GemvParams 
         mbar_arrive_warp(&m.empty[s]);
         continue;
       }
-      const uint8_t* tile = m.ring + (size_t)s * stage_bytes + (size_t)cw * kTileBytes;
-      const WBlock wb = load_wblock(tile, lane);
-      mbar_arrive_warp(&m.empty[s], wblock_dep(wb));
-      block_terms<T, SUMS>(wb, act, b, nb, nb, b, terms, lane, row, p.n_rows, p.isum_out, p.summs_out);
+      const uint8_t* tile = m.ring + (size_t)s * stage_bytes + (size_t)cw * kTile;
+      const typename F::Block wb = F::load(tile, lane);
+      mbar_arrive_warp(&m.empty[s], F::dep(wb));
+      F::template terms<T, SUMS>(wb, act, b, nb, nb, b, terms, lane, row, p.n_rows, p.isum_out, p.summs_out);
     }
     if constexpr (!SUMS) {
       mbar_arrive_warp(&m.grp[buf]);
@@ -376,7 +380,7 @@ struct Plan {
 // two that fits in the CTA's share of shared memory (half the SM for one CTA,
 // so the next kernel's CTA can be resident during the tail).  The override
 // SMEAI_GEMV_PLAN="ctas_per_sm,consumers,stages" exists for tuning sweeps.
-Plan plan_for(int T, int nb, int64_t n_groups) {
+Plan plan_for(int T, int nb, int64_t n_groups, int tile = kTileBytes) {
   const int sms = num_sms();
   Plan pl;
   if (n_groups < 6 * sms) pl = {1, 16, 0};
@@ -392,7 +396,7 @@ Plan plan_for(int T, int nb, int64_t n_groups) {
   if (ov[1] > 0 && ov[1] <= kMaxConsumers) pl.consumers = ov[1];
   const size_t fixed = smem_fixed_bytes(T, nb);
   const size_t budget = (size_t)kSmemLimit / (size_t)(pl.ctas_per_sm < 2 ? 2 : pl.ctas_per_sm);
-  const size_t stage = (size_t)pl.consumers * kTileBytes + 16;
+  const size_t stage = (size_t)pl.consumers * tile + 16;
   const int cap = pl.ctas_per_sm == 1 ? 16 : 8;
   for (int s = cap; s >= 2; s >>= 1)
     if ((ov[2] <= 0 || s <= ov[2]) && fixed + (size_t)s * stage <= budget) {
@@ -409,12 +413,12 @@ Plan plan_for(int T, int nb, int64_t n_groups) {
   return pl;
 }
 
-int plan_stages(int T, int nb) { return plan_for(T, nb, 1).stages; }
+int plan_stages(int T, int nb, int tile) { return plan_for(T, nb, 1, tile).stages; }
 
-template <int T, int EPI, int IN, bool SUMS>
+template <class F, int T, int EPI, int IN, bool SUMS>
 int launch_gemv(const Q2KWeight& w, GemvParams p, cudaStream_t stream) {
-  auto kern = q2k_gemv_kernel<T, EPI, IN, SUMS>;
-  const Plan pl = plan_for(T, w.nb, w.n_groups);
+  auto kern = q2k_gemv_kernel<F, T, EPI, IN, SUMS>;
+  const Plan pl = plan_for(T, w.nb, w.n_groups, F::kTile);
   if (pl.stages <= 0) {
     set_last_error("q2k_gemv: k=%lld too large for %d tokens per launch", (long long)w.k, T);
     return kBadArgument;
@@ -427,7 +431,7 @@ int launch_gemv(const Q2KWeight& w, GemvParams p, cudaStream_t stream) {
     set_last_error("q2k_gemv: device error word unavailable");
     return kCudaError;
   }
-  const size_t smem = smem_total_bytes(T, w.nb, pl.stages, pl.consumers);
+  const size_t smem = smem_total_bytes(T, w.nb, pl.stages, pl.consumers, F::kTile);
   static unsigned configured = 0;  // per template instance, one bit per device
   int dev = 0;
   SMEAI_CUDA_TRY(cudaGetDevice(&dev));
@@ -441,23 +445,30 @@ int launch_gemv(const Q2KWeight& w, GemvParams p, cudaStream_t stream) {
   return kOk;
 }
 
-template <int EPI, int IN>
+template <class F, int EPI, int IN>
 int dispatch_t(int T, const Q2KWeight& w, const GemvParams& p, cudaStream_t s) {
   switch (T) {
-    case 1: return launch_gemv<1, EPI, IN, false>(w, p, s);
-    case 2: return launch_gemv<2, EPI, IN, false>(w, p, s);
-    case 4: return launch_gemv<4, EPI, IN, false>(w, p, s);
-    case 8: return launch_gemv<8, EPI, IN, false>(w, p, s);
+    case 1: return launch_gemv<F, 1, EPI, IN, false>(w, p, s);
+    case 2: return launch_gemv<F, 2, EPI, IN, false>(w, p, s);
+    case 4: return launch_gemv<F, 4, EPI, IN, false>(w, p, s);
+    case 8: return launch_gemv<F, 8, EPI, IN, false>(w, p, s);
     default: return kBadArgument;
   }
 }
 
 template <int IN>
 int dispatch_epi(int epi, int T, const Q2KWeight& w, const GemvParams& p, cudaStream_t s) {
+  if (w.fmt == kFmtQ3K) {  // Q3_K weights: the store epilogue
+    if (epi != kEpiStore) {
+      set_last_error("q3k_gemv: only the store epilogue is built for Q3_K weights");
+      return kBadArgument;
+    }
+    return dispatch_t<FmtQ3K, kEpiStore, IN>(T, w, p, s);
+  }
   switch (epi) {
-    case kEpiStore: return dispatch_t<kEpiStore, IN>(T, w, p, s);
-    case kEpiResidual: return dispatch_t<kEpiResidual, IN>(T, w, p, s);
-    case kEpiSiluMul: return dispatch_t<kEpiSiluMul, IN>(T, w, p, s);
+    case kEpiStore: return dispatch_t<FmtQ2K, kEpiStore, IN>(T, w, p, s);
+    case kEpiResidual: return dispatch_t<FmtQ2K, kEpiResidual, IN>(T, w, p, s);
+    case kEpiSiluMul: return dispatch_t<FmtQ2K, kEpiSiluMul, IN>(T, w, p, s);
     default:
       set_last_error("q2k_gemv: unknown epilogue %d", epi);
       return kBadArgument;
@@ -543,7 +554,7 @@ int q2k_gemv_any(const Q2KWeight& w, int in_mode, const void* x, int64_t ld_x, f
   for (int64_t c0 = 0; c0 < n_cols;) {
     const int64_t rem = n_cols - c0;
     int T = rem >= 8 ? 8 : (rem >= 4 ? 4 : (rem >= 2 ? 2 : 1));
-    while (T > 1 && plan_stages(T, w.nb) <= 0) T >>= 1;
+    while (T > 1 && plan_stages(T, w.nb, w.fmt == kFmtQ3K ? kQ3KTileBytes : kTileBytes) <= 0) T >>= 1;
     GemvParams p = {};
     p.tiles = w.tiles;
     p.nb = w.nb;
@@ -589,7 +600,8 @@ int q2k_block_sums(const Q2KWeight& w, const void* xq, int32_t* isum, int32_t* s
   p.x = xq;
   p.isum_out = isum;
   p.summs_out = summs;
-  return launch_gemv<1, kEpiStore, kInQ8K, true>(w, p, stream);
+  if (w.fmt == kFmtQ3K) return launch_gemv<FmtQ3K, 1, kEpiStore, kInQ8K, true>(w, p, stream);
+  return launch_gemv<FmtQ2K, 1, kEpiStore, kInQ8K, true>(w, p, stream);
 }
 
 }  // namespace smeai

@@ -629,8 +629,8 @@ int q2k_program_create(const ProgPhase* phases, int n_phases, int n_cols, float 
   int nb_max = 0;
   for (int p = 0; p < n; ++p) {
     const ProgPhase& s = phases[p];
-    if (!s.w || !s.w->tiles || !s.x || !s.y || s.w->device != dev) {
-      set_last_error("q2k_program: phase %d: missing weight, input or output (or weight on another device)", p);
+    if (!s.w || !s.w->tiles || !s.x || !s.y || s.w->device != dev || s.w->fmt != kFmtQ2K) {
+      set_last_error("q2k_program: phase %d: missing weight, input or output (or a weight on another device, or not Q2_K)", p);
       return kBadArgument;
     }
     const Q2KWeight& w = *s.w;

@@ -63,6 +63,14 @@ class GGUFFile:
         check(lib().smeai_gguf_load_q2k(self.handle, t.index, ctypes.byref(h)), f"gguf_load_q2k({name})")
         return Q2KMatrix.from_handle(h, t.shape[1], t.shape[0])
 
+    def load_q3k(self, name: str):
+        """A 2-D Q3_K tensor as a device Q3KMatrix."""
+        from .q2k import Q3KMatrix
+        t = self.by_name[name]
+        h = ctypes.c_void_p()
+        check(lib().smeai_gguf_load_q3k(self.handle, t.index, ctypes.byref(h)), f"gguf_load_q3k({name})")
+        return Q3KMatrix(None, t.shape[1], t.shape[0], handle=h)
+
     def key_type(self, key: str) -> int:
         return lib().smeai_gguf_key_type(self.handle, key.encode())
 

@@ -10,6 +10,12 @@ q2k_gguf.npz
     of this repository that pins the block layout (scales/mins nibbles, 2-bit
     packing order, fp16 d/dmin).
 
+q3k_gguf.npz
+    Q3_K blocks (random hmask/qs/scales bits with seeded positive fp16 d,
+    plus an all-zero block and a block with every field at its extremes) and
+    their fp32 decoding by gguf-py 0.19.0 ``Q3_K.dequantize_blocks`` -- pins
+    the 6-bit scale packing, the high-bit mask order and the -4 offset.
+
 demo_linear.npz
     The reference example examples/demo_linear.c:16-34 (batch 2, 16 -> 16,
     inputs k%7-3 times 1/8, weights k%11-5 times 1/16, bias k%5-2 times 1/32).
@@ -66,6 +72,22 @@ def make_q2k():
     np.savez_compressed(os.path.join(HERE, "q2k_gguf.npz"), blocks=blocks, dequant=deq, source=np.array(w))
 
 
+def make_q3k():
+    from gguf.quants import Q3_K
+    rng = np.random.default_rng(20240602)
+    blocks = O.random_q3_K(rng, 64).view(np.uint8).reshape(-1, 110).copy()
+    zero = np.zeros((1, 110), np.uint8)
+    ext = np.zeros((1, 110), np.uint8)
+    ext[0, :32] = 0x00          # every high bit clear: q = low bits - 4
+    ext[0, 32:96] = 0xFF        # low bits 3
+    ext[0, 96:104] = np.array([0x00, 0xFF, 0x0F, 0xF0] * 2, np.uint8)
+    ext[0, 104:108] = np.array([0x00, 0xFF, 0x1B, 0xE4], np.uint8)
+    ext[0, 108:110] = np.frombuffer(np.float16(0.125).tobytes(), np.uint8)
+    blocks = np.concatenate([blocks, zero, ext], axis=0)
+    deq = Q3_K.dequantize_blocks(blocks).astype(np.float32).reshape(-1)
+    np.savez_compressed(os.path.join(HERE, "q3k_gguf.npz"), blocks=blocks, dequant=deq)
+
+
 def make_demo_linear():
     B, K, N = 2, 16, 16
     x = np.array([((i % 7) - 3) * 0.125 for i in range(B * K)], np.float32)
@@ -94,6 +116,7 @@ def make_lcg():
 if __name__ == "__main__":
     O.build()
     make_q2k()
+    make_q3k()
     make_demo_linear()
     make_lcg()
     print("fixtures written to", HERE)
