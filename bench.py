@@ -61,7 +61,7 @@ def parse_args():
     ap.add_argument("--gemv-rows", type=int, default=4096, help="gemv workload: weight rows")
     ap.add_argument("--gemv-k", type=int, default=4096, help="gemv workload: row length")
     ap.add_argument("--gemv-epilogue", type=int, default=0, help="gemv workload: 0 store, 1 residual, 2 silu*mul")
-    ap.add_argument("--gemv-fmt", choices=["q2k", "q3k"], default="q2k", help="gemv workload: weight format")
+    ap.add_argument("--gemv-fmt", choices=["q2k", "q3k", "q6k"], default="q2k", help="gemv workload: weight format")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="bounded CPU sample length")
     return ap.parse_args()
@@ -274,7 +274,8 @@ def gemv_roofline(gemvs, stream, dev, peak, peak_kind):
     tot_b, tot_ms = 0, 0.0
     for name, m, a, b in evs:
         d = a.elapsed_time(b)
-        nbytes = gemv_bytes(m.n_rows, m.k, 1) + (m.n_rows * m.nb * (110 - 84) if isinstance(m, Q.Q3KMatrix) else 0)
+        extra = 110 - 84 if isinstance(m, Q.Q3KMatrix) else (210 - 84 if isinstance(m, Q.Q6KMatrix) else 0)
+        nbytes = gemv_bytes(m.n_rows, m.k, 1) + m.n_rows * m.nb * extra
         agg = per.setdefault(name, [0, 0.0, 0])
         agg[0] += nbytes
         agg[1] += d
@@ -369,24 +370,25 @@ def run_ours(args):
         gemvs = stack.gemv_list()
     else:
         rows, k, epi = args.gemv_rows, args.gemv_k, args.gemv_epilogue
-        q3 = args.gemv_fmt == "q3k"
-        blk_bytes = 110 if q3 else 84
+        q3 = args.gemv_fmt in ("q3k", "q6k")          # the generic-path formats (store epilogue)
+        blk_bytes = {"q2k": 84, "q3k": 110, "q6k": 210}[args.gemv_fmt]
         mbytes = rows * (k // 256) * blk_bytes
         copies = max(4, min(64, -(-4 * 126 * 2**20 // mbytes)))   # > 4x L2 of distinct weights
         g = torch.Generator(device=dev).manual_seed(0)
         if q3:
-            # Q3_K blocks of random bits with the magnitude of a quantized N(0, 0.02) weight
-            # (this library has no Q3_K quantizer; the GEMV's work does not depend on the values)
+            # blocks of random bits with a small positive fp16 d (this library has no Q3_K /
+            # Q6_K quantizer; the GEMV's work does not depend on the values)
             import numpy as np
             rng = np.random.default_rng(0)
-            def q3_blocks():
-                b = rng.integers(0, 256, size=(rows * (k // 256), 110), dtype=np.uint8)
+            cls = Q.Q3KMatrix if args.gemv_fmt == "q3k" else Q.Q6KMatrix
+            def q_blocks():
+                b = rng.integers(0, 256, size=(rows * (k // 256), blk_bytes), dtype=np.uint8)
                 d = (np.abs(rng.standard_normal(b.shape[0])) * 0.0005 + 1e-5).astype(np.float16)
-                b[:, 108:110] = d.view(np.uint8).reshape(-1, 2)
+                b[:, blk_bytes - 2:] = d.view(np.uint8).reshape(-1, 2)
                 return torch.from_numpy(b.reshape(-1)).to(dev)
-            mats = [Q.Q3KMatrix(q3_blocks(), rows, k) for _ in range(copies)]
+            mats = [cls(q_blocks(), rows, k) for _ in range(copies)]
             if epi != 0:
-                raise SystemExit("--gemv-fmt q3k runs the store epilogue only")
+                raise SystemExit("--gemv-fmt q3k/q6k run the store epilogue only")
         else:
             mats = [Q.Q2KMatrix(Q.quantize_q2k(torch.randn((rows, k), generator=g, device=dev) * 0.02), rows, k)
                     for _ in range(copies)]
@@ -407,10 +409,10 @@ def run_ours(args):
             return y
 
         launches_per_step = 2
-        local_bytes = gemv_bytes(rows, k, 1, out_rows) + (rows * (k // 256) * (110 - 84) if q3 else 0)
+        local_bytes = gemv_bytes(rows, k, 1, out_rows) + rows * (k // 256) * (blk_bytes - 84)
         h2d, d2h = k * 4, out_rows * 4
         out_buf = y
-        workload = (f"{'Q3_K' if q3 else 'Q2_K'} x Q8_K GEMV W[{rows},{k}] ~N(0,0.02), x[{k}] ~N(0,1), epilogue {epi}, "
+        workload = (f"{args.gemv_fmt.upper().replace('K', '_K')} x Q8_K GEMV W[{rows},{k}], x[{k}] ~N(0,1), epilogue {epi}, "
                     f"{copies} rotating weight copies ({copies * mbytes / 2**20:.0f} MB > L2)")
         gemvs = [("gemv", m) for m in mats]
 

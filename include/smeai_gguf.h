@@ -74,8 +74,9 @@ int smeai_gguf_read_tensor(const void *ctx, int64_t id, void *dst, uint64_t dst_
  * with smeai_q2k_free).  Other types are refused with -3. */
 int smeai_gguf_load_q2k(const void *ctx, int64_t id, void **w_dev_out);
 
-/* The same for a 2-D Q3_K tensor (smeai_q3k_repack's handle). */
+/* The same for a 2-D Q3_K / Q6_K tensor (smeai_q3k_repack's / smeai_q6k_repack's handle). */
 int smeai_gguf_load_q3k(const void *ctx, int64_t id, void **w_dev_out);
+int smeai_gguf_load_q6k(const void *ctx, int64_t id, void **w_dev_out);
 
 /* Metadata: gguf_get_n_kv / gguf_find_key (-1 when absent), the value type
  * of a key (GGUF value-type numbering: 0 u8 .. 12 f64, 8 = string,

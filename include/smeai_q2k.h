@@ -201,6 +201,26 @@ int smeai_q3k_block_sums(const void *w_dev, const void *x_q8k_dev, int32_t *isum
 /* Device decode of n weights (n/256 blocks) to fp32. */
 int smeai_q3k_dequantize_device(const void *w_q3k_dev, int64_t n, float *y_dev, void *stream);
 
+/* ---------------- 4. Q6_K weights ----------------------------------------
+ * The reference model's one Q6_K tensor (llama.cpp/doc/SME_Q2K_OPTIMIZATION.md:
+ * 44-51) on ggml's generic path.  block_q6_K = ql[128] qh[64] scales[16]
+ * (int8) d(fp16) = 210 bytes per 256 weights.  Same contract as Q3_K: the
+ * per-super-block integers equal ggml's; ggml accumulates floats in 8
+ * position lanes, the GPU in one. */
+void dequantize_row_q6_K(const void *x, float *y, int64_t k);
+void ggml_vec_dot_q6_K_q8_K(int n, float *s, size_t bs, const void *vx, size_t bx, const void *vy, size_t by,
+                            int nrc);
+int smeai_q6k_repack(const void *w_q6k, int64_t n_rows, int64_t k, void **w_dev_out);
+void smeai_q6k_free(void *w_dev);
+int smeai_q6k_mul_mat(const void *w_dev, const void *x_q8k_dev, int64_t n_cols, float *y_dev, size_t ldy,
+                      void *stream);
+int smeai_q6k_mul_mat_f32(const void *w_dev, const float *x_dev, size_t ld_x, int64_t n_cols, float *y_dev,
+                          size_t ldy, float rms_eps, void *stream);
+/* isum (ggml's integer total) and summs = sum_j scale_j * bsums_j. */
+int smeai_q6k_block_sums(const void *w_dev, const void *x_q8k_dev, int32_t *isum_dev, int32_t *summs_dev,
+                         void *stream);
+int smeai_q6k_dequantize_device(const void *w_q6k_dev, int64_t n, float *y_dev, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

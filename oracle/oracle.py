@@ -23,8 +23,10 @@ BLOCK_Q2_K = np.dtype([("scales", np.uint8, 16), ("qs", np.uint8, 64),
                        ("d", np.uint16), ("dmin", np.uint16)])
 BLOCK_Q3_K = np.dtype([("hmask", np.uint8, 32), ("qs", np.uint8, 64), ("scales", np.uint8, 12),
                        ("d", np.uint16)])
+BLOCK_Q6_K = np.dtype([("ql", np.uint8, 128), ("qh", np.uint8, 64), ("scales", np.int8, 16), ("d", np.uint16)])
 BLOCK_Q8_K = np.dtype([("d", np.float32), ("qs", np.int8, 256), ("bsums", np.int16, 16)])
-assert BLOCK_Q2_K.itemsize == 84 and BLOCK_Q3_K.itemsize == 110 and BLOCK_Q8_K.itemsize == 292
+assert BLOCK_Q2_K.itemsize == 84 and BLOCK_Q3_K.itemsize == 110 and BLOCK_Q6_K.itemsize == 210
+assert BLOCK_Q8_K.itemsize == 292
 
 ROUND_FUSED, ROUND_SEPARATE = 0, 1
 COMBINE_FUSED, COMBINE_SEPARATE = 0, 1
@@ -69,6 +71,10 @@ def lib() -> ctypes.CDLL:
             "orc_q3k_block_sums": (None, [I, P, P, P]),
             "orc_vec_dot_q3_K_q8_K": (F, [I, P, P, I]),
             "orc_q3k_mul_mat": (None, [P, I64, I64, P, I64, P, I64, I, I]),
+            "orc_dequantize_row_q6_K": (None, [P, P, I64]),
+            "orc_q6k_block_sums": (None, [I, P, P, P]),
+            "orc_vec_dot_q6_K_q8_K": (F, [I, P, P, I]),
+            "orc_q6k_mul_mat": (None, [P, I64, I64, P, I64, P, I64, I, I]),
             "orc_rms_inv": (F, [P, I64, F]),
             "orc_rms_sumsq": (F, [P, I64]),
             "orc_rmsnorm_quantize_q8_K": (None, [P, P, I64, F, I]),
@@ -222,6 +228,42 @@ def q3k_mul_mat(w: np.ndarray, n_rows: int, k: int, xq: np.ndarray, n_cols: int,
     w, xq = np.ascontiguousarray(w), np.ascontiguousarray(xq)
     y = np.empty((n_cols, n_rows), np.float32)
     lib().orc_q3k_mul_mat(_p(w), n_rows, k, _p(xq), n_cols, _p(y), n_rows, order, n_threads)
+    return y
+
+
+def random_q6_K(rng, n_blocks: int) -> np.ndarray:
+    """Valid Q6_K blocks of random bits (any ql/qh/scales bytes) with d a
+    positive normal fp16 of the magnitude of a quantized N(0, 0.02) weight."""
+    b = rng.integers(0, 256, size=(n_blocks, 210), dtype=np.uint8)
+    d = (np.abs(rng.standard_normal(n_blocks)) * 0.00005 + 1e-6).astype(np.float16)
+    b[:, 208:210] = d.view(np.uint8).reshape(-1, 2)
+    return b.reshape(-1).view(BLOCK_Q6_K)
+
+
+def dequantize_q6_K(blocks: np.ndarray) -> np.ndarray:
+    blocks = np.ascontiguousarray(blocks)
+    out = np.empty(blocks.size * QK_K, np.float32)
+    lib().orc_dequantize_row_q6_K(_p(blocks), _p(out), out.size)
+    return out
+
+
+def q6k_block_sums(wrow: np.ndarray, xq: np.ndarray) -> np.ndarray:
+    wrow, xq = np.ascontiguousarray(wrow), np.ascontiguousarray(xq)
+    isum = np.empty(wrow.size, np.int32)
+    lib().orc_q6k_block_sums(wrow.size * QK_K, _p(wrow), _p(xq), _p(isum))
+    return isum
+
+
+def vec_dot_q6_K_q8_K(wrow, xq, order=Q3K_GGML) -> float:
+    wrow, xq = np.ascontiguousarray(wrow), np.ascontiguousarray(xq)
+    return lib().orc_vec_dot_q6_K_q8_K(wrow.size * QK_K, _p(wrow), _p(xq), order)
+
+
+def q6k_mul_mat(w: np.ndarray, n_rows: int, k: int, xq: np.ndarray, n_cols: int, order=Q3K_GGML,
+                n_threads: int = 1) -> np.ndarray:
+    w, xq = np.ascontiguousarray(w), np.ascontiguousarray(xq)
+    y = np.empty((n_cols, n_rows), np.float32)
+    lib().orc_q6k_mul_mat(_p(w), n_rows, k, _p(xq), n_cols, _p(y), n_rows, order, n_threads)
     return y
 
 

@@ -633,6 +633,91 @@ void orc_q3k_mul_mat(const orc_block_q3_K *w, int64_t n_rows, int64_t k,
 }
 
 /* ======================================================================== */
+/* Q6_K (ggml 0.9.8 generic C; the one Q6_K tensor of the reference's model,  */
+/* llama.cpp/doc/SME_Q2K_OPTIMIZATION.md:44-51).  Weight i of a 128-weight    */
+/* half (l = i % 32, group g = i / 32) is d * scale_{i/16} * (u - 32) with     */
+/* u = (low or high nibble of ql[l + 32*(g&1)]) | (bits 2g..2g+1 of qh[l])<<4 */
+/* (low nibble for g < 2, high for g >= 2).                                  */
+/* ======================================================================== */
+static int orc_q6k_quant(const orc_block_q6_K *x, int i) {
+    int half = i / 128, within = i % 128, g = within / 32, l = within % 32;
+    const uint8_t *ql = x->ql + 64 * half, *qh = x->qh + 32 * half;
+    int lo = ql[l + 32 * (g & 1)];
+    lo = (g < 2) ? (lo & 0xF) : (lo >> 4);
+    int hi = (qh[l] >> (2 * g)) & 3;
+    return (lo | (hi << 4)) - 32;
+}
+
+void orc_dequantize_row_q6_K(const orc_block_q6_K *x, float *y, int64_t k) {
+    int64_t nb = k / ORC_QK_K;
+    for (int64_t b = 0; b < nb; ++b) {
+        float d = orc_half_to_float(x[b].d);
+        for (int i = 0; i < ORC_QK_K; ++i) {
+            float dl = d * (float) x[b].scales[i / 16];
+            y[b * ORC_QK_K + i] = dl * (float) orc_q6k_quant(x + b, i);
+        }
+    }
+}
+
+/* Per super-block: isum = sum_j scale_j * sum_{i in j} q_i * q8_i. */
+void orc_q6k_block_sums(int n, const orc_block_q6_K *x, const orc_block_q8_K *y, int32_t *isum) {
+    int nb = n / ORC_QK_K;
+    for (int b = 0; b < nb; ++b) {
+        int32_t acc = 0;
+        for (int j = 0; j < 16; ++j) {
+            int32_t s = 0;
+            for (int i = 16 * j; i < 16 * j + 16; ++i) s += (int32_t) y[b].qs[i] * orc_q6k_quant(x + b, i);
+            acc += (int32_t) x[b].scales[j] * s;
+        }
+        isum[b] = acc;
+    }
+}
+
+/* ggml_vec_dot_q6_K_q8_K, generic C: the 8-lane form of the Q3_K dot above
+ * (aux32[l] over positions i = l mod 8, sums[l] = fmaf(d, aux32[l], sums[l]),
+ * then sums[0] + ... + sums[7]); ORC_Q3K_BLOCK_ORDER is the GPU's combine,
+ * sumf += (fp32(d_x) * d_y) * fp32(isum) per block. */
+float orc_vec_dot_q6_K_q8_K(int n, const orc_block_q6_K *x, const orc_block_q8_K *y, int order) {
+    int nb = n / ORC_QK_K;
+    if (order == ORC_Q3K_BLOCK_ORDER) {
+        float sumf = 0.0f;
+        for (int b = 0; b < nb; ++b) {
+            int32_t isum;
+            orc_q6k_block_sums(ORC_QK_K, x + b, y + b, &isum);
+            const float d = orc_half_to_float(x[b].d) * y[b].d;
+            sumf = sumf + d * (float) isum;
+        }
+        return sumf;
+    }
+    float sums[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    for (int b = 0; b < nb; ++b) {
+        int32_t aux32[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+        for (int j = 0; j < 16; ++j)
+            for (int i = 16 * j; i < 16 * j + 16; ++i)
+                aux32[i % 8] += (int32_t) x[b].scales[j] * ((int32_t) y[b].qs[i] * orc_q6k_quant(x + b, i));
+        const float d = orc_half_to_float(x[b].d) * y[b].d;
+        for (int l = 0; l < 8; ++l) sums[l] = fmaf(d, (float) aux32[l], sums[l]);
+    }
+    float sumf = 0.0f;
+    for (int l = 0; l < 8; ++l) sumf += sums[l];
+    return sumf;
+}
+
+void orc_q6k_mul_mat(const orc_block_q6_K *w, int64_t n_rows, int64_t k,
+                     const orc_block_q8_K *xq, int64_t n_cols, float *y, int64_t ldy,
+                     int order, int n_threads) {
+    int64_t nb = k / ORC_QK_K;
+#ifdef _OPENMP
+    if (n_threads < 1) n_threads = 1;
+#pragma omp parallel for schedule(static) num_threads(n_threads)
+#endif
+    for (int64_t r = 0; r < n_rows; ++r)
+        for (int64_t c = 0; c < n_cols; ++c)
+            y[c * ldy + r] = orc_vec_dot_q6_K_q8_K((int) k, w + r * nb, xq + c * nb, order);
+    (void) n_threads;
+}
+
+/* ======================================================================== */
 /* Decode-stack helpers (RMSNorm is the reference's sme_ai_rmsnorm_f32,      */
 /* sme_ai_ops.c:1060-1092: y = x / sqrt(mean(x^2) + eps)).  The sum of       */
 /* squares is taken in the fixed order the GPU kernels use, so both sides    */

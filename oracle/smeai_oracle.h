@@ -50,6 +50,14 @@ typedef struct {
     uint16_t d;         /* fp16 super-block scale                          */
 } orc_block_q3_K;
 
+/* ggml block_q6_K: 210 bytes per 256 weights (gguf/constants.py, Q6_K). */
+typedef struct {
+    uint8_t ql[128];    /* low 4 bits of each 6-bit quant                  */
+    uint8_t qh[64];     /* high 2 bits, 4 per byte                         */
+    int8_t scales[16];  /* 8-bit sub-block scales                          */
+    uint16_t d;         /* fp16 super-block scale                          */
+} orc_block_q6_K;
+
 /* ggml block_q8_K: 292 bytes per 256 activations (gguf/constants.py:4246). */
 typedef struct {
     float d;
@@ -112,6 +120,15 @@ void orc_dequantize_row_q3_K(const orc_block_q3_K *x, float *y, int64_t k);
 void orc_q3k_block_sums(int n, const orc_block_q3_K *x, const orc_block_q8_K *y, int32_t *isum);
 float orc_vec_dot_q3_K_q8_K(int n, const orc_block_q3_K *x, const orc_block_q8_K *y, int order);
 void orc_q3k_mul_mat(const orc_block_q3_K *w, int64_t n_rows, int64_t k,
+                     const orc_block_q8_K *xq, int64_t n_cols, float *y, int64_t ldy,
+                     int order, int n_threads);
+
+/* Q6_K: the same three forms (ggml's 8-lane generic dot; the GPU's
+ * block-order combine of the same per-block integer). */
+void orc_dequantize_row_q6_K(const orc_block_q6_K *x, float *y, int64_t k);
+void orc_q6k_block_sums(int n, const orc_block_q6_K *x, const orc_block_q8_K *y, int32_t *isum);
+float orc_vec_dot_q6_K_q8_K(int n, const orc_block_q6_K *x, const orc_block_q8_K *y, int order);
+void orc_q6k_mul_mat(const orc_block_q6_K *w, int64_t n_rows, int64_t k,
                      const orc_block_q8_K *xq, int64_t n_cols, float *y, int64_t ldy,
                      int order, int n_threads);
 

@@ -17,6 +17,7 @@ namespace {
 
 constexpr uint32_t kHandleMagic = 0x51324b57u;  // "Q2KW"
 constexpr int64_t kQ3KBytes = 110;               // ggml block_q3_K
+constexpr int64_t kQ6KBytes = 210;               // ggml block_q6_K
 
 struct Handle {
   uint32_t magic = kHandleMagic;
@@ -37,7 +38,8 @@ const Handle* as_handle(const void* p) {
 const Handle* as_fmt(const void* p, int fmt, const char* what) {
   const Handle* h = as_handle(p);
   if (h && h->w.fmt != fmt) {
-    set_last_error("%s: the handle holds a %s weight", what, h->w.fmt == kFmtQ3K ? "Q3_K" : "Q2_K");
+    set_last_error("%s: the handle holds a %s weight", what,
+                   h->w.fmt == kFmtQ3K ? "Q3_K" : h->w.fmt == kFmtQ6K ? "Q6_K" : "Q2_K");
     return nullptr;
   }
   return h;
@@ -434,6 +436,106 @@ void ggml_vec_dot_q3_K_q8_K(int n, float* s, size_t bs, const void* vx, size_t b
   if (c.init() || c.a.in(vx, nb * kQ3KBytes, c.stream) || c.b.in(vy, nb * Q8K_BLOCK_BYTES, c.stream) ||
       c.tiles.reserve(q3k_tile_bytes(1, n)) || c.y.reserve(4) ||
       q3k_repack_into(c.a.dev, 1, n, static_cast<uint8_t*>(c.tiles.ptr), &w, c.stream) ||
+      q2k_gemv(w, c.b.dev, 1, static_cast<float*>(c.y.ptr), 1, kEpiStore, nullptr, 0, c.stream) ||
+      cudaMemcpyAsync(s, c.y.ptr, 4, cudaMemcpyDeviceToHost, c.stream) != cudaSuccess ||
+      cudaStreamSynchronize(c.stream) != cudaSuccess) {
+    *s = 0.f;
+  }
+}
+
+// ---- Q6_K ----------------------------------------------------------------------
+
+int smeai_q6k_repack(const void* w_q6k, int64_t n_rows, int64_t k, void** w_dev_out) {
+  if (!w_q6k || !w_dev_out || n_rows <= 0 || k <= 0 || k % QK_K) {
+    set_last_error("smeai_q6k_repack: bad arguments");
+    return kBadArgument;
+  }
+  *w_dev_out = nullptr;
+  if (!device_ready()) {
+    set_last_error("smeai_q6k_repack: no compute-capability-10.x device");
+    return kUnsupported;
+  }
+  Staged src;
+  const size_t bytes = (size_t)n_rows * (size_t)(k / QK_K) * kQ6KBytes;
+  int st = src.in(w_q6k, bytes, nullptr);
+  if (st) return st;
+  Handle* h = new Handle();
+  st = q6k_repack(src.dev, n_rows, k, &h->w, nullptr);
+  if (st == kOk && cudaStreamSynchronize(nullptr) != cudaSuccess) {
+    set_last_error("smeai_q6k_repack: %s", cudaGetErrorString(cudaGetLastError()));
+    st = kCudaError;
+  }
+  if (st) {
+    if (h->w.tiles) cudaFree(h->w.tiles);
+    delete h;
+    return st;
+  }
+  *w_dev_out = h;
+  return kOk;
+}
+
+void smeai_q6k_free(void* w_dev) { smeai_q2k_free(w_dev); }
+
+int smeai_q6k_mul_mat(const void* w_dev, const void* x_q8k_dev, int64_t n_cols, float* y_dev, size_t ldy,
+                      void* stream) {
+  const Handle* h = as_fmt(w_dev, kFmtQ6K, "smeai_q6k_mul_mat");
+  if (!h) return kBadArgument;
+  return q2k_gemv(h->w, x_q8k_dev, n_cols, y_dev, (int64_t)ldy, kEpiStore, nullptr, 0, as_stream(stream));
+}
+
+int smeai_q6k_mul_mat_f32(const void* w_dev, const float* x_dev, size_t ld_x, int64_t n_cols, float* y_dev,
+                          size_t ldy, float rms_eps, void* stream) {
+  const Handle* h = as_fmt(w_dev, kFmtQ6K, "smeai_q6k_mul_mat_f32");
+  if (!h) return kBadArgument;
+  return q2k_gemv_any(h->w, rms_eps >= 0.f ? kInF32Rms : kInF32, x_dev, (int64_t)ld_x, rms_eps, n_cols, y_dev,
+                      (int64_t)ldy, kEpiStore, nullptr, 0, as_stream(stream));
+}
+
+int smeai_q6k_block_sums(const void* w_dev, const void* x_q8k_dev, int32_t* isum_dev, int32_t* summs_dev,
+                         void* stream) {
+  const Handle* h = as_fmt(w_dev, kFmtQ6K, "smeai_q6k_block_sums");
+  if (!h) return kBadArgument;
+  return q2k_block_sums(h->w, x_q8k_dev, isum_dev, summs_dev, as_stream(stream));
+}
+
+int smeai_q6k_dequantize_device(const void* w_q6k_dev, int64_t n, float* y_dev, void* stream) {
+  if (!w_q6k_dev || !y_dev) {
+    set_last_error("smeai_q6k_dequantize_device: NULL pointer");
+    return kBadArgument;
+  }
+  return q6k_dequantize(w_q6k_dev, n, y_dev, as_stream(stream));
+}
+
+void dequantize_row_q6_K(const void* x, float* y, int64_t k) {
+  if (!x || !y || k <= 0 || k % QK_K) {
+    set_last_error("dequantize_row_q6_K: k must be a positive multiple of 256");
+    return;
+  }
+  ThreadCtx& c = tctx();
+  if (c.init() || c.a.in(x, (size_t)(k / QK_K) * kQ6KBytes, c.stream) || c.b.out(y, (size_t)k * 4) ||
+      q6k_dequantize(c.a.dev, k, static_cast<float*>(c.b.dev), c.stream) || c.b.finish(c.stream) ||
+      cudaStreamSynchronize(c.stream) != cudaSuccess) {
+    if (!is_device_pointer(y)) memset(y, 0, (size_t)k * 4);
+  }
+}
+
+void ggml_vec_dot_q6_K_q8_K(int n, float* s, size_t bs, const void* vx, size_t bx, const void* vy, size_t by,
+                            int nrc) {
+  (void)bs;
+  (void)bx;
+  (void)by;
+  if (!s) return;
+  *s = 0.f;
+  if (!vx || !vy || n <= 0 || n % QK_K || nrc != 1) {
+    set_last_error("ggml_vec_dot_q6_K_q8_K: needs n %% 256 == 0 and nrc == 1");
+    return;
+  }
+  ThreadCtx& c = tctx();
+  const int64_t nb = n / QK_K;
+  Q2KWeight w;
+  if (c.init() || c.a.in(vx, nb * kQ6KBytes, c.stream) || c.b.in(vy, nb * Q8K_BLOCK_BYTES, c.stream) ||
+      c.tiles.reserve(q6k_tile_bytes(1, n)) || c.y.reserve(4) ||
+      q6k_repack_into(c.a.dev, 1, n, static_cast<uint8_t*>(c.tiles.ptr), &w, c.stream) ||
       q2k_gemv(w, c.b.dev, 1, static_cast<float*>(c.y.ptr), 1, kEpiStore, nullptr, 0, c.stream) ||
       cudaMemcpyAsync(s, c.y.ptr, 4, cudaMemcpyDeviceToHost, c.stream) != cudaSuccess ||
       cudaStreamSynchronize(c.stream) != cudaSuccess) {

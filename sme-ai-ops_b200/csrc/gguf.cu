@@ -446,6 +446,31 @@ int smeai_gguf_load_q3k(const void* ctx, int64_t id, void** w_dev_out) {
   return smeai_q3k_repack(host.data(), t.ne[1], t.ne[0], w_dev_out);
 }
 
+int smeai_gguf_load_q6k(const void* ctx, int64_t id, void** w_dev_out) {
+  const Ctx* c = as_ctx(ctx);
+  if (!c || !w_dev_out || id < 0 || id >= (int64_t)c->tensors.size()) {
+    set_last_error("smeai_gguf_load_q6k: bad context, tensor id or output");
+    return kBadArgument;
+  }
+  *w_dev_out = nullptr;
+  const TensorInfo& t = c->tensors[(size_t)id];
+  if (t.type != SMEAI_GGML_Q6_K || t.n_dims != 2) {
+    set_last_error("smeai_gguf_load_q6k: %s is ggml type %d with %d dims (a 2-D Q6_K tensor is required)",
+                   t.name.c_str(), t.type, t.n_dims);
+    return kUnsupported;
+  }
+  std::vector<uint8_t> host;
+  try {
+    host.resize((size_t)t.nbytes);
+  } catch (...) {
+    set_last_error("smeai_gguf_load_q6k: cannot allocate %llu host bytes", (unsigned long long)t.nbytes);
+    return kAllocFailed;
+  }
+  int st = smeai_gguf_read_tensor(ctx, id, host.data(), t.nbytes);
+  if (st != kOk) return st;
+  return smeai_q6k_repack(host.data(), t.ne[1], t.ne[0], w_dev_out);
+}
+
 int64_t smeai_gguf_n_kv(const void* ctx) {
   const Ctx* c = as_ctx(ctx);
   return c ? (int64_t)c->kv.size() : kBadArgument;

@@ -26,7 +26,9 @@ constexpr int kTileBytes = 32 * 84;
 
 // Weight formats held in the tile layout (tile bytes per 32-row group and
 // super-block: Q2_K 2688, Q3_K 3584 -- see q3k_core.cuh).
-enum WeightFmt : int { kFmtQ2K = 0, kFmtQ3K = 1 };
+enum WeightFmt : int { kFmtQ2K = 0, kFmtQ3K = 1, kFmtQ6K = 2 };
+// Tile bytes per (32-row group, super-block) of each format.
+inline int fmt_tile_bytes(int fmt) { return fmt == kFmtQ3K ? 32 * 112 : fmt == kFmtQ6K ? 32 * 212 : 32 * 84; }
 
 struct Q2KWeight {
   int fmt = kFmtQ2K;
@@ -51,6 +53,13 @@ int q3k_repack_into(const void* w_blocks_dev, int64_t n_rows, int64_t k, uint8_t
                     cudaStream_t stream);
 int q3k_repack(const void* w_blocks_dev, int64_t n_rows, int64_t k, Q2KWeight* out, cudaStream_t stream);
 int q3k_dequantize(const void* w, int64_t k_total, float* y, cudaStream_t stream);
+
+// ---- Q6_K weights (q6k_quant.cu) ----
+size_t q6k_tile_bytes(int64_t n_rows, int64_t k);
+int q6k_repack_into(const void* w_blocks_dev, int64_t n_rows, int64_t k, uint8_t* tiles, Q2KWeight* out,
+                    cudaStream_t stream);
+int q6k_repack(const void* w_blocks_dev, int64_t n_rows, int64_t k, Q2KWeight* out, cudaStream_t stream);
+int q6k_dequantize(const void* w, int64_t k_total, float* y, cudaStream_t stream);
 
 enum Epilogue : int {
   kEpiStore = 0,     // y[c*ldy + r] = acc

@@ -35,6 +35,7 @@
 #include "q8k_device.cuh"
 #include "q2k_core.cuh"
 #include "q3k_core.cuh"
+#include "q6k_core.cuh"
 
 #include <stdio.h>
 #include <stdlib.h>
@@ -403,10 +404,13 @@ Plan plan_for(int T, int nb, int64_t n_groups, int tile = kTileBytes) {
       pl.stages = s;
       break;
     }
-  if (!pl.stages)
+  // fallback: one CTA per SM with the whole shared memory, fewer consumer
+  // warps when a stage of large tiles (Q6_K: 6784 bytes) leaves no room
+  for (int c = pl.consumers; !pl.stages && c >= 4; c >>= 1)
     for (int s = 8; s >= 2; s >>= 1)
-      if (fixed + (size_t)s * stage <= (size_t)kSmemLimit) {
+      if (fixed + (size_t)s * ((size_t)c * tile + 16) <= (size_t)kSmemLimit) {
         pl.stages = s;
+        pl.consumers = c;
         pl.ctas_per_sm = 1;
         break;
       }
@@ -458,12 +462,13 @@ int dispatch_t(int T, const Q2KWeight& w, const GemvParams& p, cudaStream_t s) {
 
 template <int IN>
 int dispatch_epi(int epi, int T, const Q2KWeight& w, const GemvParams& p, cudaStream_t s) {
-  if (w.fmt == kFmtQ3K) {  // Q3_K weights: the store epilogue
+  if (w.fmt == kFmtQ3K || w.fmt == kFmtQ6K) {  // Q3_K / Q6_K weights: the store epilogue
     if (epi != kEpiStore) {
-      set_last_error("q3k_gemv: only the store epilogue is built for Q3_K weights");
+      set_last_error("gemv: only the store epilogue is built for Q3_K and Q6_K weights");
       return kBadArgument;
     }
-    return dispatch_t<FmtQ3K, kEpiStore, IN>(T, w, p, s);
+    return w.fmt == kFmtQ3K ? dispatch_t<FmtQ3K, kEpiStore, IN>(T, w, p, s)
+                            : dispatch_t<FmtQ6K, kEpiStore, IN>(T, w, p, s);
   }
   switch (epi) {
     case kEpiStore: return dispatch_t<FmtQ2K, kEpiStore, IN>(T, w, p, s);
@@ -554,7 +559,7 @@ int q2k_gemv_any(const Q2KWeight& w, int in_mode, const void* x, int64_t ld_x, f
   for (int64_t c0 = 0; c0 < n_cols;) {
     const int64_t rem = n_cols - c0;
     int T = rem >= 8 ? 8 : (rem >= 4 ? 4 : (rem >= 2 ? 2 : 1));
-    while (T > 1 && plan_stages(T, w.nb, w.fmt == kFmtQ3K ? kQ3KTileBytes : kTileBytes) <= 0) T >>= 1;
+    while (T > 1 && plan_stages(T, w.nb, fmt_tile_bytes(w.fmt)) <= 0) T >>= 1;
     GemvParams p = {};
     p.tiles = w.tiles;
     p.nb = w.nb;
@@ -601,6 +606,7 @@ int q2k_block_sums(const Q2KWeight& w, const void* xq, int32_t* isum, int32_t* s
   p.isum_out = isum;
   p.summs_out = summs;
   if (w.fmt == kFmtQ3K) return launch_gemv<FmtQ3K, 1, kEpiStore, kInQ8K, true>(w, p, stream);
+  if (w.fmt == kFmtQ6K) return launch_gemv<FmtQ6K, 1, kEpiStore, kInQ8K, true>(w, p, stream);
   return launch_gemv<FmtQ2K, 1, kEpiStore, kInQ8K, true>(w, p, stream);
 }
 

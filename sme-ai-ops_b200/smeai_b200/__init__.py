@@ -17,6 +17,7 @@ INCLUDE_DIR = os.path.abspath(os.path.join(PKG, "..", "..", "include"))
 QK_K = 256
 Q2K_BLOCK_BYTES = 84
 Q3K_BLOCK_BYTES = 110
+Q6K_BLOCK_BYTES = 210
 Q8K_BLOCK_BYTES = 292
 EPI_STORE, EPI_RESIDUAL, EPI_SILU_MUL = 0, 1, 2
 ACT_NONE, ACT_RELU, ACT_GELU, ACT_SILU = 0, 1, 2, 3
@@ -82,6 +83,15 @@ def _declare(L: ctypes.CDLL) -> None:
         "smeai_q3k_block_sums": (I, [P, P, P, P, P]),
         "smeai_q3k_dequantize_device": (I, [P, I64, P, P]),
         "smeai_gguf_load_q3k": (I, [P, I64, ctypes.POINTER(ctypes.c_void_p)]),
+        "dequantize_row_q6_K": (None, [P, P, I64]),
+        "ggml_vec_dot_q6_K_q8_K": (None, [I, P, SZ, P, SZ, P, SZ, I]),
+        "smeai_q6k_repack": (I, [P, I64, I64, ctypes.POINTER(ctypes.c_void_p)]),
+        "smeai_q6k_free": (None, [P]),
+        "smeai_q6k_mul_mat": (I, [P, P, I64, P, SZ, P]),
+        "smeai_q6k_mul_mat_f32": (I, [P, P, SZ, I64, P, SZ, F, P]),
+        "smeai_q6k_block_sums": (I, [P, P, P, P, P]),
+        "smeai_q6k_dequantize_device": (I, [P, I64, P, P]),
+        "smeai_gguf_load_q6k": (I, [P, I64, ctypes.POINTER(ctypes.c_void_p)]),
         # smeai_gguf.h
         "smeai_gguf_open": (I, [ctypes.c_char_p, ctypes.POINTER(ctypes.c_void_p)]),
         "smeai_gguf_close": (None, [P]),

@@ -71,6 +71,14 @@ class GGUFFile:
         check(lib().smeai_gguf_load_q3k(self.handle, t.index, ctypes.byref(h)), f"gguf_load_q3k({name})")
         return Q3KMatrix(None, t.shape[1], t.shape[0], handle=h)
 
+    def load_q6k(self, name: str):
+        """A 2-D Q6_K tensor as a device Q6KMatrix."""
+        from .q2k import Q6KMatrix
+        t = self.by_name[name]
+        h = ctypes.c_void_p()
+        check(lib().smeai_gguf_load_q6k(self.handle, t.index, ctypes.byref(h)), f"gguf_load_q6k({name})")
+        return Q6KMatrix(None, t.shape[1], t.shape[0], handle=h)
+
     def key_type(self, key: str) -> int:
         return lib().smeai_gguf_key_type(self.handle, key.encode())
 

@@ -6,8 +6,8 @@ import ctypes
 import numpy as np
 import torch
 
-from . import (EPI_RESIDUAL, EPI_SILU_MUL, EPI_STORE, Q2K_BLOCK_BYTES, Q3K_BLOCK_BYTES, Q8K_BLOCK_BYTES, QK_K,
-               check, lib)
+from . import (EPI_RESIDUAL, EPI_SILU_MUL, EPI_STORE, Q2K_BLOCK_BYTES, Q3K_BLOCK_BYTES, Q6K_BLOCK_BYTES,
+               Q8K_BLOCK_BYTES, QK_K, check, lib)
 
 
 def _ptr(t):
@@ -160,7 +160,7 @@ class Q2KMatrix:
 
 
 __all__ = ["quantize_q8k", "rms_quantize_q8k", "quantize_q2k", "dequantize_q2k", "Q2KMatrix", "Q3KMatrix",
-           "dequantize_q3k", "as_bytes",
+           "dequantize_q3k", "Q6KMatrix", "dequantize_q6k", "as_bytes",
            "EPI_STORE", "EPI_RESIDUAL", "EPI_SILU_MUL"]
 
 
@@ -227,6 +227,72 @@ class Q3KMatrix:
 def dequantize_q3k(blocks: torch.Tensor, k_total: int) -> torch.Tensor:
     out = torch.empty(k_total, dtype=torch.float32, device=blocks.device)
     check(lib().smeai_q3k_dequantize_device(_ptr(blocks), k_total, _ptr(out), cur_stream()), "q3k_dequantize")
+    return out
+
+
+class Q6KMatrix:
+    """A Q6_K weight [n_rows, k] in the device tile layout (smeai_q6k_*)."""
+
+    def __init__(self, blocks, n_rows: int, k: int, handle: ctypes.c_void_p | None = None):
+        assert k % QK_K == 0
+        self.n_rows, self.k, self.nb = n_rows, k, k // QK_K
+        if handle is None:
+            handle = ctypes.c_void_p()
+            if isinstance(blocks, torch.Tensor):
+                src = blocks.contiguous()
+                ptr = _ptr(src)
+                if src.is_cuda:
+                    torch.cuda.current_stream().synchronize()
+                n = src.numel()
+            else:
+                src = as_bytes(blocks)
+                ptr = ctypes.c_void_p(src.ctypes.data)
+                n = src.size
+            assert n == n_rows * self.nb * Q6K_BLOCK_BYTES
+            check(lib().smeai_q6k_repack(ptr, n_rows, k, ctypes.byref(handle)), "q6k_repack")
+        self.handle = handle
+        self.bytes = lib().smeai_q2k_weight_bytes(handle)
+
+    def mul_mat(self, xq: torch.Tensor, n_cols: int, out: torch.Tensor | None = None) -> torch.Tensor:
+        if out is None:
+            out = torch.empty((n_cols, self.n_rows), dtype=torch.float32, device=xq.device)
+        check(lib().smeai_q6k_mul_mat(self.handle, _ptr(xq), n_cols, _ptr(out), out.stride(0), cur_stream()),
+              "q6k_mul_mat")
+        return out
+
+    def mul_mat_f32(self, x: torch.Tensor, rms_eps: float | None = None,
+                    out: torch.Tensor | None = None) -> torch.Tensor:
+        x2 = x.reshape(-1, self.k)
+        n_cols = x2.shape[0]
+        if out is None:
+            out = torch.empty((n_cols, self.n_rows), dtype=torch.float32, device=x.device)
+        eps = -1.0 if rms_eps is None else rms_eps
+        check(lib().smeai_q6k_mul_mat_f32(self.handle, _ptr(x2), x2.stride(0), n_cols, _ptr(out), out.stride(0),
+                                          ctypes.c_float(eps), cur_stream()), "q6k_mul_mat_f32")
+        return out
+
+    def block_sums(self, xq_row: torch.Tensor):
+        isum = torch.empty((self.n_rows, self.nb), dtype=torch.int32, device=xq_row.device)
+        summs = torch.empty_like(isum)
+        check(lib().smeai_q6k_block_sums(self.handle, _ptr(xq_row), _ptr(isum), _ptr(summs), cur_stream()),
+              "q6k_block_sums")
+        return isum, summs
+
+    def free(self):
+        if getattr(self, "handle", None) and self.handle.value:
+            lib().smeai_q6k_free(self.handle)
+            self.handle = ctypes.c_void_p()
+
+    def __del__(self):
+        try:
+            self.free()
+        except Exception:
+            pass
+
+
+def dequantize_q6k(blocks: torch.Tensor, k_total: int) -> torch.Tensor:
+    out = torch.empty(k_total, dtype=torch.float32, device=blocks.device)
+    check(lib().smeai_q6k_dequantize_device(_ptr(blocks), k_total, _ptr(out), cur_stream()), "q6k_dequantize")
     return out
 
 

@@ -16,6 +16,12 @@ q3k_gguf.npz
     their fp32 decoding by gguf-py 0.19.0 ``Q3_K.dequantize_blocks`` -- pins
     the 6-bit scale packing, the high-bit mask order and the -4 offset.
 
+q6k_gguf.npz
+    Q6_K blocks (random ql/qh/scales bits with seeded positive fp16 d, plus an
+    all-zero block and a block at the extremes) and their fp32 decoding by
+    gguf-py 0.19.0 ``Q6_K.dequantize_blocks`` -- pins the nibble / 2-bit
+    placement, the -32 offset and the signed 8-bit scales.
+
 demo_linear.npz
     The reference example examples/demo_linear.c:16-34 (batch 2, 16 -> 16,
     inputs k%7-3 times 1/8, weights k%11-5 times 1/16, bias k%5-2 times 1/32).
@@ -88,6 +94,21 @@ def make_q3k():
     np.savez_compressed(os.path.join(HERE, "q3k_gguf.npz"), blocks=blocks, dequant=deq)
 
 
+def make_q6k():
+    from gguf.quants import Q6_K
+    rng = np.random.default_rng(20240603)
+    blocks = O.random_q6_K(rng, 64).view(np.uint8).reshape(-1, 210).copy()
+    zero = np.zeros((1, 210), np.uint8)
+    ext = np.zeros((1, 210), np.uint8)
+    ext[0, :128] = np.tile(np.array([0x0F, 0xF0, 0xFF, 0x00], np.uint8), 32)
+    ext[0, 128:192] = np.tile(np.array([0xFF, 0x00, 0x1B, 0xE4], np.uint8), 16)
+    ext[0, 192:208] = np.array([127, -128, -1, 0, 1, 64, -64, 3] * 2, np.int8).view(np.uint8)
+    ext[0, 208:210] = np.frombuffer(np.float16(0.0625).tobytes(), np.uint8)
+    blocks = np.concatenate([blocks, zero, ext], axis=0)
+    deq = Q6_K.dequantize_blocks(blocks).astype(np.float32).reshape(-1)
+    np.savez_compressed(os.path.join(HERE, "q6k_gguf.npz"), blocks=blocks, dequant=deq)
+
+
 def make_demo_linear():
     B, K, N = 2, 16, 16
     x = np.array([((i % 7) - 3) * 0.125 for i in range(B * K)], np.float32)
@@ -117,6 +138,7 @@ if __name__ == "__main__":
     O.build()
     make_q2k()
     make_q3k()
+    make_q6k()
     make_demo_linear()
     make_lcg()
     print("fixtures written to", HERE)
