@@ -178,6 +178,36 @@ sme_ai_status sme_ai_swiglu_sme_packed_f16f32(sme_ai_workspace *ws, const sme_ai
                                               const sme_ai_packed_linear_weight *down_weight,
                                               const float *down_bias, float *output);
 
+/* ---- self-attention (sme_ai_ops.h:410-455) ----------------------------------
+ * Q, K, V = input * {q,k,v}_weight + bias   (input [seq_len][model_dim])
+ * per head (model_dim / num_heads columns):
+ *   p = softmax(Q K^T / sqrtf(head_dim)), causal when `causal` is non-zero
+ *   context = p V
+ * output = fp16(context) * out_weight + out_bias.
+ * Weights are [model_dim][model_dim]; biases may be NULL.  seq_len must not
+ * exceed ws->max_batch, model_dim neither max_in_features nor
+ * max_out_features (else WORKSPACE_TOO_SMALL); model_dim % num_heads != 0 is
+ * BAD_ARGUMENT.  head_dim above 512, or a seq_len whose score rows do not fit
+ * the GPU's shared memory (about 50k keys), reports UNSUPPORTED.  The packed
+ * variant requires every weight to be model_dim x model_dim. */
+sme_ai_status sme_ai_self_attention_ref_f16f32(sme_ai_workspace *ws, const sme_ai_fp16 *input, uint64_t seq_len,
+                                               uint64_t model_dim, uint64_t num_heads,
+                                               const sme_ai_fp16 *q_weight, const float *q_bias,
+                                               const sme_ai_fp16 *k_weight, const float *k_bias,
+                                               const sme_ai_fp16 *v_weight, const float *v_bias,
+                                               const sme_ai_fp16 *out_weight, const float *out_bias, int causal,
+                                               float *output);
+sme_ai_status sme_ai_self_attention_sme_packed_f16f32(sme_ai_workspace *ws, const sme_ai_fp16 *input,
+                                                      uint64_t seq_len, uint64_t model_dim, uint64_t num_heads,
+                                                      const sme_ai_packed_linear_weight *q_weight,
+                                                      const float *q_bias,
+                                                      const sme_ai_packed_linear_weight *k_weight,
+                                                      const float *k_bias,
+                                                      const sme_ai_packed_linear_weight *v_weight,
+                                                      const float *v_bias,
+                                                      const sme_ai_packed_linear_weight *out_weight,
+                                                      const float *out_bias, int causal, float *output);
+
 /* ---- elementwise helpers of the Linear path (sme_ai_ops.h:241-270) --------
  * void, silently ignore NULL like the reference; host or device pointers. */
 void sme_ai_add_f32(float *output, const float *lhs, const float *rhs, uint64_t count);

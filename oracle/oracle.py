@@ -60,6 +60,7 @@ def lib() -> ctypes.CDLL:
             "orc_mlp_f16f32": (I, [P, U64, U64, P, U64, P, P, U64, P, P, I]),
             "orc_swiglu_f16f32": (I, [P, U64, U64, P, U64, P, P, P, P, U64, P, P]),
             "orc_pack_weight_f16_tiles": (None, [P, P, U64, U64]),
+            "orc_self_attention_f16f32": (I, [P, U64, U64, U64, P, P, P, P, P, P, P, P, I, P, P]),
             "orc_quantize_row_q8_K": (None, [P, P, I64, I]),
             "orc_quantize_row_q2_K": (None, [P, P, I64]),
             "orc_dequantize_row_q2_K": (None, [P, P, I64]),
@@ -138,6 +139,19 @@ def swiglu_f16f32(x16, batch, k, wg, hidden, bg, wu, bu, wd, n, bd):
                                  _p(wd), n, nz(bd), _p(out))
     assert rc == 0
     return out.reshape(batch, n)
+
+
+def self_attention_f16f32(x16, seq_len, model_dim, num_heads, wq, bq, wk, bk, wv, bv, wo, bo, causal,
+                          with_context=False):
+    """sme_ai_self_attention_ref_f16f32; with_context also returns the fp16 context."""
+    out = np.empty(seq_len * model_dim, np.float32)
+    ctx = np.empty(seq_len * model_dim, np.uint16)
+    nz = lambda a: None if a is None else _p(a)
+    rc = lib().orc_self_attention_f16f32(_p(x16), seq_len, model_dim, num_heads, _p(wq), nz(bq), _p(wk), nz(bk),
+                                         _p(wv), nz(bv), _p(wo), nz(bo), int(causal), _p(out), _p(ctx))
+    assert rc == 0
+    out = out.reshape(seq_len, model_dim)
+    return (out, ctx.reshape(seq_len, model_dim)) if with_context else out
 
 
 def pack_weight_f16_tiles(w16, k, n):

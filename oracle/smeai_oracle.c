@@ -217,6 +217,111 @@ int orc_swiglu_f16f32(const uint16_t *input, uint64_t batch, uint64_t in_feature
 }
 
 /*
+ * dot_f32_sve, sme_ai_ops.c:1268-1279: 16 float lanes (the 512-bit vector the
+ * API reports), lane l accumulating elements l, l+16, ... with a fused
+ * multiply-add (svmla); svaddv then reduces the lanes.  svaddv's order is
+ * implementation-defined; this restatement reduces pairwise (lane l + lane
+ * l+8, then +4, +2, +1), the order the device kernel uses.
+ */
+static float attn_dot(const float *a, const float *b, uint64_t n) {
+    float acc[16];
+    for (int l = 0; l < 16; ++l) acc[l] = 0.0f;
+    for (uint64_t i = 0; i < n; ++i) acc[i & 15] = fmaf(a[i], b[i], acc[i & 15]);
+    for (int w = 8; w >= 1; w >>= 1)
+        for (int l = 0; l < w; ++l) acc[l] = acc[l] + acc[l + w];
+    return acc[0];
+}
+
+/*
+ * Softmax of one score row in place: max, e_j = expf(v_j - max) summed
+ * sequentially (j ascending), then e_j / sum; a zero sum gives zeros.
+ * Causal rows replace v_j (j > i) by -1e30.
+ *   sme_ai_softmax_masked_rowwise_f32   sme_ai_ops.c:893-933
+ *   sme_ai_softmax_causal_rowwise_f32   sme_ai_ops.c:935-973
+ */
+static void attn_softmax_row(float *row, uint64_t n, uint64_t i, int causal) {
+    float mx = -INFINITY, sum = 0.0f;
+    for (uint64_t j = 0; j < n; ++j) {
+        float v = (causal && j > i) ? -1.0e30f : row[j];
+        if (v > mx) mx = v;
+    }
+    for (uint64_t j = 0; j < n; ++j) {
+        float v = (causal && j > i) ? -1.0e30f : row[j];
+        float ex = expf(v - mx);
+        row[j] = ex;
+        sum += ex;
+    }
+    for (uint64_t j = 0; j < n; ++j) row[j] = (sum == 0.0f) ? 0.0f : row[j] / sum;
+}
+
+/*
+ * Self-attention, sme_ai_self_attention_ref_f16f32 (sme_ai_ops.c:1320-1410):
+ *   Q, K, V = Linear(input) (k-ascending fp32 sums, + bias)
+ *   per head h (columns h*hd .. h*hd+hd-1, hd = model_dim / num_heads):
+ *     s_ij = dot(Q_i, K_j) * (1 / sqrtf(hd))      (attn_dot)
+ *     p_i  = softmax(s_i)                          (causal or not)
+ *     ctx_i = sum_j p_ij * V_j, j ascending, ctx = ctx + v*p unfused
+ *       (attention_weighted_sum_f32, :1287-1318: svmul_n then svadd)
+ *   output = Linear(fp16(ctx), out_weight) + out_bias.
+ * The reference writes V into `output` first and reuses one score buffer per
+ * head; neither changes a value.
+ */
+int orc_self_attention_f16f32(const uint16_t *input, uint64_t seq_len, uint64_t model_dim, uint64_t num_heads,
+                              const uint16_t *q_weight, const float *q_bias,
+                              const uint16_t *k_weight, const float *k_bias,
+                              const uint16_t *v_weight, const float *v_bias,
+                              const uint16_t *out_weight, const float *out_bias,
+                              int causal, float *output, uint16_t *context16) {
+    if (!input || !q_weight || !k_weight || !v_weight || !out_weight || !output || !seq_len || !model_dim ||
+        !num_heads || model_dim % num_heads)
+        return -1;
+    const uint64_t S = seq_len, D = model_dim, hd = model_dim / num_heads;
+    const float scale = 1.0f / sqrtf((float) hd);
+    float *q = (float *) malloc(S * D * sizeof(float));
+    float *k = (float *) malloc(S * D * sizeof(float));
+    float *v = (float *) malloc(S * D * sizeof(float));
+    float *ctx = (float *) malloc(S * D * sizeof(float));
+    float *sc = (float *) malloc(S * S * sizeof(float));
+    uint16_t *c16 = (uint16_t *) malloc(S * D * sizeof(uint16_t));
+    int rc = -2;
+    if (q && k && v && ctx && sc && c16) {
+        rc = orc_linear_f16f32(input, S, D, q_weight, D, q_bias, q, ORC_ACT_NONE);
+        if (!rc) rc = orc_linear_f16f32(input, S, D, k_weight, D, k_bias, k, ORC_ACT_NONE);
+        if (!rc) rc = orc_linear_f16f32(input, S, D, v_weight, D, v_bias, v, ORC_ACT_NONE);
+        for (uint64_t h = 0; !rc && h < num_heads; ++h) {
+            const uint64_t off = h * hd;
+            for (uint64_t i = 0; i < S; ++i)
+                for (uint64_t j = 0; j < S; ++j) sc[i * S + j] = attn_dot(q + i * D + off, k + j * D + off, hd) * scale;
+            for (uint64_t i = 0; i < S; ++i) attn_softmax_row(sc + i * S, S, i, causal);
+            for (uint64_t i = 0; i < S; ++i) {
+                float *c = ctx + i * D + off;
+                for (uint64_t d = 0; d < hd; ++d) c[d] = 0.0f;
+                for (uint64_t j = 0; j < S; ++j) {
+                    const float p = sc[i * S + j];
+                    const float *vr = v + j * D + off;
+                    for (uint64_t d = 0; d < hd; ++d) {
+                        float t = vr[d] * p;
+                        c[d] = c[d] + t;
+                    }
+                }
+            }
+        }
+        if (!rc) {
+            orc_floats_to_halves(ctx, c16, S * D);
+            if (context16) memcpy(context16, c16, S * D * sizeof(uint16_t));
+            rc = orc_linear_f16f32(c16, S, D, out_weight, D, out_bias, output, ORC_ACT_NONE);
+        }
+    }
+    free(q);
+    free(k);
+    free(v);
+    free(ctx);
+    free(sc);
+    free(c16);
+    return rc;
+}
+
+/*
  * The reference's packed layout: packed[n_tile][k_pad][16] fp32, zero padded,
  * k_pad/n_pad = round_up(., 16).  prepack_weight_fp16_to_sme_tiles,
  * sme_ai_ops.c:281-301.  (Used by tests to document the reference layout.)

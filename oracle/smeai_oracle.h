@@ -100,6 +100,16 @@ int orc_swiglu_f16f32(const uint16_t *input, uint64_t batch, uint64_t in_feature
                       float *output);
 void orc_pack_weight_f16_tiles(const uint16_t *weight, float *packed,
                                uint64_t in_features, uint64_t out_features);
+/* Self-attention (sme_ai_self_attention_ref_f16f32).  Weights are
+ * [model_dim][model_dim] fp16, biases may be NULL.  context16 (optional,
+ * seq_len * model_dim halves) receives the fp16 context fed to the output
+ * projection. */
+int orc_self_attention_f16f32(const uint16_t *input, uint64_t seq_len, uint64_t model_dim, uint64_t num_heads,
+                              const uint16_t *q_weight, const float *q_bias,
+                              const uint16_t *k_weight, const float *k_bias,
+                              const uint16_t *v_weight, const float *v_bias,
+                              const uint16_t *out_weight, const float *out_bias,
+                              int causal, float *output, uint16_t *context16);
 
 /* ---------------- Path B ---------------- */
 void orc_quantize_row_q8_K(const float *x, orc_block_q8_K *y, int64_t k, int rounding);

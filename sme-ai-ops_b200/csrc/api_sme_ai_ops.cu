@@ -28,7 +28,7 @@ uint64_t round16(uint64_t v) { return (v + 15) / 16 * 16; }
 struct WsPriv {
   uint32_t magic = kWsMagic;
   cudaStream_t stream = nullptr;
-  Staged in, out, b0, b1, b2;
+  Staged in, out, b0, b1, b2, b3;
   DeviceBuffer raw;  // raw weight of the "simple" path
 };
 
@@ -65,7 +65,7 @@ sme_ai_status check_ws(const sme_ai_workspace* ws, uint64_t batch, uint64_t in, 
 // Per-thread context of the workspace-less functions.
 struct RefCtx {
   cudaStream_t stream = nullptr;
-  Staged in, w, w2, w3, out, b0, b1, b2;
+  Staged in, w, w2, w3, w4, out, b0, b1, b2, b3;
   DeviceBuffer t0, t1, h16;
   bool init() {
     if (!stream && cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking) != cudaSuccess) {
@@ -579,6 +579,101 @@ sme_ai_status sme_ai_swiglu_sme_packed_f16f32(sme_ai_workspace* ws, const sme_ai
                                  static_cast<const float*>(w->b0.dev), static_cast<const float*>(w->b1.dev), hid, s);
   if (!r) r = linear_f16(hid, M, H, static_cast<const __half*>(pd->dev), pd->ldb, N,
                          static_cast<const float*>(w->b2.dev), kActNone, static_cast<float*>(w->out.dev), s);
+  if (!r) r = w->out.finish(s);
+  if (!r) r = sync(s);
+  return st(r);
+}
+
+// ---- self-attention (sme_ai_ops.c:1320-1499) -------------------------------------
+// Shared argument checks of both variants (:1343-1350 / :1435-1442).
+static sme_ai_status attention_checks(const sme_ai_workspace* ws, const void* input, uint64_t seq_len,
+                                      uint64_t model_dim, uint64_t num_heads, const void* q, const void* k,
+                                      const void* v, const void* o, const float* output) {
+  if (!ws || !input || !q || !k || !v || !o || !output || !seq_len || !model_dim || !num_heads ||
+      model_dim % num_heads)
+    return SME_AI_BAD_ARGUMENT;
+  if (seq_len > ws->max_batch || model_dim > ws->max_in_features || model_dim > ws->max_out_features)
+    return SME_AI_WORKSPACE_TOO_SMALL;
+  return SME_AI_OK;
+}
+
+// Q -> ws->tmp_f32, K -> ws->tmp2_f32 and V -> the output buffer, as the
+// reference places them; the attention kernel writes the fp16 context to
+// ws->tmp_f16 and the output projection overwrites V.
+sme_ai_status sme_ai_self_attention_ref_f16f32(sme_ai_workspace* ws, const sme_ai_fp16* input, uint64_t seq_len,
+                                               uint64_t model_dim, uint64_t num_heads, const sme_ai_fp16* q_weight,
+                                               const float* q_bias, const sme_ai_fp16* k_weight, const float* k_bias,
+                                               const sme_ai_fp16* v_weight, const float* v_bias,
+                                               const sme_ai_fp16* out_weight, const float* out_bias, int causal,
+                                               float* output) {
+  sme_ai_status c =
+      attention_checks(ws, input, seq_len, model_dim, num_heads, q_weight, k_weight, v_weight, out_weight, output);
+  if (c != SME_AI_OK) return c;
+  if (!priv(ws)) return SME_AI_BAD_ARGUMENT;
+  if (!device_ready()) return SME_AI_UNSUPPORTED;
+  RefCtx& x = rctx();
+  if (!x.init()) return SME_AI_UNSUPPORTED;
+  cudaStream_t s = x.stream;
+  const uint64_t S = seq_len, D = model_dim;
+  float *q = ws->tmp_f32, *k = ws->tmp2_f32;
+  __half* ctx16 = reinterpret_cast<__half*>(ws->tmp_f16);
+  int r = x.in.in(input, S * D * 2, s);
+  if (!r) r = x.w.in(q_weight, D * D * 2, s);
+  if (!r) r = x.w2.in(k_weight, D * D * 2, s);
+  if (!r) r = x.w3.in(v_weight, D * D * 2, s);
+  if (!r) r = x.w4.in(out_weight, D * D * 2, s);
+  if (!r) r = x.b0.in(q_bias, D * 4, s);
+  if (!r) r = x.b1.in(k_bias, D * 4, s);
+  if (!r) r = x.b2.in(v_bias, D * 4, s);
+  if (!r) r = x.b3.in(out_bias, D * 4, s);
+  if (!r) r = x.out.out(output, S * D * 4);
+  const __half* in = static_cast<const __half*>(x.in.dev);
+  float* v = static_cast<float*>(x.out.dev);
+  if (!r) r = linear_ref_f16(in, S, D, static_cast<const __half*>(x.w.dev), D, static_cast<const float*>(x.b0.dev),
+                             kActNone, q, s);
+  if (!r) r = linear_ref_f16(in, S, D, static_cast<const __half*>(x.w2.dev), D, static_cast<const float*>(x.b1.dev),
+                             kActNone, k, s);
+  if (!r) r = linear_ref_f16(in, S, D, static_cast<const __half*>(x.w3.dev), D, static_cast<const float*>(x.b2.dev),
+                             kActNone, v, s);
+  if (!r) r = attention_core(q, k, v, S, D, num_heads, causal, ctx16, s);
+  if (!r) r = linear_ref_f16(ctx16, S, D, static_cast<const __half*>(x.w4.dev), D,
+                             static_cast<const float*>(x.b3.dev), kActNone, v, s);
+  if (!r) r = x.out.finish(s);
+  if (!r) r = sync(s);
+  return st(r);
+}
+
+sme_ai_status sme_ai_self_attention_sme_packed_f16f32(
+    sme_ai_workspace* ws, const sme_ai_fp16* input, uint64_t seq_len, uint64_t model_dim, uint64_t num_heads,
+    const sme_ai_packed_linear_weight* q_weight, const float* q_bias, const sme_ai_packed_linear_weight* k_weight,
+    const float* k_bias, const sme_ai_packed_linear_weight* v_weight, const float* v_bias,
+    const sme_ai_packed_linear_weight* out_weight, const float* out_bias, int causal, float* output) {
+  sme_ai_status c =
+      attention_checks(ws, input, seq_len, model_dim, num_heads, q_weight, k_weight, v_weight, out_weight, output);
+  if (c != SME_AI_OK) return c;
+  for (const sme_ai_packed_linear_weight* pw : {q_weight, k_weight, v_weight, out_weight})
+    if (pw->in_features != model_dim || pw->out_features != model_dim) return SME_AI_BAD_ARGUMENT;
+  WsPriv* w = priv(ws);
+  const PackedPriv *pq = ppriv(q_weight), *pk = ppriv(k_weight), *pv = ppriv(v_weight), *po = ppriv(out_weight);
+  if (!w || !pq || !pk || !pv || !po || pq->is_f32 || pk->is_f32 || pv->is_f32 || po->is_f32)
+    return SME_AI_BAD_ARGUMENT;
+  cudaStream_t s = w->stream;
+  const uint64_t S = seq_len, D = model_dim;
+  float *q = ws->tmp_f32, *k = ws->tmp2_f32;
+  __half* ctx16 = reinterpret_cast<__half*>(ws->tmp_f16);
+  int r = w->in.in(input, S * D * 2, s);
+  if (!r) r = w->b0.in(q_bias, D * 4, s);
+  if (!r) r = w->b1.in(k_bias, D * 4, s);
+  if (!r) r = w->b2.in(v_bias, D * 4, s);
+  if (!r) r = w->b3.in(out_bias, D * 4, s);
+  if (!r) r = w->out.out(output, S * D * 4);
+  const __half* in = static_cast<const __half*>(w->in.dev);
+  float* v = static_cast<float*>(w->out.dev);
+  if (!r) r = packed_linear_dev(in, S, q_weight, static_cast<const float*>(w->b0.dev), kActNone, q, s);
+  if (!r) r = packed_linear_dev(in, S, k_weight, static_cast<const float*>(w->b1.dev), kActNone, k, s);
+  if (!r) r = packed_linear_dev(in, S, v_weight, static_cast<const float*>(w->b2.dev), kActNone, v, s);
+  if (!r) r = attention_core(q, k, v, S, D, num_heads, causal, ctx16, s);
+  if (!r) r = packed_linear_dev(ctx16, S, out_weight, static_cast<const float*>(w->b3.dev), kActNone, v, s);
   if (!r) r = w->out.finish(s);
   if (!r) r = sync(s);
   return st(r);

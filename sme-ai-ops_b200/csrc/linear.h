@@ -25,6 +25,10 @@ int linear_ref_f16(const __half* A, int64_t M, int64_t K, const __half* W, int64
 int f32_to_f16(const float* x, __half* y, int64_t n, cudaStream_t s);
 int silu_mul_f16(const float* g, const float* u, __half* h, int64_t n, cudaStream_t s);
 int act_inplace(float* x, int64_t n, int act, cudaStream_t s);
+// Per-head scores, softmax and weighted sum of the reference's self-attention:
+// Q, K, V [S][D] fp32 (heads of D / heads columns), ctx16 [S][D] fp16.
+int attention_core(const float* Q, const float* K, const float* V, int64_t S, int64_t D, int64_t heads, int causal,
+                   __half* ctx16, cudaStream_t s);
 int pack_weight_f16(const __half* w, int64_t K, int64_t N, __half* out, int64_t k_pad, int64_t n_pad,
                     cudaStream_t s);
 

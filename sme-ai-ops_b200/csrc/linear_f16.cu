@@ -169,6 +169,7 @@ int launch_linear(const TIn* A, int64_t M, int64_t K, int64_t lda, const TIn* B,
 template <typename TIn>
 __global__ void linear_ref_kernel(const TIn* __restrict__ A, int64_t M, int64_t K, const TIn* __restrict__ W,
                                   int64_t N, const float* __restrict__ bias, int act, float* __restrict__ C) {
+  pdl_wait();  // A may be the previous kernel's output
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= M * N) return;
   const int64_t r = i / N, c = i % N;
@@ -179,12 +180,14 @@ __global__ void linear_ref_kernel(const TIn* __restrict__ A, int64_t M, int64_t 
 }
 
 __global__ void f32_to_f16_kernel(const float* __restrict__ x, __half* __restrict__ y, int64_t n) {
+  pdl_wait();
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i < n) y[i] = __float2half_rn(x[i]);
 }
 
 __global__ void silu_mul_f16_kernel(const float* __restrict__ g, const float* __restrict__ u,
                                     __half* __restrict__ h, int64_t n) {
+  pdl_wait();
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i < n) {
     const float x = g[i];
@@ -194,6 +197,7 @@ __global__ void silu_mul_f16_kernel(const float* __restrict__ g, const float* __
 }
 
 __global__ void act_inplace_kernel(float* __restrict__ x, int64_t n, int act) {
+  pdl_wait();
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i < n) x[i] = activate(x[i], act);
 }
