@@ -17,6 +17,9 @@ Workloads (one "step" each):
                      over 64 distinct weight copies (352 MB > L2).
   prefill            activations [512,4096] (Q8_K per row) x W[11008,4096] Q2_K
                      on the tcgen05 tensor cores.
+  attention          sme_ai_self_attention packed, causal: 2048 tokens,
+                     model_dim 4096, 32 heads (fp16 weights, fp32 projections,
+                     scores, softmax and weighted sum); its own metric, tokens/s.
 
 Metric: "Q2_K mul_mat HBM GB/s": algorithmic bytes of every GEMV in the step
 (Q2_K weights + Q8_K activations + fp32 outputs), summed over ranks, per
@@ -51,7 +54,10 @@ def parse_args():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["decode", "gemv", "prefill"], default="decode")
+    ap.add_argument("--workload", choices=["decode", "gemv", "prefill", "attention"], default="decode")
+    ap.add_argument("--attn-seq", type=int, default=2048, help="attention workload: tokens")
+    ap.add_argument("--attn-dim", type=int, default=4096, help="attention workload: model_dim")
+    ap.add_argument("--attn-heads", type=int, default=32, help="attention workload: heads")
     ap.add_argument("--prefill-tokens", type=int, default=512, help="prefill workload: activation rows")
     ap.add_argument("--layers", type=int, default=32)
     ap.add_argument("--quant", choices=["fused", "separate", "mixed", "program"], default="program",
@@ -586,10 +592,183 @@ def run_ours(args):
     return 0
 
 
+def run_attention(args):
+    """--workload attention: one step = one causal self-attention of
+    args.attn_seq tokens through sme_ai_self_attention_packed_f16f32_device
+    (four packed projections + the score/softmax/weighted-sum kernel) on
+    device-resident data; e2e = the reference-facing synchronous entry point
+    with host buffers.  N GPUs run N independent replicas."""
+    import ctypes
+
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    import smeai_b200 as S
+
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    L = S.lib()
+    assert S.device_ready(), S.last_error()
+    Sq, D, H = args.attn_seq, args.attn_dim, args.attn_heads
+    hd = D // H
+    P = ctypes.c_void_p
+    rng = np.random.default_rng(1234)
+    f16 = lambda n, sc: (rng.standard_normal(n) * sc).astype(np.float16).view(np.uint16)
+    x16 = f16(Sq * D, 1.0)
+    w16 = [f16(D * D, D ** -0.5) for _ in range(4)]
+    b32 = [(rng.standard_normal(D) * 0.02).astype(np.float32) for _ in range(4)]
+    ws = S.Workspace()
+    assert L.sme_ai_workspace_init(ctypes.byref(ws), Sq, D, D) == 0, S.last_error()
+    pws = []
+    for w in w16:
+        pw = S.PackedWeight()
+        assert L.sme_ai_packed_linear_weight_init(ctypes.byref(pw), P(w.ctypes.data), D, D) == 0, S.last_error()
+        pws.append(pw)
+    xd = torch.from_numpy(x16).to(dev)
+    bd = [torch.from_numpy(b).to(dev) for b in b32]
+    od = torch.empty(Sq * D, dtype=torch.float32, device=dev)
+    stream = torch.cuda.Stream(device=dev)
+    d = lambda t: P(t.data_ptr())
+
+    def step():
+        r = L.sme_ai_self_attention_packed_f16f32_device(
+            ctypes.byref(ws), d(xd), Sq, D, H, ctypes.byref(pws[0]), d(bd[0]), ctypes.byref(pws[1]), d(bd[1]),
+            ctypes.byref(pws[2]), d(bd[2]), ctypes.byref(pws[3]), d(bd[3]), 1, d(od), P(stream.cuda_stream))
+        assert r == 0, S.last_error()
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    for _ in range(max(3, args.warmup)):
+        step()
+    stream.synchronize()
+    barrier()
+    sampler = ClockSampler(local)
+    sampler.start()
+    time.sleep(0.3)
+    torch.cuda.synchronize()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        step()
+    e1.record(stream)
+    e1.synchronize()
+    barrier()
+    ms = e0.elapsed_time(e1) / args.steps
+    clocks = sampler.stop()
+    if world > 1:
+        t = torch.tensor([ms], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    value = world * Sq / (ms / 1e3)
+
+    # the core kernel alone (events on its stream; Q/K/V from the last step)
+    qd = torch.empty(Sq * D, dtype=torch.float32, device=dev)
+    kd, vd = torch.empty_like(qd), torch.empty_like(qd)
+    for t in (qd, kd, vd):
+        t.normal_()
+    cd = torch.empty(Sq * D, dtype=torch.float16, device=dev)
+    evs = []
+    with torch.cuda.stream(stream):
+        torch.cuda._sleep(20_000_000)
+        for _ in range(5):
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            assert L.sme_ai_self_attention_core_f32_device(d(qd), d(kd), d(vd), Sq, D, H, 1, d(cd),
+                                                           P(stream.cuda_stream)) == 0, S.last_error()
+            b.record(stream)
+            evs.append((a, b))
+    stream.synchronize()
+    core_ms = sorted(a.elapsed_time(b) for a, b in evs)[len(evs) // 2]
+    pairs = Sq * (Sq + 1) // 2                    # (i, j <= i) score / weight pairs per head
+    core_flops = 4 * hd * pairs * H               # QK^T fma + (mul, add) of the weighted sum
+    proj_flops = 4 * 2 * Sq * D * D
+    fp32_peak = 148 * 128 * 2 * 1.965e9 / 1e12   # nominal FP32 CUDA-core rate at the max clock
+    achieved = core_flops / (core_ms / 1e3) / 1e12
+    roofline = {"bound": "fp32", "kernel": "attention_kernel (scores + softmax + weighted sum)",
+                "achieved": achieved, "peak": fp32_peak, "unit": "TFLOP/s", "frac": achieved / fp32_peak,
+                "peak_kind": "nominal (no measured fp32 CUDA-core peak on this pool)", "traffic": None,
+                "flops_per_launch": core_flops, "median_launch_us": core_ms * 1e3,
+                "core_share_of_step": core_ms / ms, "projection_flops_per_step": proj_flops}
+
+    # e2e: the synchronous reference-facing call with host buffers
+    out_h = np.zeros(Sq * D, np.float32)
+    pp = lambda a: P(a.ctypes.data)
+
+    def e2e_step():
+        r = L.sme_ai_self_attention_sme_packed_f16f32(
+            ctypes.byref(ws), pp(x16), Sq, D, H, ctypes.byref(pws[0]), pp(b32[0]), ctypes.byref(pws[1]),
+            pp(b32[1]), ctypes.byref(pws[2]), pp(b32[2]), ctypes.byref(pws[3]), pp(b32[3]), 1, pp(out_h))
+        assert r == 0, S.last_error()
+
+    e2e_step()
+    barrier()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        e2e_step()
+    e2e_ms = (time.perf_counter() - t0) / args.steps * 1e3
+    if world > 1:
+        t = torch.tensor([e2e_ms], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        from oracle import oracle as O
+        O.build()
+        cs = 8
+        t0, reps = time.perf_counter(), 0
+        while True:
+            O.self_attention_f16f32(x16[:cs * D], cs, D, H, *[a for pair in zip(w16, b32) for a in pair], 1)
+            reps += 1
+            if time.perf_counter() - t0 >= min(args.cpu_seconds, 30.0):
+                break
+        per = (time.perf_counter() - t0) / reps
+        cpu = {"value": cs / per, "unit": "tokens/s", "cores": 1, "kind": "port",
+               "sample": f"{reps} x the oracle's self-attention (the reference's ref path restated in scalar C, "
+                         f"its Linear's column-strided weight reads included) on the first {cs} tokens at "
+                         f"model_dim {D}, {H} heads, causal; {per * 1e3:.0f} ms each"}
+    for pw in pws:
+        L.sme_ai_packed_linear_weight_destroy(ctypes.byref(pw))
+    L.sme_ai_workspace_destroy(ctypes.byref(ws))
+    if rank == 0:
+        line = {
+            "metric": "self-attention (packed, causal) tokens/s", "value": value, "unit": "tokens/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16xf32",
+            "data": "synthetic",
+            "config": {"workload": f"causal self-attention, {Sq} tokens, model_dim {D}, {H} heads (head_dim {hd}); "
+                                   "fp16 packed weights ~N(0, 1/D), fp16 input ~N(0,1)",
+                       "global_batch": world * Sq, "seq_len": Sq, "parallelism": f"{world} replicas",
+                       "l2": "inputs larger than L2: a step touches 4 x 32 MB of fp16 weights, the 16 MB input "
+                             "and 3 x 32 MB of fp32 Q/K/V plus the output (~270 MB > 126 MB)"},
+            "clocks": clocks,
+            "e2e": {"value": world * Sq / (e2e_ms / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": Sq * D * 2 + 4 * D * 4,
+                    "d2h_bytes_per_step": Sq * D * 4, "ms_per_step": e2e_ms},
+            "gpu_launches": 5 * args.steps,
+            "roofline": roofline,
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+    barrier()
+    if world > 1:
+        dist.destroy_process_group()
+    return 0
+
+
 def main():
     args = parse_args()
     if args.impl == "reference":
         return run_reference(args)
+    if args.workload == "attention":
+        return run_attention(args)
     return run_ours(args)
 
 

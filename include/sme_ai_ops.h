@@ -237,6 +237,31 @@ sme_ai_status sme_ai_linear_packed_f16f32_device(const sme_ai_fp16 *input, uint6
                                                  const sme_ai_packed_linear_weight *packed_weight,
                                                  const float *bias, int act, float *output, void *stream);
 
+/* Asynchronous device-pointer form of sme_ai_self_attention_sme_packed_f16f32:
+ * same checks and results; input, biases and output are device memory, work
+ * is queued on `stream` (a cudaStream_t, NULL = legacy default) and the call
+ * returns without waiting.  Q, K and the fp16 context live in the
+ * workspace's device scratch, so calls sharing a workspace must be ordered
+ * on one stream. */
+sme_ai_status sme_ai_self_attention_packed_f16f32_device(const sme_ai_workspace *ws, const sme_ai_fp16 *input,
+                                                         uint64_t seq_len, uint64_t model_dim, uint64_t num_heads,
+                                                         const sme_ai_packed_linear_weight *q_weight,
+                                                         const float *q_bias,
+                                                         const sme_ai_packed_linear_weight *k_weight,
+                                                         const float *k_bias,
+                                                         const sme_ai_packed_linear_weight *v_weight,
+                                                         const float *v_bias,
+                                                         const sme_ai_packed_linear_weight *out_weight,
+                                                         const float *out_bias, int causal, float *output,
+                                                         void *stream);
+
+/* The per-head core alone (scores, softmax, weighted sum; the reference's
+ * sme_ai_ops.c:1383-1402 loop): q, k, v [seq_len][model_dim] fp32 device
+ * arrays, context [seq_len][model_dim] fp16, queued on `stream`. */
+sme_ai_status sme_ai_self_attention_core_f32_device(const float *q, const float *k, const float *v,
+                                                    uint64_t seq_len, uint64_t model_dim, uint64_t num_heads,
+                                                    int causal, sme_ai_fp16 *context, void *stream);
+
 /* SwiGLU on packed weights for callers that cannot allocate device memory.
  * No counterpart in the reference.  Some callers may not call cudaMalloc at
  * all: code running under a framework that owns the whole device heap

@@ -643,6 +643,33 @@ sme_ai_status sme_ai_self_attention_ref_f16f32(sme_ai_workspace* ws, const sme_a
   return st(r);
 }
 
+// Checks of the packed variant beyond the shared ones (:1443-1448).
+static sme_ai_status attention_packed_checks(uint64_t model_dim, const sme_ai_packed_linear_weight* const (&pw)[4],
+                                             const PackedPriv* (&pp)[4]) {
+  for (int t = 0; t < 4; ++t) {
+    if (pw[t]->in_features != model_dim || pw[t]->out_features != model_dim) return SME_AI_BAD_ARGUMENT;
+    pp[t] = ppriv(pw[t]);
+    if (!pp[t] || pp[t]->is_f32) return SME_AI_BAD_ARGUMENT;
+  }
+  return SME_AI_OK;
+}
+
+// The packed attention on device pointers, queued on s: projections into
+// ws->tmp_f32 (Q), ws->tmp2_f32 (K) and `out` (V), the attention kernel into
+// ws->tmp_f16, the output projection over V.
+static int attention_packed_dev(const sme_ai_workspace* ws, const __half* in, uint64_t S, uint64_t D, uint64_t heads,
+                                const sme_ai_packed_linear_weight* const (&pw)[4], const float* const (&bias)[4],
+                                int causal, float* out, cudaStream_t s) {
+  float *q = ws->tmp_f32, *k = ws->tmp2_f32;
+  __half* ctx16 = reinterpret_cast<__half*>(ws->tmp_f16);
+  int r = packed_linear_dev(in, S, pw[0], bias[0], kActNone, q, s);
+  if (!r) r = packed_linear_dev(in, S, pw[1], bias[1], kActNone, k, s);
+  if (!r) r = packed_linear_dev(in, S, pw[2], bias[2], kActNone, out, s);
+  if (!r) r = attention_core(q, k, out, S, D, heads, causal, ctx16, s);
+  if (!r) r = packed_linear_dev(ctx16, S, pw[3], bias[3], kActNone, out, s);
+  return r;
+}
+
 sme_ai_status sme_ai_self_attention_sme_packed_f16f32(
     sme_ai_workspace* ws, const sme_ai_fp16* input, uint64_t seq_len, uint64_t model_dim, uint64_t num_heads,
     const sme_ai_packed_linear_weight* q_weight, const float* q_bias, const sme_ai_packed_linear_weight* k_weight,
@@ -651,32 +678,55 @@ sme_ai_status sme_ai_self_attention_sme_packed_f16f32(
   sme_ai_status c =
       attention_checks(ws, input, seq_len, model_dim, num_heads, q_weight, k_weight, v_weight, out_weight, output);
   if (c != SME_AI_OK) return c;
-  for (const sme_ai_packed_linear_weight* pw : {q_weight, k_weight, v_weight, out_weight})
-    if (pw->in_features != model_dim || pw->out_features != model_dim) return SME_AI_BAD_ARGUMENT;
+  const sme_ai_packed_linear_weight* const pw[4] = {q_weight, k_weight, v_weight, out_weight};
+  const PackedPriv* pp[4];
+  c = attention_packed_checks(model_dim, pw, pp);
+  if (c != SME_AI_OK) return c;
   WsPriv* w = priv(ws);
-  const PackedPriv *pq = ppriv(q_weight), *pk = ppriv(k_weight), *pv = ppriv(v_weight), *po = ppriv(out_weight);
-  if (!w || !pq || !pk || !pv || !po || pq->is_f32 || pk->is_f32 || pv->is_f32 || po->is_f32)
-    return SME_AI_BAD_ARGUMENT;
+  if (!w) return SME_AI_BAD_ARGUMENT;
   cudaStream_t s = w->stream;
   const uint64_t S = seq_len, D = model_dim;
-  float *q = ws->tmp_f32, *k = ws->tmp2_f32;
-  __half* ctx16 = reinterpret_cast<__half*>(ws->tmp_f16);
   int r = w->in.in(input, S * D * 2, s);
   if (!r) r = w->b0.in(q_bias, D * 4, s);
   if (!r) r = w->b1.in(k_bias, D * 4, s);
   if (!r) r = w->b2.in(v_bias, D * 4, s);
   if (!r) r = w->b3.in(out_bias, D * 4, s);
   if (!r) r = w->out.out(output, S * D * 4);
-  const __half* in = static_cast<const __half*>(w->in.dev);
-  float* v = static_cast<float*>(w->out.dev);
-  if (!r) r = packed_linear_dev(in, S, q_weight, static_cast<const float*>(w->b0.dev), kActNone, q, s);
-  if (!r) r = packed_linear_dev(in, S, k_weight, static_cast<const float*>(w->b1.dev), kActNone, k, s);
-  if (!r) r = packed_linear_dev(in, S, v_weight, static_cast<const float*>(w->b2.dev), kActNone, v, s);
-  if (!r) r = attention_core(q, k, v, S, D, num_heads, causal, ctx16, s);
-  if (!r) r = packed_linear_dev(ctx16, S, out_weight, static_cast<const float*>(w->b3.dev), kActNone, v, s);
+  const float* const bias[4] = {static_cast<const float*>(w->b0.dev), static_cast<const float*>(w->b1.dev),
+                                static_cast<const float*>(w->b2.dev), static_cast<const float*>(w->b3.dev)};
+  if (!r) r = attention_packed_dev(ws, static_cast<const __half*>(w->in.dev), S, D, num_heads, pw, bias, causal,
+                                   static_cast<float*>(w->out.dev), s);
   if (!r) r = w->out.finish(s);
   if (!r) r = sync(s);
   return st(r);
+}
+
+sme_ai_status sme_ai_self_attention_packed_f16f32_device(
+    const sme_ai_workspace* ws, const sme_ai_fp16* input, uint64_t seq_len, uint64_t model_dim, uint64_t num_heads,
+    const sme_ai_packed_linear_weight* q_weight, const float* q_bias, const sme_ai_packed_linear_weight* k_weight,
+    const float* k_bias, const sme_ai_packed_linear_weight* v_weight, const float* v_bias,
+    const sme_ai_packed_linear_weight* out_weight, const float* out_bias, int causal, float* output, void* stream) {
+  sme_ai_status c =
+      attention_checks(ws, input, seq_len, model_dim, num_heads, q_weight, k_weight, v_weight, out_weight, output);
+  if (c != SME_AI_OK) return c;
+  const sme_ai_packed_linear_weight* const pw[4] = {q_weight, k_weight, v_weight, out_weight};
+  const PackedPriv* pp[4];
+  c = attention_packed_checks(model_dim, pw, pp);
+  if (c != SME_AI_OK) return c;
+  if (!priv(ws)) return SME_AI_BAD_ARGUMENT;
+  const float* const bias[4] = {q_bias, k_bias, v_bias, out_bias};
+  return st(attention_packed_dev(ws, reinterpret_cast<const __half*>(input), seq_len, model_dim, num_heads, pw, bias,
+                                 causal, output, static_cast<cudaStream_t>(stream)));
+}
+
+sme_ai_status sme_ai_self_attention_core_f32_device(const float* q, const float* k, const float* v, uint64_t seq_len,
+                                                    uint64_t model_dim, uint64_t num_heads, int causal,
+                                                    sme_ai_fp16* context, void* stream) {
+  if (!q || !k || !v || !context || !seq_len || !model_dim || !num_heads || model_dim % num_heads)
+    return SME_AI_BAD_ARGUMENT;
+  if (!device_ready()) return SME_AI_UNSUPPORTED;
+  return st(attention_core(q, k, v, (int64_t)seq_len, (int64_t)model_dim, (int64_t)num_heads, causal,
+                           reinterpret_cast<__half*>(context), static_cast<cudaStream_t>(stream)));
 }
 
 // ---- elementwise -----------------------------------------------------------------

@@ -145,6 +145,9 @@ def _declare(L: ctypes.CDLL) -> None:
         "sme_ai_swiglu_packed_f16f32_noalloc": (I, [P, U64, PW, P, PW, P, PW, P, P, P]),
         "sme_ai_self_attention_ref_f16f32": (I, [WS, P, U64, U64, U64, P, P, P, P, P, P, P, P, I, P]),
         "sme_ai_self_attention_sme_packed_f16f32": (I, [WS, P, U64, U64, U64, PW, P, PW, P, PW, P, PW, P, I, P]),
+        "sme_ai_self_attention_packed_f16f32_device": (I, [WS, P, U64, U64, U64, PW, P, PW, P, PW, P, PW, P, I, P,
+                                                           P]),
+        "sme_ai_self_attention_core_f32_device": (I, [P, P, P, U64, U64, U64, I, P, P]),
         "sme_ai_add_f32": (None, [P, P, P, U64]),
         "sme_ai_mul_f32": (None, [P, P, P, U64]),
         "sme_ai_residual_add_f32": (None, [P, P, P, U64]),

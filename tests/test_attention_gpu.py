@@ -166,3 +166,42 @@ def test_attention_status_codes(L, oracle):
         L.sme_ai_packed_linear_weight_destroy(ctypes.byref(a))
     for w in (ws, small):
         L.sme_ai_workspace_destroy(ctypes.byref(w))
+
+
+def test_attention_device_entry_points(L, oracle):
+    """The asynchronous device-pointer form on a caller's stream equals the
+    synchronous call bit for bit; the core alone, fed the restatement's Q, K
+    and V, reproduces its fp16 context."""
+    S_, D, H = 40, 128, 4
+    x16, (wq, wk, wv, wo), (bq, bk, bv, bo) = data(oracle, S_, D, 4001)
+    ws = make_ws(L, S_, D, D)
+    pws = [make_packed(L, w, D, D) for w in (wq, wk, wv, wo)]
+    host = np.zeros((S_, D), np.float32)
+    assert L.sme_ai_self_attention_sme_packed_f16f32(ctypes.byref(ws), p(x16), S_, D, H, ctypes.byref(pws[0]), p(bq),
+                                                     ctypes.byref(pws[1]), p(bk), ctypes.byref(pws[2]), p(bv),
+                                                     ctypes.byref(pws[3]), p(bo), 1, p(host)) == 0
+    dev = lambda a: torch.from_numpy(a).cuda()
+    d = lambda t: P(t.data_ptr())
+    xd, bqd, bkd, bvd, bod = (dev(a) for a in (x16, bq, bk, bv, bo))
+    od = torch.zeros(S_ * D, dtype=torch.float32, device="cuda")
+    st = torch.cuda.Stream()
+    assert L.sme_ai_self_attention_packed_f16f32_device(
+        ctypes.byref(ws), d(xd), S_, D, H, ctypes.byref(pws[0]), d(bqd), ctypes.byref(pws[1]), d(bkd),
+        ctypes.byref(pws[2]), d(bvd), ctypes.byref(pws[3]), d(bod), 1, d(od), P(st.cuda_stream)) == 0
+    st.synchronize()
+    assert np.array_equal(od.cpu().numpy().reshape(S_, D), host)
+
+    _, c_exp = oracle.self_attention_f16f32(x16, S_, D, H, wq, bq, wk, bk, wv, bv, wo, bo, 1, with_context=True)
+    q, k, v = (dev(oracle.linear_f16f32(x16, S_, D, w, D, b)) for w, b in ((wq, bq), (wk, bk), (wv, bv)))
+    ctx = torch.zeros(S_ * D, dtype=torch.float16, device="cuda")
+    assert L.sme_ai_self_attention_core_f32_device(d(q), d(k), d(v), S_, D, H, 1, d(ctx), P(st.cuda_stream)) == 0
+    st.synchronize()
+    c = ctx.cpu().numpy().view(np.uint16).reshape(S_, D)
+    assert np.mean(c == c_exp) >= 0.99
+    cf, ef = c.view(np.float16).astype(np.float64), c_exp.view(np.float16).astype(np.float64)
+    assert np.all(np.abs(cf - ef) <= np.abs(ef) * 2.0 ** -10 + 1e-7)
+    assert L.sme_ai_self_attention_core_f32_device(d(q), d(k), d(v), S_, D, 3, 1, d(ctx), None) == \
+        S.SME_AI_BAD_ARGUMENT
+    for a in pws:
+        L.sme_ai_packed_linear_weight_destroy(ctypes.byref(a))
+    L.sme_ai_workspace_destroy(ctypes.byref(ws))
