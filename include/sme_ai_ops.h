@@ -240,10 +240,13 @@ sme_ai_status sme_ai_linear_packed_f16f32_device(const sme_ai_fp16 *input, uint6
 /* Asynchronous device-pointer form of sme_ai_self_attention_sme_packed_f16f32:
  * same checks and results; input, biases and output are device memory, work
  * is queued on `stream` (a cudaStream_t, NULL = legacy default) and the call
- * returns without waiting.  Q, K and the fp16 context live in the
- * workspace's device scratch, so calls sharing a workspace must be ordered
- * on one stream. */
-sme_ai_status sme_ai_self_attention_packed_f16f32_device(const sme_ai_workspace *ws, const sme_ai_fp16 *input,
+ * returns without waiting.  Q, K, the fp16 context and the score matrix
+ * live in the workspace's device scratch, so calls sharing a workspace must
+ * be ordered on one stream.  For head_dim 32, 64 or 128 and 256 <= seq_len
+ * <= 16384 the scores of a chunk of heads (at most 256 MB, or one head) are
+ * kept in a workspace-owned device buffer that the first call needing it
+ * allocates (a cudaMalloc, which may synchronize the device). */
+sme_ai_status sme_ai_self_attention_packed_f16f32_device(sme_ai_workspace *ws, const sme_ai_fp16 *input,
                                                          uint64_t seq_len, uint64_t model_dim, uint64_t num_heads,
                                                          const sme_ai_packed_linear_weight *q_weight,
                                                          const float *q_bias,
@@ -257,7 +260,9 @@ sme_ai_status sme_ai_self_attention_packed_f16f32_device(const sme_ai_workspace 
 
 /* The per-head core alone (scores, softmax, weighted sum; the reference's
  * sme_ai_ops.c:1383-1402 loop): q, k, v [seq_len][model_dim] fp32 device
- * arrays, context [seq_len][model_dim] fp16, queued on `stream`. */
+ * arrays, context [seq_len][model_dim] fp16, queued on `stream`.  The score
+ * buffer of the tiled shapes (see above) belongs to the calling thread: calls
+ * from one thread must be ordered on one stream. */
 sme_ai_status sme_ai_self_attention_core_f32_device(const float *q, const float *k, const float *v,
                                                     uint64_t seq_len, uint64_t model_dim, uint64_t num_heads,
                                                     int causal, sme_ai_fp16 *context, void *stream);

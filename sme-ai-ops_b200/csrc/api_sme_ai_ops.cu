@@ -29,7 +29,8 @@ struct WsPriv {
   uint32_t magic = kWsMagic;
   cudaStream_t stream = nullptr;
   Staged in, out, b0, b1, b2, b3;
-  DeviceBuffer raw;  // raw weight of the "simple" path
+  DeviceBuffer raw;
+  DeviceBuffer scores;  // self-attention score matrix (tiled path)  // raw weight of the "simple" path
 };
 
 // Library state behind packed->packed_weight.
@@ -635,7 +636,10 @@ sme_ai_status sme_ai_self_attention_ref_f16f32(sme_ai_workspace* ws, const sme_a
                              kActNone, k, s);
   if (!r) r = linear_ref_f16(in, S, D, static_cast<const __half*>(x.w3.dev), D, static_cast<const float*>(x.b2.dev),
                              kActNone, v, s);
-  if (!r) r = attention_core(q, k, v, S, D, num_heads, causal, ctx16, s);
+  DeviceBuffer& sc = priv(ws)->scores;
+  const size_t sc_bytes = attention_scratch_bytes(S, D, num_heads);
+  if (!r && sc_bytes) r = sc.reserve(sc_bytes);
+  if (!r) r = attention_core(q, k, v, S, D, num_heads, causal, ctx16, static_cast<float*>(sc.ptr), sc.cap, s);
   if (!r) r = linear_ref_f16(ctx16, S, D, static_cast<const __half*>(x.w4.dev), D,
                              static_cast<const float*>(x.b3.dev), kActNone, v, s);
   if (!r) r = x.out.finish(s);
@@ -657,7 +661,7 @@ static sme_ai_status attention_packed_checks(uint64_t model_dim, const sme_ai_pa
 // The packed attention on device pointers, queued on s: projections into
 // ws->tmp_f32 (Q), ws->tmp2_f32 (K) and `out` (V), the attention kernel into
 // ws->tmp_f16, the output projection over V.
-static int attention_packed_dev(const sme_ai_workspace* ws, const __half* in, uint64_t S, uint64_t D, uint64_t heads,
+static int attention_packed_dev(sme_ai_workspace* ws, const __half* in, uint64_t S, uint64_t D, uint64_t heads,
                                 const sme_ai_packed_linear_weight* const (&pw)[4], const float* const (&bias)[4],
                                 int causal, float* out, cudaStream_t s) {
   float *q = ws->tmp_f32, *k = ws->tmp2_f32;
@@ -665,7 +669,10 @@ static int attention_packed_dev(const sme_ai_workspace* ws, const __half* in, ui
   int r = packed_linear_dev(in, S, pw[0], bias[0], kActNone, q, s);
   if (!r) r = packed_linear_dev(in, S, pw[1], bias[1], kActNone, k, s);
   if (!r) r = packed_linear_dev(in, S, pw[2], bias[2], kActNone, out, s);
-  if (!r) r = attention_core(q, k, out, S, D, heads, causal, ctx16, s);
+  DeviceBuffer& sc = priv(ws)->scores;
+  const size_t sc_bytes = attention_scratch_bytes(S, D, heads);
+  if (!r && sc_bytes) r = sc.reserve(sc_bytes);
+  if (!r) r = attention_core(q, k, out, S, D, heads, causal, ctx16, static_cast<float*>(sc.ptr), sc.cap, s);
   if (!r) r = packed_linear_dev(ctx16, S, pw[3], bias[3], kActNone, out, s);
   return r;
 }
@@ -702,7 +709,7 @@ sme_ai_status sme_ai_self_attention_sme_packed_f16f32(
 }
 
 sme_ai_status sme_ai_self_attention_packed_f16f32_device(
-    const sme_ai_workspace* ws, const sme_ai_fp16* input, uint64_t seq_len, uint64_t model_dim, uint64_t num_heads,
+    sme_ai_workspace* ws, const sme_ai_fp16* input, uint64_t seq_len, uint64_t model_dim, uint64_t num_heads,
     const sme_ai_packed_linear_weight* q_weight, const float* q_bias, const sme_ai_packed_linear_weight* k_weight,
     const float* k_bias, const sme_ai_packed_linear_weight* v_weight, const float* v_bias,
     const sme_ai_packed_linear_weight* out_weight, const float* out_bias, int causal, float* output, void* stream) {
@@ -725,8 +732,15 @@ sme_ai_status sme_ai_self_attention_core_f32_device(const float* q, const float*
   if (!q || !k || !v || !context || !seq_len || !model_dim || !num_heads || model_dim % num_heads)
     return SME_AI_BAD_ARGUMENT;
   if (!device_ready()) return SME_AI_UNSUPPORTED;
+  thread_local DeviceBuffer sc;
+  const size_t sc_bytes = attention_scratch_bytes((int64_t)seq_len, (int64_t)model_dim, (int64_t)num_heads);
+  if (sc_bytes) {
+    const int r = sc.reserve(sc_bytes);
+    if (r) return st(r);
+  }
   return st(attention_core(q, k, v, (int64_t)seq_len, (int64_t)model_dim, (int64_t)num_heads, causal,
-                           reinterpret_cast<__half*>(context), static_cast<cudaStream_t>(stream)));
+                           reinterpret_cast<__half*>(context), static_cast<float*>(sc.ptr), sc.cap,
+                           static_cast<cudaStream_t>(stream)));
 }
 
 // ---- elementwise -----------------------------------------------------------------

@@ -27,8 +27,12 @@ int silu_mul_f16(const float* g, const float* u, __half* h, int64_t n, cudaStrea
 int act_inplace(float* x, int64_t n, int act, cudaStream_t s);
 // Per-head scores, softmax and weighted sum of the reference's self-attention:
 // Q, K, V [S][D] fp32 (heads of D / heads columns), ctx16 [S][D] fp16.
+// `scores` (device, scores_bytes) backs the tiled kernels' score matrix;
+// attention_scratch_bytes() gives the size they need (0 when the fused
+// one-kernel path serves the shape).  Without it the fused path runs.
+size_t attention_scratch_bytes(int64_t S, int64_t D, int64_t heads);
 int attention_core(const float* Q, const float* K, const float* V, int64_t S, int64_t D, int64_t heads, int causal,
-                   __half* ctx16, cudaStream_t s);
+                   __half* ctx16, float* scores, size_t scores_bytes, cudaStream_t s);
 int pack_weight_f16(const __half* w, int64_t K, int64_t N, __half* out, int64_t k_pad, int64_t n_pad,
                     cudaStream_t s);
 

@@ -14,6 +14,8 @@
 //   kEpiF16      h = fp16(act(acc + bias))               (MLP hidden, :504-529)
 //   kEpiSwiGLU   h = fp16(silu(acc_g + bg) * (acc_u + bu)) (gate and up in one
 //                kernel: two accumulator sets over one A tile, :1227-1265)
+#include <type_traits>
+
 #include "common.cuh"
 #include "linear.h"
 
@@ -146,12 +148,178 @@ __global__ void __launch_bounds__((BM / TM) * (BN / TN)) linear_ffma_kernel(
   }
 }
 
+// Register-tiled FFMA GEMM for large fp16 problems.  CTA tile 128 x BN
+// (BN = 16 * TN) of outputs, 256 threads as 16 x 16, each owning 8 x TN
+// outputs: rows ty*4 + {0..3} and 64 + ty*4 + {0..3}, columns tx*TN/2 + ..
+// and BN/2 + tx*TN/2 + .., so every shared-memory vector read of a warp is
+// conflict-free.  k advances 16 at a time: the next step's operands are
+// fetched into registers (one 16-byte load of A and one TN-half load of B
+// per thread) while the current step's FFMAs run, then converted to fp32 and
+// stored into the other shared buffer.  Each output still sums its products
+// in k order with one accumulator, so results are those of linear_ffma_kernel
+// bit for bit.  Requirements (checked by the launcher): K and lda multiples of
+// 8, ldb a multiple of 16, 16-byte aligned A and B, B zero padded to
+// round_up(K, 16) rows and ldb columns (the packed-weight layout).
+template <int TN, int EPI>
+__global__ void __launch_bounds__(256, 2) linear_tiled_kernel(
+    const __half* __restrict__ A, int64_t M, int64_t K, int64_t lda, const __half* __restrict__ B,
+    const __half* __restrict__ B2, int64_t ldb, int64_t N, const float* __restrict__ bias,
+    const float* __restrict__ bias2, int act, float* __restrict__ C, __half* __restrict__ C16, int64_t ldc) {
+  constexpr int BM = 128, BN = 16 * TN, HN = TN / 2;
+  constexpr bool kPair = EPI == kEpiSwiGLU;
+  using BVec = typename std::conditional<TN == 8, uint4, uint2>::type;
+  __shared__ __align__(16) float As[2][BK][BM];
+  __shared__ __align__(16) float Bs[2][BK][BN];
+  __shared__ __align__(16) float Bs2[kPair ? 2 : 1][BK][kPair ? BN : 4];
+
+  const int tid = threadIdx.x;
+  const int tx = tid & 15, ty = tid >> 4;
+  const int64_t m0 = (int64_t)blockIdx.y * BM, n0 = (int64_t)blockIdx.x * BN;
+  // operand fetch coordinates: A row tid % 128, k half tid / 128; B row tid / 16, TN columns
+  const int ra = tid & 127, ka = (tid >> 7) * 8;
+  const int rb = tid >> 4, cb = (tid & 15) * TN;
+  const bool a_row = m0 + ra < M;
+  const bool b_col = n0 + cb + TN <= ldb;
+  const __half* a_src = A + (a_row ? (m0 + ra) * lda : 0) + ka;
+  const __half* b_src = B + (int64_t)rb * ldb + n0 + cb;
+  const __half* b2_src = kPair ? B2 + (int64_t)rb * ldb + n0 + cb : nullptr;
+
+  float acc[8][TN], acc2[kPair ? 8 : 1][kPair ? TN : 1];
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+#pragma unroll
+    for (int j = 0; j < TN; ++j) acc[i][j] = 0.f;
+  if constexpr (kPair) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+#pragma unroll
+      for (int j = 0; j < TN; ++j) acc2[i][j] = 0.f;
+  }
+
+  pdl_trigger();
+  pdl_wait();
+
+  uint4 av;
+  BVec bv, bv2;
+  auto fetch = [&](int64_t k0) {
+    av = (a_row && k0 + ka < K) ? *reinterpret_cast<const uint4*>(a_src + k0) : make_uint4(0, 0, 0, 0);
+    if (b_col) {
+      bv = *reinterpret_cast<const BVec*>(b_src + k0 * ldb);
+      if constexpr (kPair) bv2 = *reinterpret_cast<const BVec*>(b2_src + k0 * ldb);
+    } else {
+      bv = BVec{};
+      if constexpr (kPair) bv2 = BVec{};
+    }
+  };
+  auto stash = [&](int buf) {
+    const __half* ah = reinterpret_cast<const __half*>(&av);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) As[buf][ka + i][ra] = __half2float(ah[i]);
+    const __half* bh = reinterpret_cast<const __half*>(&bv);
+#pragma unroll
+    for (int j = 0; j < TN; j += 4)
+      *reinterpret_cast<float4*>(&Bs[buf][rb][cb + j]) =
+          make_float4(__half2float(bh[j]), __half2float(bh[j + 1]), __half2float(bh[j + 2]), __half2float(bh[j + 3]));
+    if constexpr (kPair) {
+      const __half* b2h = reinterpret_cast<const __half*>(&bv2);
+#pragma unroll
+      for (int j = 0; j < TN; j += 4)
+        *reinterpret_cast<float4*>(&Bs2[buf][rb][cb + j]) = make_float4(
+            __half2float(b2h[j]), __half2float(b2h[j + 1]), __half2float(b2h[j + 2]), __half2float(b2h[j + 3]));
+    }
+  };
+
+  const int64_t nk = (K + BK - 1) / BK;
+  fetch(0);
+  stash(0);
+  __syncthreads();
+  int buf = 0;
+  for (int64_t kt = 0; kt < nk; ++kt) {
+    const bool more = kt + 1 < nk;
+    if (more) fetch((kt + 1) * BK);
+#pragma unroll
+    for (int kk = 0; kk < BK; ++kk) {
+      float a[8], b[TN];
+      const float4 a0 = *reinterpret_cast<const float4*>(&As[buf][kk][ty * 4]);
+      const float4 a1 = *reinterpret_cast<const float4*>(&As[buf][kk][64 + ty * 4]);
+      a[0] = a0.x; a[1] = a0.y; a[2] = a0.z; a[3] = a0.w;
+      a[4] = a1.x; a[5] = a1.y; a[6] = a1.z; a[7] = a1.w;
+      if constexpr (TN == 8) {
+        const float4 b0 = *reinterpret_cast<const float4*>(&Bs[buf][kk][tx * 4]);
+        const float4 b1 = *reinterpret_cast<const float4*>(&Bs[buf][kk][64 + tx * 4]);
+        b[0] = b0.x; b[1] = b0.y; b[2] = b0.z; b[3] = b0.w;
+        b[4] = b1.x; b[5] = b1.y; b[6] = b1.z; b[7] = b1.w;
+      } else {
+        const float2 b0 = *reinterpret_cast<const float2*>(&Bs[buf][kk][tx * 2]);
+        const float2 b1 = *reinterpret_cast<const float2*>(&Bs[buf][kk][32 + tx * 2]);
+        b[0] = b0.x; b[1] = b0.y; b[2] = b1.x; b[3] = b1.y;
+      }
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+#pragma unroll
+        for (int j = 0; j < TN; ++j) acc[i][j] = __fmaf_rn(a[i], b[j], acc[i][j]);
+      if constexpr (kPair) {
+        float b2[TN];
+        const float2 c0 = *reinterpret_cast<const float2*>(&Bs2[buf][kk][tx * 2]);
+        const float2 c1 = *reinterpret_cast<const float2*>(&Bs2[buf][kk][32 + tx * 2]);
+        b2[0] = c0.x; b2[1] = c0.y; b2[2] = c1.x; b2[3] = c1.y;
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+#pragma unroll
+          for (int j = 0; j < TN; ++j) acc2[i][j] = __fmaf_rn(a[i], b2[j], acc2[i][j]);
+      }
+    }
+    if (more) stash(buf ^ 1);
+    __syncthreads();
+    buf ^= 1;
+  }
+
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int64_t gm = m0 + (i < 4 ? ty * 4 + i : 64 + ty * 4 + i - 4);
+    if (gm >= M) continue;
+#pragma unroll
+    for (int j = 0; j < TN; ++j) {
+      const int64_t gn = n0 + (j < HN ? tx * HN + j : BN / 2 + tx * HN + j - HN);
+      if (gn >= N) continue;
+      float v = acc[i][j];
+      if (bias) v = v + bias[gn];
+      if constexpr (EPI == kEpiSwiGLU) {
+        float u = acc2[i][j];
+        if (bias2) u = u + bias2[gn];
+        const float sv = v / (1.0f + expf(-v));
+        C16[gm * ldc + gn] = __float2half_rn(sv * u);
+      } else if constexpr (EPI == kEpiF16) {
+        C16[gm * ldc + gn] = __float2half_rn(activate(v, act));
+      } else {
+        C[gm * ldc + gn] = activate(v, act);
+      }
+    }
+  }
+}
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
 template <int EPI, typename TIn>
 int launch_linear(const TIn* A, int64_t M, int64_t K, int64_t lda, const TIn* B, const TIn* B2, int64_t ldb,
                   int64_t N, const float* bias, const float* bias2, int act, float* C, __half* C16, int64_t ldc,
                   cudaStream_t s) {
-  // Large problems: 64x64 tiles of 256 threads; small ones: 32x32 tiles of 64
-  // threads so that more SMs take part.
+  // Large fp16 problems: the register-tiled kernel (128 x 128 tiles; 128 x 64
+  // for the gate/up pair); mid-sized ones 64x64 tiles of 256 threads; small
+  // ones 32x32 tiles of 64 threads so that more SMs take part.
+  if constexpr (std::is_same<TIn, __half>::value) {
+    constexpr int TN = EPI == kEpiSwiGLU ? 4 : 8;
+    constexpr int BN = 16 * TN;
+    const int64_t tiles = ((M + 127) / 128) * ((N + BN - 1) / BN);
+    const bool ok = K % 8 == 0 && lda % 8 == 0 && ldb % 16 == 0 && ldb >= N && aligned16(A) && aligned16(B) &&
+                    (EPI != kEpiSwiGLU || aligned16(B2));
+    if (ok && tiles >= 120) {
+      dim3 grid((unsigned)((N + BN - 1) / BN), (unsigned)((M + 127) / 128));
+      SMEAI_CUDA_TRY(launch(linear_tiled_kernel<TN, EPI>, grid, dim3(256), 0, s, A, M, K, lda, B, B2, ldb, N, bias,
+                            bias2, act, C, C16, ldc));
+      return kOk;
+    }
+  }
   const int64_t big_tiles = ((M + 63) / 64) * ((N + 63) / 64);
   if (big_tiles >= 148) {
     auto k = linear_ffma_kernel<64, 64, 4, 4, EPI, TIn>;

@@ -205,3 +205,19 @@ def test_attention_device_entry_points(L, oracle):
     for a in pws:
         L.sme_ai_packed_linear_weight_destroy(ctypes.byref(a))
     L.sme_ai_workspace_destroy(ctypes.byref(ws))
+
+
+@pytest.mark.parametrize("S_,D,H,causal", [(300, 128, 4, 1), (300, 128, 4, 0), (257, 256, 2, 1), (640, 128, 2, 0),
+                                           (256, 64, 2, 1)])
+def test_attention_tiled_shapes(L, oracle, S_, D, H, causal):
+    """Shapes served by the tiled kernels (head_dim 32 / 64 / 128, 256 <= S):
+    ragged last query / key tiles (S = 300, 257), causal and full."""
+    run_both(L, oracle, S_, D, H, causal, 40 + S_)
+
+
+def test_attention_tiled_head_chunks(L, oracle, monkeypatch):
+    """A score budget of one head's matrix: heads are processed one chunk at a time."""
+    monkeypatch.setenv("SMEAI_ATTN_SCORE_BUDGET", str(300 * 320 * 4 * 2))  # two heads per chunk
+    run_both(L, oracle, 300, 160, 5, 1, 77)
+    monkeypatch.setenv("SMEAI_ATTN_SCORE_BUDGET", "1")                      # one head per chunk
+    run_both(L, oracle, 300, 96, 3, 0, 78)
