@@ -243,7 +243,7 @@ sme_ai_status sme_ai_linear_packed_f16f32_device(const sme_ai_fp16 *input, uint6
  * returns without waiting.  Q, K, the fp16 context and the score matrix
  * live in the workspace's device scratch, so calls sharing a workspace must
  * be ordered on one stream.  For head_dim 32, 64 or 128 and 256 <= seq_len
- * <= 16384 the scores of a chunk of heads (at most 256 MB, or one head) are
+ * <= 16384 the scores of a chunk of heads (at most 1 GiB, or one head) are
  * kept in a workspace-owned device buffer that the first call needing it
  * allocates (a cudaMalloc, which may synchronize the device). */
 sme_ai_status sme_ai_self_attention_packed_f16f32_device(sme_ai_workspace *ws, const sme_ai_fp16 *input,

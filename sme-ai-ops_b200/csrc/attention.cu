@@ -183,7 +183,7 @@ int launch_attention(const float* Q, const float* K, const float* V, int64_t S, 
 // ---- tiled path ----------------------------------------------------------------------
 constexpr int kTQ = 64;                         // query / key rows per score tile
 constexpr int kTJ = 32;                         // keys per weighted-sum step
-constexpr size_t kScoreBudget = 256ull << 20;   // score buffer per chunk of heads
+constexpr size_t kScoreBudget = 1ull << 30;     // score buffer per chunk of heads
 
 // The budget, overridable with SMEAI_ATTN_SCORE_BUDGET (bytes; tests use a
 // small one to run several chunks of heads).
@@ -221,10 +221,12 @@ __device__ __forceinline__ void tile_pair(int t, int tiles, int causal, int& ib,
 // with fused multiply-adds, and the lanes are summed pairwise (l + l+8, then
 // +4, +2, +1).  Lanes are evaluated in bit-reversed order (0, 8, 4, 12, ..),
 // the post-order of that tree, so each pair is added as soon as both exist.
+template <int HD>
 __global__ void __launch_bounds__(256, 2) attn_scores_kernel(const float* __restrict__ Q,
                                                              const float* __restrict__ K, int64_t S, int64_t D,
-                                                             int hd, int h0, float scale, int causal, int tiles,
+                                                             int h0, float scale, int causal, int tiles,
                                                              float* __restrict__ sc, int64_t ldsc) {
+  constexpr int hd = HD;
   extern __shared__ __align__(16) float smem[];
   float* Qt = smem;
   float* Kt = smem + hd * kTQ;
@@ -261,6 +263,7 @@ __global__ void __launch_bounds__(256, 2) attn_scores_kernel(const float* __rest
     for (int ii = 0; ii < 4; ++ii)
 #pragma unroll
       for (int jj = 0; jj < 4; ++jj) a[ii][jj] = 0.f;
+#pragma unroll
     for (int d = l; d < hd; d += 16) {
       const float4 q4 = *reinterpret_cast<const float4*>(Qt + d * kTQ + ty * 4);
       const float4 k4 = *reinterpret_cast<const float4*>(Kt + d * kTQ + tx * 4);
@@ -296,15 +299,15 @@ __global__ void __launch_bounds__(256, 2) attn_scores_kernel(const float* __rest
   }
 }
 
-// Softmax of score rows in place, one warp per row (head blockIdx.y, rows
-// blockIdx.x * warps + w): max, expf(s - max), the sequential sum (lane 0,
+// Softmax of score rows in place, one warp per row (head blockIdx.y; CTAs
+// take row blocks from the last one down): max, expf(s - max), the sequential sum (lane 0,
 // j ascending), e / sum; causal rows then zero their entries up to the end
 // of the diagonal 64-key tile, which the weighted-sum kernel reads.
 __global__ void __launch_bounds__(256) attn_softmax_kernel(float* __restrict__ sc, int64_t S, int64_t ldsc,
                                                            int causal) {
   extern __shared__ __align__(16) float smem[];
   const int warps = blockDim.x >> 5, w = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int64_t i = (int64_t)blockIdx.x * warps + w;
+  const int64_t i = (int64_t)(gridDim.x - 1 - blockIdx.x) * warps + w;  // longest causal rows first
   float* e = smem + (size_t)w * (size_t)ldsc;
   pdl_trigger();
   pdl_wait();
@@ -340,7 +343,7 @@ __global__ void __launch_bounds__(256) attn_softmax_kernel(float* __restrict__ s
 }
 
 // ctx16[i][off + d] = fp16(sum_j p_ij * V_j[d]) for 64 query rows (query
-// tile blockIdx.x) of head h0 + blockIdx.y; keys in ascending order, 32 per
+// tiles from the last one down) of head h0 + blockIdx.y; keys in ascending order, 32 per
 // step, each term a multiply then an add (two roundings).  256 threads as
 // 16 x 16: rows ty*4 .. ty*4+3, columns tx*CW/2 + .. and HD/2 + tx*CW/2 + ..
 // (CW = HD/16 columns per thread).  Shared memory: Pt [32][64] (P transposed),
@@ -353,7 +356,8 @@ __global__ void __launch_bounds__(256) attn_pv_kernel(const float* __restrict__ 
   __shared__ __align__(16) float Pt[kTJ][kTQ];
   __shared__ __align__(16) float Vs[kTJ][HD];
   const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
-  const int64_t i0 = (int64_t)blockIdx.x * kTQ;
+  // last query tile first: causal tiles' work grows with the tile index
+  const int64_t i0 = (int64_t)(gridDim.x - 1 - blockIdx.x) * kTQ;
   const int64_t off = (int64_t)(h0 + (int)blockIdx.y) * HD;
   const float* P = sc + (int64_t)blockIdx.y * S * ldsc;
   const int64_t jmax = causal ? (i0 + kTQ < S ? i0 + kTQ : S) : S;
@@ -438,12 +442,13 @@ int attention_tiled(const float* Q, const float* K, const float* V, int64_t S, i
   int warps = 8;
   while (warps > 1 && (size_t)warps * ldsc * sizeof(float) > (size_t)kSmemLimit) --warps;
   const size_t sm_smem = (size_t)warps * ldsc * sizeof(float);
-  SMEAI_CUDA_TRY(cudaFuncSetAttribute(attn_scores_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sc_smem));
+  auto scores_k = hd == 32 ? attn_scores_kernel<32> : hd == 64 ? attn_scores_kernel<64> : attn_scores_kernel<128>;
+  SMEAI_CUDA_TRY(cudaFuncSetAttribute(scores_k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sc_smem));
   SMEAI_CUDA_TRY(cudaFuncSetAttribute(attn_softmax_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm_smem));
   for (int64_t h0 = 0; h0 < heads; h0 += hc_max) {
     const int64_t hc = heads - h0 < hc_max ? heads - h0 : hc_max;
-    SMEAI_CUDA_TRY(launch(attn_scores_kernel, dim3((unsigned)pairs, (unsigned)hc), dim3(256), sc_smem, s, Q, K, S, D,
-                          hd, (int)h0, scale, causal, tiles, scores, ldsc));
+    SMEAI_CUDA_TRY(launch(scores_k, dim3((unsigned)pairs, (unsigned)hc), dim3(256), sc_smem, s, Q, K, S, D, (int)h0,
+                          scale, causal, tiles, scores, ldsc));
     SMEAI_CUDA_TRY(launch(attn_softmax_kernel, dim3((unsigned)((S + warps - 1) / warps), (unsigned)hc),
                           dim3(warps * 32), sm_smem, s, scores, S, ldsc, causal));
     const dim3 pv_grid((unsigned)((S + kTQ - 1) / kTQ), (unsigned)hc);
