@@ -12,7 +12,10 @@ Workloads (one "step" each):
                      gate/up and lm_head inputs).  On one GPU the whole step is
                      one persistent kernel (q2k_program_kernel); on N GPUs the
                      weights are row-sharded and each linear is one GEMV launch
-                     followed by an NCCL all-gather of the output slices.
+                     whose finishers also store their rows into every rank's
+                     copy of the next input over NVLink (CUDA-IPC peer memory)
+                     and signal it; the next GEMV waits for all ranks' rows
+                     (--quant separate: NCCL all-gathers instead).
   gemv               one Q2_K x Q8_K GEMV W[4096,4096] x x[4096], rotating
                      over 64 distinct weight copies (352 MB > L2).
   prefill            activations [512,4096] (Q8_K per row) x W[11008,4096] Q2_K
@@ -569,7 +572,10 @@ def run_ours(args):
             "pct_of_hbm_peak": value / (peak * world) * 100,
             "config": {"workload": workload,
                        "global_batch": args.prefill_tokens if args.workload == "prefill" else 1, "seq_len": 1,
-                       "parallelism": f"row-shard tp{world}" if world > 1 else "single GPU",
+                       "parallelism": (f"row-shard tp{world}, " + ("all-gather fused into each GEMV (NVLink "
+                                       "peer stores + signals)" if stack.quant == "peer" else "NCCL all-gather")
+                                       if args.workload == "decode" else f"row-shard tp{world}")
+                       if world > 1 else "single GPU",
                        "l2": "inputs larger than L2 (2.17 GB of weights per step)" if args.workload == "decode"
                        else "inputs larger than L2 (rotating distinct weight copies)",
                        **({"prefill_ops_per_step": prefill_ops, "tops": prefill_ops / (ms / 1e3) / 1e12}

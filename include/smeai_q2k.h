@@ -158,6 +158,42 @@ int smeai_q2k_mul_mat_f32_ex(const void *w_dev, const float *x_dev, size_t ld_x,
                              size_t ldy, int epilogue, const float *resid_dev, size_t ld_resid, float rms_eps,
                              void *stream);
 
+/* Row-sharded GEMV with its all-gather fused in (multi-GPU decode, one process
+ * per GPU).  Each rank holds a row shard of W; this call computes the shard's
+ * rows like smeai_q2k_mul_mat_f32_ex and, in the same kernel, stores the rows
+ * at or past local output row `row0` of every finished 32-row group into each
+ * dst[q] (peer memory opened with smeai_ipc_open, or this GPU's own) at row
+ * (r - row0), token stride ld_dst floats, then bumps each sig[q] once per
+ * finished group with a system-scope release.  When wait_sig is set the kernel first waits (bounded,
+ * 10 s; a timeout is reported by smeai_take_device_error) until *wait_sig has
+ * reached (*epoch + 1) * wait_count -- the row groups every rank of the
+ * producing call publishes per step -- so its input may be rows other GPUs
+ * store.  n_cols must be 1, 2, 4 or 8 (one launch); Q2_K weights, fp32 input. */
+typedef struct {
+    int n_dst;                  /* destinations (<= 8) */
+    float *dst[8];
+    int64_t ld_dst;
+    int64_t row0;               /* first exchanged local output row (a multiple of 16) */
+    int n_sig;                  /* signal words bumped per exchanged row group (<= 8) */
+    unsigned *sig[8];
+    const unsigned *wait_sig;   /* NULL: no wait */
+    unsigned wait_count;
+    const unsigned *epoch;      /* this rank's step counter (device word) */
+} smeai_peer_exchange;
+int smeai_q2k_mul_mat_f32_peer(const void *w_dev, const float *x_dev, size_t ld_x, int64_t n_cols, float *y_dev,
+                               size_t ldy, int epilogue, const float *resid_dev, size_t ld_resid, float rms_eps,
+                               const smeai_peer_exchange *ex, void *stream);
+/* End of a step: wait (bounded) until *sig reaches (*epoch + 1) * count, then
+ * advance *epoch (queued on stream; one thread). */
+int smeai_peer_step_end(const unsigned *sig, unsigned count, unsigned *epoch, void *stream);
+/* Device memory shareable with the other processes of the node: bytes
+ * zero-filled, *ptr its address here, handle[64] the CUDA IPC handle to send
+ * to the peers, which map it with smeai_ipc_open (peer access enabled). */
+int smeai_ipc_alloc(size_t bytes, void **ptr, void *handle64);
+void smeai_ipc_free(void *ptr);
+int smeai_ipc_open(const void *handle64, void **ptr);
+void smeai_ipc_close(void *ptr);
+
 /* Exactness probe: the integer parts of the dot for every (row, super-block)
  * against ONE Q8_K row, [n_rows][k/256] int32 each:
  *   isum  = sum_j scale_j * sum_{i in sub-block j} q2_i * q8_i

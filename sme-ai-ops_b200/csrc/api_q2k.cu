@@ -320,6 +320,87 @@ int smeai_q2k_mul_mat_f32_ex(const void* w_dev, const float* x_dev, size_t ld_x,
                       (int64_t)ldy, epilogue, resid_dev, (int64_t)ld_resid, as_stream(stream));
 }
 
+int smeai_q2k_mul_mat_f32_peer(const void* w_dev, const float* x_dev, size_t ld_x, int64_t n_cols, float* y_dev,
+                               size_t ldy, int epilogue, const float* resid_dev, size_t ld_resid, float rms_eps,
+                               const smeai_peer_exchange* ex, void* stream) {
+  const Handle* h = as_fmt(w_dev, kFmtQ2K, "smeai_q2k_mul_mat_f32_peer");
+  if (!h) return kBadArgument;
+  if (!ex) {
+    set_last_error("smeai_q2k_mul_mat_f32_peer: NULL exchange");
+    return kBadArgument;
+  }
+  PeerExchange e;
+  e.n_dst = ex->n_dst;
+  e.n_sig = ex->n_sig;
+  if (e.n_dst < 0 || e.n_dst > kMaxPeers || e.n_sig < 0 || e.n_sig > kMaxPeers) {
+    set_last_error("smeai_q2k_mul_mat_f32_peer: at most %d destinations and signals", kMaxPeers);
+    return kBadArgument;
+  }
+  for (int q = 0; q < e.n_dst; ++q) e.dst[q] = ex->dst[q];
+  for (int q = 0; q < e.n_sig; ++q) e.sig[q] = ex->sig[q];
+  e.ld_dst = ex->ld_dst;
+  e.row0 = ex->row0;
+  e.wait_sig = ex->wait_sig;
+  e.wait_count = ex->wait_count;
+  e.epoch = ex->epoch;
+  return q2k_gemv_any(h->w, rms_eps >= 0.f ? kInF32Rms : kInF32, x_dev, (int64_t)ld_x, rms_eps, n_cols, y_dev,
+                      (int64_t)ldy, epilogue, resid_dev, (int64_t)ld_resid, as_stream(stream), &e);
+}
+
+int smeai_peer_step_end(const unsigned* sig, unsigned count, unsigned* epoch, void* stream) {
+  return peer_step_end(sig, count, epoch, as_stream(stream));
+}
+
+int smeai_ipc_alloc(size_t bytes, void** ptr, void* handle64) {
+  if (!ptr || !handle64 || !bytes) {
+    set_last_error("smeai_ipc_alloc: bad arguments");
+    return kBadArgument;
+  }
+  static_assert(sizeof(cudaIpcMemHandle_t) == 64, "CUDA IPC handles are 64 bytes");
+  void* p = nullptr;
+  if (cudaMalloc(&p, bytes) != cudaSuccess) {
+    cudaGetLastError();
+    set_last_error("smeai_ipc_alloc: cudaMalloc of %zu bytes failed", bytes);
+    return kAllocFailed;
+  }
+  cudaIpcMemHandle_t hd;
+  if (cudaMemset(p, 0, bytes) != cudaSuccess || cudaIpcGetMemHandle(&hd, p) != cudaSuccess) {
+    const cudaError_t e = cudaGetLastError();
+    cudaFree(p);
+    set_last_error("smeai_ipc_alloc: %s", cudaGetErrorString(e));
+    return kCudaError;
+  }
+  memcpy(handle64, &hd, sizeof(hd));
+  *ptr = p;
+  return kOk;
+}
+
+void smeai_ipc_free(void* ptr) {
+  if (ptr) cudaFree(ptr);
+}
+
+int smeai_ipc_open(const void* handle64, void** ptr) {
+  if (!handle64 || !ptr) {
+    set_last_error("smeai_ipc_open: bad arguments");
+    return kBadArgument;
+  }
+  cudaIpcMemHandle_t hd;
+  memcpy(&hd, handle64, sizeof(hd));
+  void* p = nullptr;
+  const cudaError_t e = cudaIpcOpenMemHandle(&p, hd, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    set_last_error("smeai_ipc_open: %s", cudaGetErrorString(e));
+    return kUnsupported;
+  }
+  *ptr = p;
+  return kOk;
+}
+
+void smeai_ipc_close(void* ptr) {
+  if (ptr) cudaIpcCloseMemHandle(ptr);
+}
+
 int smeai_q2k_block_sums(const void* w_dev, const void* x_q8k_dev, int32_t* isum_dev, int32_t* summs_dev,
                          void* stream) {
   const Handle* h = as_fmt(w_dev, kFmtQ2K, "smeai_q2k_block_sums");

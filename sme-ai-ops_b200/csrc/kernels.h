@@ -71,8 +71,34 @@ enum Epilogue : int {
 // rows quantized to Q8_K in the kernel's prologue, optionally after an RMSNorm.
 enum InMode : int { kInQ8K = 0, kInF32 = 1, kInF32Rms = 2 };
 
+// Cross-GPU exchange of a row-sharded GEMV's output (peer memory mapped
+// through CUDA IPC): the rows of every finished row group at or past local
+// output row row0 are also stored to each dst[q] (at row - row0, token stride
+// ld_dst); then, for every finished group, each sig[q] is bumped once
+// (system-scope release) -- so a full count also says that every CTA of the
+// call has finished reading its input.  A GEMV with
+// wait_sig first waits (bounded) until *wait_sig reaches
+// (*epoch + 1) * wait_count -- every rank's row groups of the producing GEMV in
+// this step -- and then reads its input through L2.
+constexpr int kMaxPeers = 8;
+struct PeerExchange {
+  int n_dst = 0;
+  float* dst[kMaxPeers] = {};
+  int64_t ld_dst = 0;
+  int64_t row0 = 0;
+  int n_sig = 0;
+  unsigned* sig[kMaxPeers] = {};
+  const unsigned* wait_sig = nullptr;
+  unsigned wait_count = 0;
+  const unsigned* epoch = nullptr;
+};
+
 int q2k_gemv_any(const Q2KWeight& w, int in_mode, const void* x, int64_t ld_x, float eps, int64_t n_cols,
-                 float* y, int64_t ldy, int epilogue, const float* resid, int64_t ld_resid, cudaStream_t stream);
+                 float* y, int64_t ldy, int epilogue, const float* resid, int64_t ld_resid, cudaStream_t stream,
+                 const PeerExchange* ex = nullptr);
+// End of a step on one rank: wait (bounded) until *sig reaches
+// (*epoch + 1) * count, then advance *epoch.
+int peer_step_end(const unsigned* sig, unsigned count, unsigned* epoch, cudaStream_t stream);
 
 // y = W x for n_cols Q8_K activation rows (ggml layout, contiguous rows).
 int q2k_gemv(const Q2KWeight& w, const void* xq, int64_t n_cols, float* y, int64_t ldy, int epilogue,

@@ -48,6 +48,38 @@ namespace {
 constexpr int kMaxConsumers = 16;
 constexpr int kMaxThreads = (kMaxConsumers + 1) * 32;
 constexpr uint64_t kWaitTimeoutNs = 2000000000ull;  // 2 s
+constexpr uint64_t kPeerTimeoutNs = 10000000000ull; // 10 s: another GPU's step
+
+__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ uint64_t now_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+// Bounded wait until *sig reaches (*epoch + 1) * count (wrap-safe); false on timeout.
+__device__ bool peer_wait(const unsigned* sig, const unsigned* epoch, unsigned count) {
+  const unsigned target = (ld_acquire_sys(epoch) + 1u) * count;
+  const uint64_t t0 = now_ns();
+  while ((int)(ld_acquire_sys(sig) - target) < 0) {
+    if (now_ns() - t0 > kPeerTimeoutNs) return false;
+    __nanosleep(64);
+  }
+  return true;
+}
+// Publish one finished row group to every rank: the warp's stores (to this
+// GPU and the peers) are ordered before lane 0's system-scope fence and the
+// signal increments.
+__device__ __forceinline__ void peer_signal(const PeerExchange& ex, int lane) {
+  __syncwarp();
+  if (lane == 0) {
+    __threadfence_system();
+    for (int q = 0; q < ex.n_sig; ++q) atomicAdd_system(ex.sig[q], 1u);
+  }
+}
 
 struct GemvParams {
   const uint8_t* tiles;
@@ -66,6 +98,7 @@ struct GemvParams {
   unsigned* err;
   int stages;        // ring depth (a power of two)
   int log2_stages;
+  PeerExchange ex;   // cross-GPU output exchange (n_dst = n_sig = 0 and no wait_sig: off)
 };
 
 // Shared-memory carve-up for T tokens (16-byte aligned pieces).
@@ -133,7 +166,10 @@ __device__ __forceinline__ void finish_group(const float* terms, int nb, int64_t
         }
         if (2 * orow < p.n_rows) {
           const float sg = __fdiv_rn(g, __fadd_rn(1.0f, expf(-g)));
-          p.y[t * p.ldy + orow] = __fmul_rn(sg, u);
+          const float h = __fmul_rn(sg, u);
+          p.y[t * p.ldy + orow] = h;
+          if (orow >= p.ex.row0)
+            for (int q = 0; q < p.ex.n_dst; ++q) p.ex.dst[q][t * p.ex.ld_dst + (orow - p.ex.row0)] = h;
         }
       }
     }
@@ -155,6 +191,8 @@ __device__ __forceinline__ void finish_group(const float* terms, int nb, int64_t
       if (orow < p.n_rows) {
         if constexpr (EPI == kEpiResidual) s = __fadd_rn(p.resid[t * p.ld_resid + orow], s);
         p.y[t * p.ldy + orow] = s;
+        if (orow >= p.ex.row0)
+          for (int q = 0; q < p.ex.n_dst; ++q) p.ex.dst[q][t * p.ex.ld_dst + (orow - p.ex.row0)] = s;
       }
     }
   }
@@ -226,6 +264,22 @@ __global__ void __launch_bounds__(kMaxThreads) q2k_gemv_kernel(const GemvParams 
   // ---- consumers
   const int cw = warp - 1;
   pdl_wait();
+  const bool peer_in = p.ex.wait_sig != nullptr;
+  if (peer_in) {  // the input holds rows other GPUs store: wait for all of them
+    int ok = 1;
+    if (cw == 0 && lane == 0) {
+      ok = peer_wait(p.ex.wait_sig, p.ex.epoch, p.ex.wait_count) ? 1 : 0;
+      if (!ok) raise_device_error(p.err, kDevErrTimeout);
+    }
+    int all;  // the consumer warps meet (named barrier 1) and learn the waiter's result
+    asm volatile(
+        "{\n .reg .pred pi, po;\n setp.ne.s32 pi, %1, 0;\n bar.red.and.pred po, 1, %2, pi;\n"
+        " selp.s32 %0, 1, 0, po;\n}"
+        : "=r"(all)
+        : "r"(ok), "r"(kConsumers * 32)
+        : "memory");
+    if (!all) return;
+  }
 
   // activation prologue: this warp's own super-blocks b = cw (mod kConsumers)
   if constexpr (IN == kInQ8K) {
@@ -242,7 +296,8 @@ __global__ void __launch_bounds__(kMaxThreads) q2k_gemv_kernel(const GemvParams 
       for (int i = cw; i < T * nb; i += kConsumers) {
         const int t = i / nb, b = i - t * nb;
         float v[8];
-        load8(x + t * p.ld_x + b * QK_K + lane * 8, v);
+        if (peer_in) load8_cg(x + t * p.ld_x + b * QK_K + lane * 8, v);
+        else load8(x + t * p.ld_x + b * QK_K + lane * 8, v);
         const float s = group_sumsq_load8(v);
         if ((lane & 3) == 0) m.rsum[t * gs + b * 8 + (lane >> 2)] = s;
       }
@@ -268,7 +323,8 @@ __global__ void __launch_bounds__(kMaxThreads) q2k_gemv_kernel(const GemvParams 
 #pragma unroll 1
       for (int t = 0; t < T; ++t) {
         float v[8];
-        load8(x + t * p.ld_x + b * QK_K + lane * 8, v);
+        if (peer_in) load8_cg(x + t * p.ld_x + b * QK_K + lane * 8, v);
+        else load8(x + t * p.ld_x + b * QK_K + lane * 8, v);
         if constexpr (IN == kInF32Rms) {
           const float inv = m.rsum[t * (8 * nb + 1) + 8 * nb];
 #pragma unroll
@@ -315,6 +371,7 @@ __global__ void __launch_bounds__(kMaxThreads) q2k_gemv_kernel(const GemvParams 
           return;
         }
         finish_group<T, EPI>(terms, nb, group, lane, p);
+        if (p.ex.n_sig) peer_signal(p.ex, lane);  // every group: its CTA no longer reads the input
         mbar_arrive_warp(&m.tfree[buf]);
       }
     }
@@ -530,10 +587,35 @@ int q2k_repack(const void* w_blocks_dev, int64_t n_rows, int64_t k, Q2KWeight* o
 }
 
 int q2k_gemv_any(const Q2KWeight& w, int in_mode, const void* x, int64_t ld_x, float eps, int64_t n_cols,
-                 float* y, int64_t ldy, int epilogue, const float* resid, int64_t ld_resid, cudaStream_t stream) {
+                 float* y, int64_t ldy, int epilogue, const float* resid, int64_t ld_resid, cudaStream_t stream,
+                 const PeerExchange* ex) {
   if (!w.tiles || !x || !y || n_cols <= 0) {
     set_last_error("q2k_gemv: bad arguments");
     return kBadArgument;
+  }
+  if (ex) {
+    const bool single = n_cols == 1 || n_cols == 2 || n_cols == 4 || n_cols == 8;
+    if (!single || ex->n_dst < 0 || ex->n_dst > kMaxPeers || ex->n_sig < 0 || ex->n_sig > kMaxPeers ||
+        (ex->wait_sig && (!ex->epoch || !ex->wait_count)) || (ex->wait_sig && in_mode == kInQ8K) ||
+        ex->row0 < 0 || ex->row0 % 16 || (ex->n_dst && ex->ld_dst <= 0)) {
+      set_last_error("q2k_gemv: bad peer exchange (1/2/4/8 tokens, <= %d peers, fp32 input when waiting, "
+                     "row0 a multiple of 16)", kMaxPeers);
+      return kBadArgument;
+    }
+    for (int q = 0; q < ex->n_dst; ++q)
+      if (!ex->dst[q]) {
+        set_last_error("q2k_gemv: NULL peer destination %d", q);
+        return kBadArgument;
+      }
+    for (int q = 0; q < ex->n_sig; ++q)
+      if (!ex->sig[q]) {
+        set_last_error("q2k_gemv: NULL peer signal %d", q);
+        return kBadArgument;
+      }
+    if (w.fmt != kFmtQ2K) {
+      set_last_error("q2k_gemv: the peer exchange is built for Q2_K weights");
+      return kBadArgument;
+    }
   }
   if (in_mode == kInQ8K && (reinterpret_cast<uintptr_t>(x) & 3)) {
     set_last_error("q2k_gemv: Q8_K activations must be 4-byte aligned");
@@ -573,6 +655,7 @@ int q2k_gemv_any(const Q2KWeight& w, int in_mode, const void* x, int64_t ld_x, f
     p.ldy = ldy;
     p.resid = resid ? resid + c0 * ld_resid : nullptr;
     p.ld_resid = ld_resid;
+    if (ex) p.ex = *ex;
     int st;
     switch (in_mode) {
       case kInQ8K: st = dispatch_epi<kInQ8K>(epilogue, T, w, p, stream); break;
@@ -585,6 +668,28 @@ int q2k_gemv_any(const Q2KWeight& w, int in_mode, const void* x, int64_t ld_x, f
     if (st != kOk) return st;
     c0 += T;
   }
+  return kOk;
+}
+
+namespace {
+__global__ void peer_step_end_kernel(const unsigned* sig, unsigned count, unsigned* epoch, unsigned* err) {
+  if (!peer_wait(sig, epoch, count)) raise_device_error(err, kDevErrTimeout);
+  *epoch = *epoch + 1u;
+}
+}  // namespace
+
+int peer_step_end(const unsigned* sig, unsigned count, unsigned* epoch, cudaStream_t stream) {
+  if (!sig || !epoch || !count) {
+    set_last_error("peer_step_end: bad arguments");
+    return kBadArgument;
+  }
+  unsigned* err = device_error_ptr();
+  if (!err) {
+    set_last_error("peer_step_end: device error word unavailable");
+    return kCudaError;
+  }
+  peer_step_end_kernel<<<1, 1, 0, stream>>>(sig, count, epoch, err);
+  SMEAI_CUDA_TRY(cudaGetLastError());
   return kOk;
 }
 

@@ -60,6 +60,13 @@ class Q2KPhase(ctypes.Structure):
                 ("epilogue", ctypes.c_int), ("resid", ctypes.c_void_p), ("ld_resid", ctypes.c_size_t)]
 
 
+class PeerExchange(ctypes.Structure):
+    """smeai_peer_exchange: the fused all-gather of a row-sharded GEMV."""
+    _fields_ = [("n_dst", ctypes.c_int), ("dst", ctypes.c_void_p * 8), ("ld_dst", ctypes.c_int64),
+                ("row0", ctypes.c_int64), ("n_sig", ctypes.c_int), ("sig", ctypes.c_void_p * 8),
+                ("wait_sig", ctypes.c_void_p), ("wait_count", ctypes.c_uint), ("epoch", ctypes.c_void_p)]
+
+
 def _declare(L: ctypes.CDLL) -> None:
     P, U64, I64, I, F, SZ = (ctypes.c_void_p, ctypes.c_uint64, ctypes.c_int64, ctypes.c_int,
                              ctypes.c_float, ctypes.c_size_t)
@@ -120,6 +127,12 @@ def _declare(L: ctypes.CDLL) -> None:
         "smeai_q2k_mul_mat_tc": (I, [P, P, I64, P, SZ, P]),
         "smeai_q2k_mul_mat_f32": (I, [P, P, I64, P, SZ, P]),
         "smeai_q2k_mul_mat_f32_ex": (I, [P, P, SZ, I64, P, SZ, I, P, SZ, F, P]),
+        "smeai_q2k_mul_mat_f32_peer": (I, [P, P, SZ, I64, P, SZ, I, P, SZ, F, ctypes.POINTER(PeerExchange), P]),
+        "smeai_peer_step_end": (I, [P, ctypes.c_uint, P, P]),
+        "smeai_ipc_alloc": (I, [SZ, ctypes.POINTER(ctypes.c_void_p), P]),
+        "smeai_ipc_free": (None, [P]),
+        "smeai_ipc_open": (I, [P, ctypes.POINTER(ctypes.c_void_p)]),
+        "smeai_ipc_close": (None, [P]),
         "smeai_q2k_block_sums": (I, [P, P, P, P, P]),
         "smeai_q2k_program_create": (I, [ctypes.POINTER(Q2KPhase), I, I64, F, ctypes.POINTER(ctypes.c_void_p)]),
         "smeai_q2k_program_run": (I, [P, P]),
@@ -191,6 +204,14 @@ def check(status: int, what: str = "") -> None:
 
 def device_ready() -> bool:
     return bool(lib().smeai_device_ready())
+
+
+def take_device_error() -> int:
+    """The device error word of the current GPU (a bounded wait that timed
+    out sets it), cleared; 0 when no kernel reported one."""
+    code = ctypes.c_uint(0)
+    check(lib().smeai_take_device_error(ctypes.byref(code)), "take_device_error")
+    return code.value
 
 
 def exported_symbols_from_headers() -> list[str]:

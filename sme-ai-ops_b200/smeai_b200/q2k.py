@@ -140,6 +140,20 @@ class Q2KMatrix:
               "q2k_mul_mat_f32_ex")
         return out
 
+    def mul_mat_f32_peer(self, x: torch.Tensor, n_cols: int, out: torch.Tensor, ex, epilogue: int = EPI_STORE,
+                         resid: torch.Tensor | None = None, rms_eps: float | None = None) -> torch.Tensor:
+        """mul_mat_f32_ex with the fused cross-GPU exchange `ex` (a PeerExchange)."""
+        out_rows = self.n_rows // 2 if epilogue == EPI_SILU_MUL else self.n_rows
+        assert x.dtype == torch.float32 and x.stride(-1) == 1
+        ld_x = x.stride(0) if x.dim() == 2 else self.k
+        ldy = out.stride(0) if out.dim() == 2 else out_rows
+        ldr = 0 if resid is None else (resid.stride(0) if resid.dim() == 2 else out_rows)
+        eps = -1.0 if rms_eps is None else float(rms_eps)
+        check(lib().smeai_q2k_mul_mat_f32_peer(self.handle, _ptr(x), ld_x, n_cols, _ptr(out), ldy, epilogue,
+                                               _ptr(resid), ldr, ctypes.c_float(eps), ctypes.byref(ex),
+                                               cur_stream()), "q2k_mul_mat_f32_peer")
+        return out
+
     def block_sums(self, xq: torch.Tensor):
         isum = torch.empty((self.n_rows, self.nb), dtype=torch.int32, device=xq.device)
         summs = torch.empty_like(isum)

@@ -83,9 +83,18 @@ class Q2KDecodeStack:
         # separate for the plain re-quantizations (o, down).  All three give
         # bit-identical results.  "program" (one GPU; batch 1, 2, 4 or 8): the
         # whole step is ONE persistent kernel (Q2KProgram) -- same bits again.
-        assert quant in ("fused", "separate", "mixed", "program")
-        if quant == "program" and world > 1:
-            quant = "separate"   # the next input is only complete after the all-gather
+        # "peer" (N > 1 GPUs; batch 1, 2, 4 or 8): every GEMV stores its rows into
+        # all ranks' copies of the next input and signals them in the same kernel
+        # (the all-gather fused in, over CUDA-IPC peer memory); the next GEMV waits
+        # for every rank's rows.  Falls back to "separate" + NCCL when a shard is
+        # not 32-row aligned or the peers cannot be mapped.
+        assert quant in ("fused", "separate", "mixed", "program", "peer")
+        if quant in ("program", "peer") and world > 1:
+            aligned = all((shard_range(hidden, q, world)[1] - shard_range(hidden, q, world)[0]) % 32 == 0
+                          for q in range(world))
+            quant = "peer" if aligned and batch in (1, 2, 4, 8) else "separate"
+        elif quant == "peer":
+            quant = "program"
         if quant == "program" and batch not in (1, 2, 4, 8):
             quant = "separate"
         self.prog = None
@@ -135,6 +144,9 @@ class Q2KDecodeStack:
         self.hq = torch.empty((B, ffn // QK_K * Q8K_BLOCK_BYTES), dtype=u8, device=d)
         self.lg_loc = torch.empty((B, vs), dtype=f32, device=d)
         self.logits = torch.empty((B, vocab), dtype=f32, device=d)
+        self.arena = None
+        if self.quant == "peer":
+            self._setup_peer()
 
     # --------------------------------------------------------------- weights
     def _draw(self, seed, layer, mat, rows, k, lo, hi, std):
@@ -160,6 +172,49 @@ class Q2KDecodeStack:
             return
         gather_rows(full, local, full.shape[1], self.world, self.group)
 
+    # --------------------------------------------------------------- fused exchange
+    def _setup_peer(self):
+        """Peer arena and the exchange descriptors of every GEMV ("peer" mode)."""
+        from .peer import PeerArena, PeerUnavailable, decode_plan, make_exchange
+        B, H, F, V, L, W, r = self.B, self.H, self.F, self.V, self.L, self.world, self.rank
+        layout = [("x", B * H * 4), ("v", B * H * 4), ("h", B * F * 4), ("lg", B * V * 4), ("sig", (4 * L + 1) * 4),
+                  ("epoch", 4)]
+        try:
+            ar = PeerArena(layout, self.dev, r, W, self.group)
+        except PeerUnavailable:
+            self.quant = "separate"
+            return
+        self.arena = ar
+        f32 = torch.float32
+        self.x, self.v_full = ar.tensor("x", f32, (B, H)), ar.tensor("v", f32, (B, H))
+        self.h_full, self.logits = ar.tensor("h", f32, (B, F)), ar.tensor("lg", f32, (B, V))
+        epoch = ar.addr(r, "epoch")
+        exs = []
+        for name, dst, ld, row0, sig, wait, count in decode_plan(H, F, V, L, r, W, shard_range):
+            if name == "end":
+                self.end = (ar.addr(r, "sig", 4 * wait), count, epoch)
+                continue
+            exs.append(make_exchange([ar.addr(q, buf, 4 * off) for q, buf, off in dst], ld, row0,
+                                     [ar.addr(q, "sig", 4 * sig) for q in range(W)],
+                                     ar.addr(r, "sig", 4 * wait) if wait is not None else 0,
+                                     count if wait is not None else 0, epoch if wait is not None else 0))
+        self.ex = [tuple(exs[4 * li:4 * li + 4]) for li in range(L)]
+        self.ex_lm = exs[4 * L]
+
+    def _step_peer(self):
+        from . import check, lib
+        B, e = self.B, self.eps
+        xs = self.x[:, self.h_lo:self.h_hi]
+        for (wqkv, wo, wgu, wd), (eq, eo, egu, ed) in zip(self.layers, self.ex):
+            wqkv.mul_mat_f32_peer(self.x, B, self.qkv, eq, rms_eps=e)
+            wo.mul_mat_f32_peer(self.v_full, B, xs, eo, EPI_RESIDUAL, resid=xs)
+            wgu.mul_mat_f32_peer(self.x, B, self.h_full[:, self.f_lo:self.f_hi], egu, EPI_SILU_MUL, rms_eps=e)
+            wd.mul_mat_f32_peer(self.h_full, B, xs, ed, EPI_RESIDUAL, resid=xs)
+        self.lm.mul_mat_f32_peer(self.x, B, self.logits[:, self.v_lo:self.v_hi], self.ex_lm, rms_eps=e)
+        sig, count, epoch = self.end
+        check(lib().smeai_peer_step_end(sig, count, epoch, Q.cur_stream()), "peer_step_end")
+        return self.logits
+
     # --------------------------------------------------------------- one token
     def _lin(self, m, x, out, epilogue=EPI_STORE, resid=None, rms=False, qbuf=None):
         """One linear: y = W Q8_K([rmsnorm] x) with the stack's quantization placement."""
@@ -184,6 +239,8 @@ class Q2KDecodeStack:
                 self.prog = self._build_program()
             self.prog.run()
             return self.logits
+        if self.quant == "peer":
+            return self._step_peer()
         L = self._lin
         for wqkv, wo, wgu, wd in self.layers:
             L(wqkv, self.x, self.qkv, rms=True, qbuf=self.xq)
@@ -229,6 +286,8 @@ class Q2KDecodeStack:
         linear whose quantization is not fused."""
         if self.quant == "program":
             return 1
+        if self.quant == "peer":
+            return self.L * 4 + 2          # the GEMVs and the step-end kernel
         chunks = self.B // 8 + bin(self.B % 8).count("1")
         per_layer = {"fused": 0, "separate": 4, "mixed": 2}[self.quant]
         return (self.L * 4 + 1) * chunks + self.L * per_layer + (1 if self.quant == "separate" else 0)
@@ -254,6 +313,14 @@ class Q2KDecodeStack:
         if self.prog is not None:
             self.prog.free()
             self.prog = None
+        if self.arena is not None:
+            # no rank may still store into this arena: all ranks' steps are done
+            torch.cuda.synchronize(self.dev)
+            import torch.distributed as dist
+            dist.barrier(group=self.group)
+            self.x = self.v_full = self.h_full = self.logits = None
+            self.arena.close()
+            self.arena = None
         for layer in self.layers:
             for m in layer:
                 m.free()

@@ -1,6 +1,8 @@
-"""Row-sharded decode stack on 2 GPUs (NCCL all-gathers) against the
-single-GPU stack: logits must be bit-identical (sharding only moves rows
-between GPUs; every row's arithmetic is unchanged).  Skips with < 2 GPUs."""
+"""Row-sharded decode stack on 2 GPUs against the single-GPU stack, with NCCL
+all-gathers ("separate") and with the all-gather fused into each GEMV over
+CUDA-IPC peer memory ("peer"): logits must be bit-identical (sharding only
+moves rows between GPUs; every row's arithmetic is unchanged), eagerly and
+from a CUDA graph replayed twice.  Skips with < 2 GPUs."""
 import datetime
 import os
 import socket
@@ -22,7 +24,7 @@ def _port():
     return p
 
 
-def _rank(rank, world, port, results):
+def _rank(rank, world, port, quant, results):
     import sys
     root = os.path.abspath(os.path.join(os.path.dirname(__file__), ".."))
     for p in (root, os.path.join(root, "sme-ai-ops_b200")):
@@ -36,31 +38,41 @@ def _rank(rank, world, port, results):
     dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
                             device_id=dev)
     try:
-        st = Q2KDecodeStack(rank=rank, world=world, device=dev, **DIMS)
+        st = Q2KDecodeStack(rank=rank, world=world, device=dev, quant=quant, **DIMS)
+        assert st.quant == quant, st.quant
         eager = st.step().clone()
         stream = torch.cuda.Stream()
         g = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g, stream=stream):
             st.step()
-        with torch.cuda.stream(stream):
-            g.replay()
-        stream.synchronize()
-        results[rank] = (eager.cpu(), st.logits.cpu().clone())
+        graphed = []
+        for _ in range(2):
+            with torch.cuda.stream(stream):
+                g.replay()
+            stream.synchronize()
+            graphed.append(st.logits.cpu().clone())
+        import smeai_b200 as S
+        code = S.take_device_error()
+        results[rank] = (eager.cpu(), graphed, code)
         del g
         dist.barrier()
+        st.free()
     finally:
         dist.destroy_process_group()
 
 
-def test_two_gpu_sharded_stack_matches_single_gpu(cuda):
+@pytest.mark.parametrize("quant", ["separate", "peer"])
+def test_two_gpu_sharded_stack_matches_single_gpu(cuda, quant):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
     from smeai_b200.stack import Q2KDecodeStack
     ref = Q2KDecodeStack(device=cuda, **DIMS).step().cpu().clone()
     torch.cuda.synchronize()
     results = mp.get_context("spawn").Manager().dict()
-    mp.start_processes(_rank, args=(2, _port(), results), nprocs=2, start_method="spawn")
+    mp.start_processes(_rank, args=(2, _port(), quant, results), nprocs=2, start_method="spawn")
     for r in range(2):
-        eager, graphed = results[r]
+        eager, graphed, code = results[r]
+        assert code == 0, (r, code)
         assert torch.equal(eager, ref), r
-        assert torch.equal(graphed, ref), r
+        for gl in graphed:
+            assert torch.equal(gl, ref), r
