@@ -76,8 +76,9 @@ __device__ bool peer_wait(const unsigned* sig, const unsigned* epoch, unsigned c
 __device__ __forceinline__ void peer_signal(const PeerExchange& ex, int lane) {
   __syncwarp();
   if (lane == 0) {
-    __threadfence_system();
-    for (int q = 0; q < ex.n_sig; ++q) atomicAdd_system(ex.sig[q], 1u);
+    asm volatile("fence.acq_rel.sys;" ::: "memory");
+    for (int q = 0; q < ex.n_sig; ++q)
+      asm volatile("red.relaxed.sys.global.add.u32 [%0], 1;" ::"l"(ex.sig[q]) : "memory");
   }
 }
 
