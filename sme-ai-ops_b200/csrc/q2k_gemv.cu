@@ -151,7 +151,7 @@ __device__ __forceinline__ Smem carve(uint8_t* base, int T, int nb, int stages, 
 }
 
 // Ordered sum over super-blocks of one row group, then the epilogue.
-template <int T, int EPI>
+template <int T, int EPI, bool PEER>
 __device__ __forceinline__ void finish_group(const float* terms, int nb, int64_t group, int lane,
                                              const GemvParams& p) {
   if constexpr (EPI == kEpiSiluMul) {
@@ -169,8 +169,10 @@ __device__ __forceinline__ void finish_group(const float* terms, int nb, int64_t
           const float sg = __fdiv_rn(g, __fadd_rn(1.0f, expf(-g)));
           const float h = __fmul_rn(sg, u);
           p.y[t * p.ldy + orow] = h;
-          if (orow >= p.ex.row0)
-            for (int q = 0; q < p.ex.n_dst; ++q) p.ex.dst[q][t * p.ex.ld_dst + (orow - p.ex.row0)] = h;
+          if constexpr (PEER) {
+            if (orow >= p.ex.row0)
+              for (int q = 0; q < p.ex.n_dst; ++q) p.ex.dst[q][t * p.ex.ld_dst + (orow - p.ex.row0)] = h;
+          }
         }
       }
     }
@@ -192,16 +194,20 @@ __device__ __forceinline__ void finish_group(const float* terms, int nb, int64_t
       if (orow < p.n_rows) {
         if constexpr (EPI == kEpiResidual) s = __fadd_rn(p.resid[t * p.ld_resid + orow], s);
         p.y[t * p.ldy + orow] = s;
-        if (orow >= p.ex.row0)
-          for (int q = 0; q < p.ex.n_dst; ++q) p.ex.dst[q][t * p.ex.ld_dst + (orow - p.ex.row0)] = s;
+        if constexpr (PEER) {
+          if (orow >= p.ex.row0)
+            for (int q = 0; q < p.ex.n_dst; ++q) p.ex.dst[q][t * p.ex.ld_dst + (orow - p.ex.row0)] = s;
+        }
       }
     }
   }
 }
 
 // F: the weight format (FmtQ2K, FmtQ3K in q3k_core.cuh) -- tile size, the
-// lane's block load and the integer core; everything else is shared.
-template <class F, int T, int EPI, int IN, bool SUMS>
+// lane's block load and the integer core; everything else is shared.  PEER:
+// the cross-GPU exchange of p.ex is compiled in (a separate instance, so the
+// single-GPU kernels carry none of its code).
+template <class F, int T, int EPI, int IN, bool SUMS, bool PEER>
 __global__ void __launch_bounds__(kMaxThreads) q2k_gemv_kernel(const GemvParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -265,7 +271,7 @@ __global__ void __launch_bounds__(kMaxThreads) q2k_gemv_kernel(const GemvParams 
   // ---- consumers
   const int cw = warp - 1;
   pdl_wait();
-  const bool peer_in = p.ex.wait_sig != nullptr;
+  const bool peer_in = PEER && p.ex.wait_sig != nullptr;
   if (peer_in) {  // the input holds rows other GPUs store: wait for all of them
     int ok = 1;
     if (cw == 0 && lane == 0) {
@@ -371,8 +377,8 @@ __global__ void __launch_bounds__(kMaxThreads) q2k_gemv_kernel(const GemvParams 
           raise_device_error(p.err, kDevErrTimeout);
           return;
         }
-        finish_group<T, EPI>(terms, nb, group, lane, p);
-        if (p.ex.n_sig) peer_signal(p.ex, lane);  // every group: its CTA no longer reads the input
+        finish_group<T, EPI, PEER>(terms, nb, group, lane, p);
+        if (PEER && p.ex.n_sig) peer_signal(p.ex, lane);  // every group: its CTA no longer reads the input
         mbar_arrive_warp(&m.tfree[buf]);
       }
     }
@@ -477,9 +483,9 @@ Plan plan_for(int T, int nb, int64_t n_groups, int tile = kTileBytes) {
 
 int plan_stages(int T, int nb, int tile) { return plan_for(T, nb, 1, tile).stages; }
 
-template <class F, int T, int EPI, int IN, bool SUMS>
+template <class F, int T, int EPI, int IN, bool SUMS, bool PEER = false>
 int launch_gemv(const Q2KWeight& w, GemvParams p, cudaStream_t stream) {
-  auto kern = q2k_gemv_kernel<F, T, EPI, IN, SUMS>;
+  auto kern = q2k_gemv_kernel<F, T, EPI, IN, SUMS, PEER>;
   const Plan pl = plan_for(T, w.nb, w.n_groups, F::kTile);
   if (pl.stages <= 0) {
     set_last_error("q2k_gemv: k=%lld too large for %d tokens per launch", (long long)w.k, T);
@@ -507,19 +513,19 @@ int launch_gemv(const Q2KWeight& w, GemvParams p, cudaStream_t stream) {
   return kOk;
 }
 
-template <class F, int EPI, int IN>
+template <class F, int EPI, int IN, bool PEER = false>
 int dispatch_t(int T, const Q2KWeight& w, const GemvParams& p, cudaStream_t s) {
   switch (T) {
-    case 1: return launch_gemv<F, 1, EPI, IN, false>(w, p, s);
-    case 2: return launch_gemv<F, 2, EPI, IN, false>(w, p, s);
-    case 4: return launch_gemv<F, 4, EPI, IN, false>(w, p, s);
-    case 8: return launch_gemv<F, 8, EPI, IN, false>(w, p, s);
+    case 1: return launch_gemv<F, 1, EPI, IN, false, PEER>(w, p, s);
+    case 2: return launch_gemv<F, 2, EPI, IN, false, PEER>(w, p, s);
+    case 4: return launch_gemv<F, 4, EPI, IN, false, PEER>(w, p, s);
+    case 8: return launch_gemv<F, 8, EPI, IN, false, PEER>(w, p, s);
     default: return kBadArgument;
   }
 }
 
 template <int IN>
-int dispatch_epi(int epi, int T, const Q2KWeight& w, const GemvParams& p, cudaStream_t s) {
+int dispatch_epi(int epi, int T, const Q2KWeight& w, const GemvParams& p, cudaStream_t s, bool peer = false) {
   if (w.fmt == kFmtQ3K || w.fmt == kFmtQ6K) {  // Q3_K / Q6_K weights: the store epilogue
     if (epi != kEpiStore) {
       set_last_error("gemv: only the store epilogue is built for Q3_K and Q6_K weights");
@@ -527,6 +533,16 @@ int dispatch_epi(int epi, int T, const Q2KWeight& w, const GemvParams& p, cudaSt
     }
     return w.fmt == kFmtQ3K ? dispatch_t<FmtQ3K, kEpiStore, IN>(T, w, p, s)
                             : dispatch_t<FmtQ6K, kEpiStore, IN>(T, w, p, s);
+  }
+  if constexpr (IN != kInQ8K) {
+    if (peer) {
+      switch (epi) {
+        case kEpiStore: return dispatch_t<FmtQ2K, kEpiStore, IN, true>(T, w, p, s);
+        case kEpiResidual: return dispatch_t<FmtQ2K, kEpiResidual, IN, true>(T, w, p, s);
+        case kEpiSiluMul: return dispatch_t<FmtQ2K, kEpiSiluMul, IN, true>(T, w, p, s);
+        default: break;
+      }
+    }
   }
   switch (epi) {
     case kEpiStore: return dispatch_t<FmtQ2K, kEpiStore, IN>(T, w, p, s);
@@ -597,9 +613,9 @@ int q2k_gemv_any(const Q2KWeight& w, int in_mode, const void* x, int64_t ld_x, f
   if (ex) {
     const bool single = n_cols == 1 || n_cols == 2 || n_cols == 4 || n_cols == 8;
     if (!single || ex->n_dst < 0 || ex->n_dst > kMaxPeers || ex->n_sig < 0 || ex->n_sig > kMaxPeers ||
-        (ex->wait_sig && (!ex->epoch || !ex->wait_count)) || (ex->wait_sig && in_mode == kInQ8K) ||
+        (ex->wait_sig && (!ex->epoch || !ex->wait_count)) || in_mode == kInQ8K ||
         ex->row0 < 0 || ex->row0 % 16 || (ex->n_dst && ex->ld_dst <= 0)) {
-      set_last_error("q2k_gemv: bad peer exchange (1/2/4/8 tokens, <= %d peers, fp32 input when waiting, "
+      set_last_error("q2k_gemv: bad peer exchange (1/2/4/8 tokens, <= %d peers, fp32 input, "
                      "row0 a multiple of 16)", kMaxPeers);
       return kBadArgument;
     }
@@ -660,8 +676,8 @@ int q2k_gemv_any(const Q2KWeight& w, int in_mode, const void* x, int64_t ld_x, f
     int st;
     switch (in_mode) {
       case kInQ8K: st = dispatch_epi<kInQ8K>(epilogue, T, w, p, stream); break;
-      case kInF32: st = dispatch_epi<kInF32>(epilogue, T, w, p, stream); break;
-      case kInF32Rms: st = dispatch_epi<kInF32Rms>(epilogue, T, w, p, stream); break;
+      case kInF32: st = dispatch_epi<kInF32>(epilogue, T, w, p, stream, ex != nullptr); break;
+      case kInF32Rms: st = dispatch_epi<kInF32Rms>(epilogue, T, w, p, stream, ex != nullptr); break;
       default:
         set_last_error("q2k_gemv: unknown input mode %d", in_mode);
         return kBadArgument;
@@ -711,9 +727,9 @@ int q2k_block_sums(const Q2KWeight& w, const void* xq, int32_t* isum, int32_t* s
   p.x = xq;
   p.isum_out = isum;
   p.summs_out = summs;
-  if (w.fmt == kFmtQ3K) return launch_gemv<FmtQ3K, 1, kEpiStore, kInQ8K, true>(w, p, stream);
-  if (w.fmt == kFmtQ6K) return launch_gemv<FmtQ6K, 1, kEpiStore, kInQ8K, true>(w, p, stream);
-  return launch_gemv<FmtQ2K, 1, kEpiStore, kInQ8K, true>(w, p, stream);
+  if (w.fmt == kFmtQ3K) return launch_gemv<FmtQ3K, 1, kEpiStore, kInQ8K, true, false>(w, p, stream);
+  if (w.fmt == kFmtQ6K) return launch_gemv<FmtQ6K, 1, kEpiStore, kInQ8K, true, false>(w, p, stream);
+  return launch_gemv<FmtQ2K, 1, kEpiStore, kInQ8K, true, false>(w, p, stream);
 }
 
 }  // namespace smeai
