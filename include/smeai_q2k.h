@@ -163,8 +163,9 @@ int smeai_q2k_mul_mat_f32_ex(const void *w_dev, const float *x_dev, size_t ld_x,
  * rows like smeai_q2k_mul_mat_f32_ex and, in the same kernel, stores the rows
  * at or past local output row `row0` of every finished 32-row group into each
  * dst[q] (peer memory opened with smeai_ipc_open, or this GPU's own) at row
- * (r - row0), token stride ld_dst floats, then bumps each sig[q] once per
- * finished group with a system-scope release.  When wait_sig is set the kernel first waits (bounded,
+ * (r - row0), token stride ld_dst floats; when all of a CTA's groups are
+ * stored it raises each sig[q] by its number of row groups (system-scope
+ * fence, then the additions), so every row group of the call counts once.  When wait_sig is set the kernel first waits (bounded,
  * 10 s; a timeout is reported by smeai_take_device_error) until *wait_sig has
  * reached (*epoch + 1) * wait_count -- the row groups every rank of the
  * producing call publishes per step -- so its input may be rows other GPUs

@@ -74,9 +74,10 @@ enum InMode : int { kInQ8K = 0, kInF32 = 1, kInF32Rms = 2 };
 // Cross-GPU exchange of a row-sharded GEMV's output (peer memory mapped
 // through CUDA IPC): the rows of every finished row group at or past local
 // output row row0 are also stored to each dst[q] (at row - row0, token stride
-// ld_dst); then, for every finished group, each sig[q] is bumped once
-// (system-scope release) -- so a full count also says that every CTA of the
-// call has finished reading its input.  A GEMV with
+// ld_dst); once all of a CTA's groups are stored, each sig[q] is raised by
+// the CTA's number of row groups (one system-scope fence, then relaxed
+// reductions) -- so a full count also says that every CTA of the call has
+// finished reading its input.  A GEMV with
 // wait_sig first waits (bounded) until *wait_sig reaches
 // (*epoch + 1) * wait_count -- every rank's row groups of the producing GEMV in
 // this step -- and then reads its input through L2.

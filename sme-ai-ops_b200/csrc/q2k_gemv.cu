@@ -70,16 +70,13 @@ __device__ bool peer_wait(const unsigned* sig, const unsigned* epoch, unsigned c
   }
   return true;
 }
-// Publish one finished row group to every rank: the warp's stores (to this
-// GPU and the peers) are ordered before lane 0's system-scope fence and the
-// signal increments.
-__device__ __forceinline__ void peer_signal(const PeerExchange& ex, int lane) {
-  __syncwarp();
-  if (lane == 0) {
-    asm volatile("fence.acq_rel.sys;" ::: "memory");
-    for (int q = 0; q < ex.n_sig; ++q)
-      asm volatile("red.relaxed.sys.global.add.u32 [%0], 1;" ::"l"(ex.sig[q]) : "memory");
-  }
+// Publish a CTA's finished row groups to every rank, once: the consumer warps'
+// stores (to this GPU and the peers) are ordered by the mbarrier before the
+// one system-scope fence and the signal increments (ng each).
+__device__ __forceinline__ void peer_signal(const PeerExchange& ex, unsigned ng) {
+  asm volatile("fence.acq_rel.sys;" ::: "memory");
+  for (int q = 0; q < ex.n_sig; ++q)
+    asm volatile("red.relaxed.sys.global.add.u32 [%0], %1;" ::"l"(ex.sig[q]), "r"(ng) : "memory");
 }
 
 struct GemvParams {
@@ -115,13 +112,14 @@ struct Smem {
   uint64_t* grp;   // [2] all consumer lanes finished a row group
   uint64_t* tfree; // [2] the finisher has consumed the terms buffer
   uint64_t* rms;   // [2] group sums written / 1/rms ready
+  uint64_t* done;  // [1] every consumer warp has finished its row groups (peer signal)
 };
 
 __host__ __device__ __forceinline__ size_t align16(size_t v) { return (v + 15) & ~(size_t)15; }
 
 __host__ __device__ __forceinline__ size_t smem_fixed_bytes(int T, int nb) {
   return align16((size_t)T * nb * 256) + align16((size_t)T * nb * 32) + align16((size_t)T * nb * 4) +
-         align16((size_t)T * (8 * nb + 1) * 4) + align16((size_t)2 * T * nb * 128) + 8 * 6;
+         align16((size_t)T * (8 * nb + 1) * 4) + align16((size_t)2 * T * nb * 128) + 8 * 7;
 }
 __host__ __device__ __forceinline__ size_t smem_total_bytes(int T, int nb, int stages, int consumers, int tile) {
   return (size_t)stages * consumers * tile + smem_fixed_bytes(T, nb) + (size_t)stages * 16;
@@ -147,6 +145,7 @@ __device__ __forceinline__ Smem carve(uint8_t* base, int T, int nb, int stages, 
   m.grp = m.empty + stages;
   m.tfree = m.grp + 2;
   m.rms = m.tfree + 2;
+  m.done = m.rms + 2;
   return m;
 }
 
@@ -236,6 +235,7 @@ __global__ void __launch_bounds__(kMaxThreads) q2k_gemv_kernel(const GemvParams 
     mbar_init(&m.tfree[1], 1);
     mbar_init(&m.rms[0], kConsumers);
     mbar_init(&m.rms[1], 1);
+    mbar_init(&m.done[0], kConsumers);
     mbar_fence_init();
   }
   __syncthreads();
@@ -378,8 +378,17 @@ __global__ void __launch_bounds__(kMaxThreads) q2k_gemv_kernel(const GemvParams 
           return;
         }
         finish_group<T, EPI, PEER>(terms, nb, group, lane, p);
-        if (PEER && p.ex.n_sig) peer_signal(p.ex, lane);  // every group: its CTA no longer reads the input
         mbar_arrive_warp(&m.tfree[buf]);
+      }
+    }
+  }
+  if constexpr (PEER) {
+    // every group counts (its CTA no longer reads the input): one signal per CTA
+    if (p.ex.n_sig) {
+      mbar_arrive_warp(m.done);
+      if (cw == 0 && lane == 0) {
+        if (mbar_wait_bounded(m.done, 0u, kWaitTimeoutNs)) peer_signal(p.ex, (unsigned)ng);
+        else raise_device_error(p.err, kDevErrTimeout);
       }
     }
   }
