@@ -499,6 +499,9 @@ def run_ours(args):
     clocks = sampler.stop()
     ms = max_over_ranks(ms)
     value = total_bytes / (ms / 1e3) / 1e9
+    code = S.take_device_error()
+    if code:  # a bounded wait gave up (a kernel or a peer never arrived): the timing is void
+        raise S.SmeaiError(f"device error word {code:#x} set during the timed steps")
 
     # ---- end to end: pinned host input -> H2D -> step -> D2H of the result
     host_x = torch.empty(x_in.shape, dtype=torch.float32, pin_memory=True)
