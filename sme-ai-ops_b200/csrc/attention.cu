@@ -19,7 +19,7 @@
 //     of heads -- attn_scores_kernel (64 x 64 score tiles, 4 x 4 per thread,
 //     the 16 dot-product lanes evaluated in the order of their pairwise tree,
 //     so only four partial sums per score are live), attn_softmax_kernel (one
-//     warp per score row) and attn_pv_kernel (64 query rows x head_dim per
+//     warp per score row, held in registers up to 2048 keys) and attn_pv_kernel (64 query rows x head_dim per
 //     CTA, keys in order) -- through a score buffer of heads x S x S floats;
 //   fused (everything else): attention_kernel, one warp per query row.
 // Causal rows skip keys j > i: the reference gives them -1e30, whose
@@ -303,6 +303,7 @@ __global__ void __launch_bounds__(256, 2) attn_scores_kernel(const float* __rest
 // take row blocks from the last one down): max, expf(s - max), the sequential sum (lane 0,
 // j ascending), e / sum; causal rows then zero their entries up to the end
 // of the diagonal 64-key tile, which the weighted-sum kernel reads.
+template <int R>  // R > 0: the row held in registers, R values per lane (S <= 32 R); 0: staged only
 __global__ void __launch_bounds__(256) attn_softmax_kernel(float* __restrict__ sc, int64_t S, int64_t ldsc,
                                                            int causal) {
   extern __shared__ __align__(16) float smem[];
@@ -315,26 +316,55 @@ __global__ void __launch_bounds__(256) attn_softmax_kernel(float* __restrict__ s
   float* row = sc + ((int64_t)blockIdx.y * S + i) * ldsc;
   const int64_t n = causal ? i + 1 : S;
   float mx = -INFINITY;
-  for (int64_t j = lane; j < n; j += 32) {
-    const float v = row[j];
-    e[j] = v;
-    mx = fmaxf(mx, v);
+  float v[R > 0 ? R : 1];
+  if constexpr (R > 0) {
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      const int64_t j = lane + 32 * r;
+      v[r] = j < n ? row[j] : -INFINITY;
+      mx = fmaxf(mx, v[r]);
+    }
+  } else {
+    for (int64_t j = lane; j < n; j += 32) {
+      const float x = row[j];
+      e[j] = x;
+      mx = fmaxf(mx, x);
+    }
   }
 #pragma unroll
   for (int o = 16; o >= 1; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-  for (int64_t j = lane; j < n; j += 32) e[j] = expf(__fsub_rn(e[j], mx));
+  if constexpr (R > 0) {
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      const int64_t j = lane + 32 * r;
+      if (j < n) {
+        v[r] = expf(__fsub_rn(v[r], mx));
+        e[j] = v[r];
+      }
+    }
+  } else {
+    for (int64_t j = lane; j < n; j += 32) e[j] = expf(__fsub_rn(e[j], mx));
+  }
   __syncwarp();
   float sum = 0.f;
-  if (lane == 0) {
+  if (lane == 0) {  // in key order, four at a time from shared memory
     int64_t j = 0;
     for (; j + 4 <= n; j += 4) {
-      const float a = e[j], b = e[j + 1], c = e[j + 2], d = e[j + 3];
-      sum = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(sum, a), b), c), d);
+      const float4 q = *reinterpret_cast<const float4*>(e + j);
+      sum = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(sum, q.x), q.y), q.z), q.w);
     }
     for (; j < n; ++j) sum = __fadd_rn(sum, e[j]);
   }
   sum = __shfl_sync(0xffffffffu, sum, 0);
-  for (int64_t j = lane; j < n; j += 32) row[j] = sum == 0.f ? 0.f : __fdiv_rn(e[j], sum);
+  if constexpr (R > 0) {
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      const int64_t j = lane + 32 * r;
+      if (j < n) row[j] = sum == 0.f ? 0.f : __fdiv_rn(v[r], sum);
+    }
+  } else {
+    for (int64_t j = lane; j < n; j += 32) row[j] = sum == 0.f ? 0.f : __fdiv_rn(e[j], sum);
+  }
   if (causal) {
     const int64_t tile_end = (i / kTQ + 1) * kTQ;
     const int64_t jend = tile_end < S ? tile_end : S;
@@ -444,12 +474,16 @@ int attention_tiled(const float* Q, const float* K, const float* V, int64_t S, i
   const size_t sm_smem = (size_t)warps * ldsc * sizeof(float);
   auto scores_k = hd == 32 ? attn_scores_kernel<32> : hd == 64 ? attn_scores_kernel<64> : attn_scores_kernel<128>;
   SMEAI_CUDA_TRY(cudaFuncSetAttribute(scores_k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sc_smem));
-  SMEAI_CUDA_TRY(cudaFuncSetAttribute(attn_softmax_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm_smem));
+  auto softmax_k = S <= 512    ? attn_softmax_kernel<16>
+                   : S <= 1024 ? attn_softmax_kernel<32>
+                   : S <= 2048 ? attn_softmax_kernel<64>
+                               : attn_softmax_kernel<0>;
+  SMEAI_CUDA_TRY(cudaFuncSetAttribute(softmax_k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm_smem));
   for (int64_t h0 = 0; h0 < heads; h0 += hc_max) {
     const int64_t hc = heads - h0 < hc_max ? heads - h0 : hc_max;
     SMEAI_CUDA_TRY(launch(scores_k, dim3((unsigned)pairs, (unsigned)hc), dim3(256), sc_smem, s, Q, K, S, D, (int)h0,
                           scale, causal, tiles, scores, ldsc));
-    SMEAI_CUDA_TRY(launch(attn_softmax_kernel, dim3((unsigned)((S + warps - 1) / warps), (unsigned)hc),
+    SMEAI_CUDA_TRY(launch(softmax_k, dim3((unsigned)((S + warps - 1) / warps), (unsigned)hc),
                           dim3(warps * 32), sm_smem, s, scores, S, ldsc, causal));
     const dim3 pv_grid((unsigned)((S + kTQ - 1) / kTQ), (unsigned)hc);
     if (hd == 32)
