@@ -239,18 +239,26 @@ __global__ void __launch_bounds__(256, 2) attn_scores_kernel(const float* __rest
   pdl_trigger();
   pdl_wait();
   const float4 z4 = make_float4(0.f, 0.f, 0.f, 0.f);
-  for (int e = tid; e < kTQ * hd / 4; e += 256) {
-    const int r = e % kTQ, c = (e / kTQ) * 4;
-    const float4 q = i0 + r < S ? *reinterpret_cast<const float4*>(Q + (i0 + r) * D + off + c) : z4;
-    const float4 k = j0 + r < S ? *reinterpret_cast<const float4*>(K + (j0 + r) * D + off + c) : z4;
-    Qt[(c + 0) * kTQ + r] = q.x;
-    Qt[(c + 1) * kTQ + r] = q.y;
-    Qt[(c + 2) * kTQ + r] = q.z;
-    Qt[(c + 3) * kTQ + r] = q.w;
-    Kt[(c + 0) * kTQ + r] = k.x;
-    Kt[(c + 1) * kTQ + r] = k.y;
-    Kt[(c + 2) * kTQ + r] = k.z;
-    Kt[(c + 3) * kTQ + r] = k.w;
+  // all of the thread's tile loads in flight at once, then the transposed stores
+  constexpr int kIt = kTQ * hd / 4 / 256;
+  float4 qv[kIt], kv[kIt];
+#pragma unroll
+  for (int it = 0; it < kIt; ++it) {
+    const int e = tid + 256 * it, r = e % kTQ, c = (e / kTQ) * 4;
+    qv[it] = i0 + r < S ? *reinterpret_cast<const float4*>(Q + (i0 + r) * D + off + c) : z4;
+    kv[it] = j0 + r < S ? *reinterpret_cast<const float4*>(K + (j0 + r) * D + off + c) : z4;
+  }
+#pragma unroll
+  for (int it = 0; it < kIt; ++it) {
+    const int e = tid + 256 * it, r = e % kTQ, c = (e / kTQ) * 4;
+    Qt[(c + 0) * kTQ + r] = qv[it].x;
+    Qt[(c + 1) * kTQ + r] = qv[it].y;
+    Qt[(c + 2) * kTQ + r] = qv[it].z;
+    Qt[(c + 3) * kTQ + r] = qv[it].w;
+    Kt[(c + 0) * kTQ + r] = kv[it].x;
+    Kt[(c + 1) * kTQ + r] = kv[it].y;
+    Kt[(c + 2) * kTQ + r] = kv[it].z;
+    Kt[(c + 3) * kTQ + r] = kv[it].w;
   }
   __syncthreads();
 
@@ -399,23 +407,43 @@ __global__ void __launch_bounds__(256) attn_pv_kernel(const float* __restrict__ 
   pdl_trigger();
   pdl_wait();
   const float4 z4 = make_float4(0.f, 0.f, 0.f, 0.f);
+  // the next step's P and V are fetched into registers while the current
+  // step's products run, then stored over the shared tiles
+  constexpr int kPIt = kTQ * kTJ / 4 / 256, kVIt = kTJ * HD / 4 / 256;
+  float4 pr[kPIt], vr[kVIt];
+  auto fetch = [&](int64_t j0) {
+#pragma unroll
+    for (int it = 0; it < kPIt; ++it) {  // P rows i0 + r, keys j0 + c .. c+3
+      const int e = tid + 256 * it, r = e % kTQ, c = (e / kTQ) * 4;
+      pr[it] = (i0 + r < S && j0 + c < jmax) ? *reinterpret_cast<const float4*>(P + (i0 + r) * ldsc + j0 + c) : z4;
+    }
+#pragma unroll
+    for (int it = 0; it < kVIt; ++it) {
+      const int e = tid + 256 * it, r = e / (HD / 4), c = (e % (HD / 4)) * 4;
+      vr[it] = j0 + r < jmax ? *reinterpret_cast<const float4*>(V + (j0 + r) * D + off + c) : z4;
+    }
+  };
+  auto stash = [&]() {
+#pragma unroll
+    for (int it = 0; it < kPIt; ++it) {
+      const int e = tid + 256 * it, r = e % kTQ, c = (e / kTQ) * 4;
+      Pt[c + 0][r] = pr[it].x;
+      Pt[c + 1][r] = pr[it].y;
+      Pt[c + 2][r] = pr[it].z;
+      Pt[c + 3][r] = pr[it].w;
+    }
+#pragma unroll
+    for (int it = 0; it < kVIt; ++it) {
+      const int e = tid + 256 * it, r = e / (HD / 4), c = (e % (HD / 4)) * 4;
+      *reinterpret_cast<float4*>(&Vs[r][c]) = vr[it];
+    }
+  };
+  fetch(0);
   for (int64_t j0 = 0; j0 < jmax; j0 += kTJ) {
+    __syncthreads();  // the previous step's products are done with the tiles
+    stash();
     __syncthreads();
-    for (int e = tid; e < kTQ * kTJ / 4; e += 256) {  // P rows i0 + r, keys j0 + c .. c+3
-      const int r = e % kTQ, c = (e / kTQ) * 4;
-      float4 v = z4;
-      if (i0 + r < S && j0 + c < jmax) v = *reinterpret_cast<const float4*>(P + (i0 + r) * ldsc + j0 + c);
-      Pt[c + 0][r] = v.x;
-      Pt[c + 1][r] = v.y;
-      Pt[c + 2][r] = v.z;
-      Pt[c + 3][r] = v.w;
-    }
-    for (int e = tid; e < kTJ * HD / 4; e += 256) {
-      const int r = e / (HD / 4), c = (e % (HD / 4)) * 4;
-      *reinterpret_cast<float4*>(&Vs[r][c]) =
-          j0 + r < jmax ? *reinterpret_cast<const float4*>(V + (j0 + r) * D + off + c) : z4;
-    }
-    __syncthreads();
+    if (j0 + kTJ < jmax) fetch(j0 + kTJ);
 #pragma unroll 4
     for (int jj = 0; jj < kTJ; ++jj) {
       const float4 p4 = *reinterpret_cast<const float4*>(&Pt[jj][ty * 4]);
