@@ -1,5 +1,5 @@
 #!/usr/bin/env python
-"""Benchmark of the Q2_K mul_mat hot path on B200 (see DESIGN.md for the metric).
+"""Benchmark of the Q2_K mul_mat hot path on B200 (one JSON line per run; the metric is defined below).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
                     [--workload decode|gemv|prefill] [--quant program|separate|fused|mixed]
