@@ -1,7 +1,7 @@
 """ctypes view of the CPU oracle (oracle/smeai_oracle.c).
 
 TEST INFRASTRUCTURE ONLY: imported by tests/, ``__graft_entry__.smoke()`` and
-the CPU-baseline leg of ``bench.py`` as the checker.  The product library never
+the CPU-baseline leg of ``bench.py`` to produce the expected results.  The product library never
 imports it.
 
 Arrays are numpy; Q2_K / Q8_K blocks are structured numpy arrays whose byte
