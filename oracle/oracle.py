@@ -1,8 +1,8 @@
 """ctypes view of the CPU oracle (oracle/smeai_oracle.c).
 
-TEST INFRASTRUCTURE ONLY: imported by tests/, ``__graft_entry__.smoke()`` and
-the CPU-baseline leg of ``bench.py`` to produce the expected results.  The product library never
-imports it.
+TEST INFRASTRUCTURE ONLY: imported by tests/ and ``__graft_entry__.smoke()`` for
+the expected results, and timed by the CPU-baseline leg of ``bench.py``.  The
+product library never imports it.
 
 Arrays are numpy; Q2_K / Q8_K blocks are structured numpy arrays whose byte
 layout equals ggml's block_q2_K (84 B) and block_q8_K (292 B).
