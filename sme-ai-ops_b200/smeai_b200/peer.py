@@ -10,6 +10,7 @@ signal word in the same kernel (smeai_q2k_mul_mat_f32_peer).
 """
 from __future__ import annotations
 
+import contextlib
 import ctypes
 import math
 
@@ -86,10 +87,15 @@ class PeerArena:
         self.nbytes = total
         L = lib()
         ptr, handle = ctypes.c_void_p(), (ctypes.c_ubyte * 64)()
-        # every rank takes part in both exchanges, so a local failure cannot
-        # leave the others waiting in a collective; the decision is shared
-        with torch.cuda.device(device):
-            ok = L.smeai_ipc_alloc(total, ctypes.byref(ptr), handle) == 0
+        on_dev = lambda: torch.cuda.device(device) if device is not None else contextlib.nullcontext()
+        # every rank takes part in both exchanges, so a local failure (an error
+        # code or an exception) cannot leave the others waiting in a
+        # collective; the decision is shared
+        try:
+            with on_dev():
+                ok = L.smeai_ipc_alloc(total, ctypes.byref(ptr), handle) == 0
+        except Exception:
+            ok = False
         self.local = ptr.value if ok else 0
         self.base, self._opened, self._span = [0] * world, [], None
         handles = [None] * world
@@ -101,10 +107,14 @@ class PeerArena:
                     continue
                 hq = (ctypes.c_ubyte * 64).from_buffer_copy(handles[q])
                 pq = ctypes.c_void_p()
-                with torch.cuda.device(device):
-                    if L.smeai_ipc_open(hq, ctypes.byref(pq)) != 0:
-                        ok = False
-                        break
+                try:
+                    with on_dev():
+                        opened = L.smeai_ipc_open(hq, ctypes.byref(pq)) == 0
+                except Exception:
+                    opened = False
+                if not opened:
+                    ok = False
+                    break
                 self.base[q] = pq.value
                 self._opened.append(pq.value)
         else:
