@@ -72,6 +72,8 @@ def parse_args():
     ap.add_argument("--gemv-epilogue", type=int, default=0, help="gemv workload: 0 store, 1 residual, 2 silu*mul")
     ap.add_argument("--gemv-fmt", choices=["q2k", "q3k", "q6k"], default="q2k", help="gemv workload: weight format")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-configs", action="store_true",
+                    help="decode on one GPU: skip the per-configuration measurements (configs 1-4)")
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="bounded CPU sample length")
     return ap.parse_args()
 
@@ -161,9 +163,10 @@ class ClockSampler:
 class CpuLayerSample:
     """The oracle (ggml generic-C restatement) on one full layer of the stack:
     qkv, o, gate+up and down GEMVs at full shape, batch 1, rows split over
-    the host's cores with OpenMP.  Weights are valid random Q2_K blocks with
-    the magnitudes of quantized N(0, 0.02) draws (the CPU work does not
-    depend on the values); activations are Q8_K of N(0, 1)."""
+    the host's cores with OpenMP.  Weights are random Q2_K blocks with the
+    magnitudes of quantized N(0, 0.02) draws, not the GPU run's seeded
+    weights: the generic dot's work does not depend on the values.
+    Activations are Q8_K of N(0, 1)."""
 
     def __init__(self, hidden=4096, ffn=11008, n_threads=1, seed=0):
         import numpy as np
@@ -186,9 +189,9 @@ class CpuLayerSample:
         self.xs = {k: O.quantize_q8_K(rng.standard_normal(k).astype(np.float32)) for k in (hidden, ffn)}
         self.layer_bytes = sum(gemv_bytes(r, k, 1) for r, k in self.mats)
 
-    def run_once(self):
+    def run_once(self, threads=None):
         for (r, k), w in zip(self.mats, self.ws):
-            self.O.q2k_mul_mat(w, r, k, self.xs[k], 1, n_threads=self.threads)
+            self.O.q2k_mul_mat(w, r, k, self.xs[k], 1, n_threads=self.threads if threads is None else threads)
 
     def timed(self, seconds):
         """Repeat the layer until `seconds` elapsed (at least once): (GB/s, s per layer, reps)."""
@@ -201,6 +204,313 @@ class CpuLayerSample:
                 break
         per_layer = el / reps
         return self.layer_bytes / per_layer / 1e9, per_layer, reps
+
+
+def cpu_rate(unit_fn, seconds, threads):
+    """Repeat unit_fn(threads) until `seconds` elapsed (at least twice):
+    seconds per unit, units run."""
+    unit_fn(threads)
+    reps, t0 = 0, time.perf_counter()
+    while True:
+        unit_fn(threads)
+        reps += 1
+        el = time.perf_counter() - t0
+        if el >= seconds and reps >= 2:
+            return el / reps, reps
+
+
+def cpu_baseline_pair(unit_fn, seconds, per_unit, unit, sample, single_only=False):
+    """CPU baseline of the oracle (-march=native build) on this host: one
+    thread and every host thread (OpenMP rows).  per_unit converts seconds
+    per unit into the metric's unit.  value = the all-cores figure."""
+    from oracle import oracle as O
+    O.select(native=True)
+    try:
+        threads = os.cpu_count() or 1
+        s1, r1 = cpu_rate(unit_fn, seconds, 1)
+        out = {"unit": unit, "kind": "port", "cpu_model": O.cpu_model(), "nproc": threads,
+               "build": "gcc -O3 -march=native -ffp-contract=off -fopenmp",
+               "single_thread": {"value": per_unit(s1), "cores": 1, "reps": r1}}
+        if single_only:
+            out.update(value=per_unit(s1), cores=1, sample=sample + " (a scalar loop: one thread)")
+        else:
+            sa, ra = cpu_rate(unit_fn, seconds, threads)
+            out["all_cores"] = {"value": per_unit(sa), "cores": threads, "reps": ra}
+            out.update(value=per_unit(sa), cores=threads, sample=sample)
+        return out
+    finally:
+        O.select(native=False)
+
+
+def graph_time(step, stream, calls, replays, warmup):
+    """Capture `calls` back-to-back calls of step() in a CUDA graph, replay it
+    `warmup` times, then time `replays` replays with CUDA events on the stream:
+    device ms per call."""
+    import torch
+    with torch.cuda.stream(stream):
+        step()
+    stream.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=stream):
+        for _ in range(calls):
+            step()
+    for _ in range(max(3, warmup)):
+        with torch.cuda.stream(stream):
+            g.replay()
+    stream.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    with torch.cuda.stream(stream):
+        for _ in range(replays):
+            g.replay()
+    e1.record(stream)
+    e1.synchronize()
+    ms = e0.elapsed_time(e1) / (replays * calls)
+    del g
+    return ms
+
+
+def per_launch_ms(launch, stream, n):
+    """Median device time of n single launches, each bracketed by events on
+    the stream and queued behind a sleep kernel (launch gaps do not count)."""
+    import torch
+    evs = []
+    with torch.cuda.stream(stream):
+        torch.cuda._sleep(20_000_000)
+        for i in range(n):
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            launch(i)
+            b.record(stream)
+            evs.append((a, b))
+    stream.synchronize()
+    return statistics.median(a.elapsed_time(b) for a, b in evs)
+
+
+def run_configs(dev, stream, args, peak, peak_kind):
+    """Configurations 1-4 of the workload list, each with its own value,
+    roofline and CPU baseline (the headline is configuration 5)."""
+    import ctypes
+
+    import numpy as np
+    import torch
+
+    import smeai_b200 as S
+    from oracle import oracle as O
+    from smeai_b200 import q2k as Q
+    from smeai_b200.stack import gemv_bytes
+    L = S.lib()
+    P = ctypes.c_void_p
+    cpu_s = max(1.5, args.cpu_seconds / 5)
+    steps, warm = max(args.steps, 10), args.warmup
+    fp32_peak = 148 * 128 * 2 * 1.965e9 / 1e12
+    out = {}
+
+    # ---- 1: fp16-ABI packed Linear X[128,512] . W[512,512]^T + b
+    B, K, N = 128, 512, 512
+    rng = np.random.default_rng(0)
+    x16 = rng.standard_normal((B, K)).astype(np.float16)
+    w = rng.uniform(-1 / np.sqrt(K), 1 / np.sqrt(K), (N, K)).astype(np.float32)
+    wt16 = np.ascontiguousarray(w.T).astype(np.float16)          # the ABI's W[in][out]
+    bias = (rng.standard_normal(N) * 0.02).astype(np.float32)
+    ws, pw = S.Workspace(), S.PackedWeight()
+    S.check(L.sme_ai_workspace_init(ctypes.byref(ws), B, K, N), "workspace_init")
+    S.check(L.sme_ai_packed_linear_weight_init(ctypes.byref(pw), P(wt16.ctypes.data), K, N), "packed_init")
+    xd = torch.from_numpy(x16.view(np.int16)).to(dev)
+    bd = torch.from_numpy(bias).to(dev)
+    yd = torch.empty((B, N), device=dev)
+    st = P(stream.cuda_stream)
+    lin = lambda: L.sme_ai_linear_packed_f16f32_device(P(xd.data_ptr()), B, ctypes.byref(pw), P(bd.data_ptr()), 0,
+                                                      P(yd.data_ptr()), st)
+    ms = graph_time(lin, stream, 50, steps, warm)
+    flops = 2 * B * K * N
+    exp = O.linear_f16f32(x16.view(np.uint16), B, K, wt16.view(np.uint16), N, bias)
+    exact = bool(np.array_equal(yd.cpu().numpy().view(np.uint32), exp.view(np.uint32)))
+    yh = np.zeros((B, N), np.float32)
+    host = lambda: L.sme_ai_linear_sme_packed_f16f32(ctypes.byref(ws), P(x16.ctypes.data), B, ctypes.byref(pw),
+                                                     P(bias.ctypes.data), P(yh.ctypes.data))
+    host()
+    t0, reps = time.perf_counter(), 0
+    while reps < 200:
+        host()
+        reps += 1
+    e2e_ms = (time.perf_counter() - t0) / reps * 1e3
+    one = lambda n: O.linear_f16f32(x16.view(np.uint16), B, K, wt16.view(np.uint16), N, bias)
+    out["config1_fp_linear"] = {
+        "workload": "fp16-ABI packed Linear X[128,512] ~N(0,1) . W[512,512]^T ~U(+-1/sqrt(512)) + b ~N(0,0.02) "
+                    "-> fp32 (sme_ai_linear_packed_f16f32_device)",
+        "value": flops / (ms / 1e3) / 1e9, "unit": "GFLOP/s", "us_per_call": ms * 1e3,
+        "bit_exact_vs_oracle": exact,
+        "e2e": {"value": flops / (e2e_ms / 1e3) / 1e9, "unit": "GFLOP/s", "us_per_call": e2e_ms * 1e3,
+                "entry": "sme_ai_linear_sme_packed_f16f32 (host buffers, synchronous)",
+                "h2d_bytes_per_call": B * K * 2 + N * 4, "d2h_bytes_per_call": B * N * 4},
+        "roofline": {"bound": "fp32 FFMA (latency at this size)", "achieved": flops / (ms / 1e3) / 1e12,
+                     "peak": fp32_peak, "unit": "TFLOP/s", "frac": flops / (ms / 1e3) / 1e12 / fp32_peak,
+                     "peak_kind": "nominal FP32 CUDA-core rate (no measured fp32 peak on this pool)",
+                     "traffic": None, "flops_per_launch": flops},
+        "cpu_baseline": cpu_baseline_pair(one, cpu_s, lambda sec: flops / sec / 1e9, "GFLOP/s",
+                                          "the oracle's scalar_matmul_f16f16_f32 restatement on the same inputs",
+                                          single_only=True),
+    }
+    L.sme_ai_packed_linear_weight_destroy(ctypes.byref(pw))
+    L.sme_ai_workspace_destroy(ctypes.byref(ws))
+
+    # ---- 2: Q2_K x Q8_K GEMV W[4096,4096]
+    rows, k = 4096, 4096
+    nb = k // 256
+    mbytes = rows * nb * 84
+    copies = max(4, -(-4 * 126 * 2**20 // mbytes))
+    g = torch.Generator(device=dev).manual_seed(0)
+    blocks = [Q.quantize_q2k(torch.randn((rows, k), generator=g, device=dev) * 0.02) for _ in range(copies)]
+    mats = [Q.Q2KMatrix(b, rows, k) for b in blocks]
+    x = torch.randn((1, k), generator=g, device=dev)
+    xq = Q.quantize_q8k(x)
+    y = torch.empty((1, rows), device=dev)
+    it = {"i": 0}
+
+    def gemv_step():
+        m = mats[it["i"] % copies]
+        it["i"] += 1
+        m.mul_mat(xq, 1, out=y)
+
+    ms = graph_time(gemv_step, stream, copies, steps, warm)
+    nbytes = gemv_bytes(rows, k, 1)
+    lms = per_launch_ms(lambda i: mats[i % copies].mul_mat(xq, 1, out=y), stream, 16)
+    w0 = blocks[0].cpu().numpy().reshape(-1).view(O.BLOCK_Q2_K)
+    xq0 = xq.cpu().numpy().reshape(-1).view(O.BLOCK_Q8_K)
+    exact = bool(np.array_equal(mats[0].mul_mat(xq, 1).cpu().numpy().view(np.uint32),
+                                O.q2k_mul_mat(w0, rows, k, xq0, 1, n_threads=os.cpu_count()).view(np.uint32)))
+    ratio = traffic_ratio()
+    out["config2_gemv"] = {
+        "workload": f"Q2_K x Q8_K GEMV W[4096,4096] ~N(0,0.02) -> Q2_K, x[4096] ~N(0,1) -> Q8_K, y[4096]; "
+                    f"{copies} rotating weight copies ({copies * mbytes / 2**20:.0f} MB > L2)",
+        "value": nbytes / (ms / 1e3) / 1e9, "unit": "GB/s", "us_per_call": ms * 1e3, "bit_exact_vs_oracle": exact,
+        "roofline": {"bound": "hbm", "kernel": "q2k_gemv_kernel", "achieved": nbytes / (lms / 1e3) / 1e9,
+                     "peak": peak, "unit": "GB/s", "frac": nbytes / (lms / 1e3) / 1e9 / peak, "peak_kind": peak_kind,
+                     "traffic": ratio * nbytes if ratio else None, "algorithmic_bytes_per_launch": nbytes,
+                     "median_launch_us": lms * 1e3},
+        "cpu_baseline": cpu_baseline_pair(lambda n: O.q2k_mul_mat(w0, rows, k, xq0, 1, n_threads=n), cpu_s,
+                                          lambda sec: nbytes / sec / 1e9, "GB/s",
+                                          "the oracle's generic-C Q2_K x Q8_K dot over the same W and x"),
+    }
+    del mats, blocks
+
+    # ---- 3: SwiGLU MLP decode, batch 1 and 8 (the two phases as one program launch)
+    H, F = 4096, 11008
+    per_copy = (2 * F * (H // 256) + H * (F // 256)) * 84
+    copies = max(3, -(-4 * 126 * 2**20 // per_copy))
+    gu_m, dn_m, blk = [], [], None
+    for c in range(copies):
+        wg = Q.quantize_q2k(torch.randn((F, H), generator=g, device=dev) * 0.02)
+        wu = Q.quantize_q2k(torch.randn((F, H), generator=g, device=dev) * 0.02)
+        wd = Q.quantize_q2k(torch.randn((H, F), generator=g, device=dev) * 0.02)
+        gu_m.append(Q.Q2KMatrix(torch.stack([wg, wu], 1).reshape(2 * F, -1), 2 * F, H))
+        dn_m.append(Q.Q2KMatrix(wd, H, F))
+        if c == 0:
+            blk = [t.cpu().numpy().reshape(-1).view(O.BLOCK_Q2_K) for t in (wg, wu, wd)]
+        del wg, wu, wd
+    for B in (1, 8):
+        xb = torch.randn((B, H), generator=g, device=dev)
+        hb = torch.empty((B, F), device=dev)
+        yb = torch.empty((B, H), device=dev)
+        progs = [Q.Q2KProgram([dict(w=gu_m[c], x=xb, input=S.IN_F32, y=hb, epilogue=S.EPI_SILU_MUL),
+                               dict(w=dn_m[c], x=hb, input=S.IN_F32, y=yb)], B) for c in range(copies)]
+        it = {"i": 0}
+
+        def mlp_step():
+            progs[it["i"] % copies].run()
+            it["i"] += 1
+
+        ms = graph_time(mlp_step, stream, copies, steps, warm)
+        nbytes = gemv_bytes(2 * F, H, B, F) + gemv_bytes(H, F, B)
+        lms = per_launch_ms(lambda i: progs[i % copies].run(), stream, 12)
+        progs[0].run()
+        torch.cuda.synchronize()
+        y_gpu, h_gpu = yb.cpu().numpy(), hb.cpu().numpy()
+        xq_o = O.quantize_q8_K(xb.cpu().numpy().reshape(-1))
+        gg = O.q2k_mul_mat(blk[0], F, H, xq_o, B, n_threads=os.cpu_count())
+        uu = O.q2k_mul_mat(blk[1], F, H, xq_o, B, n_threads=os.cpu_count())
+        h_o = O.silu_mul(gg.reshape(-1), uu.reshape(-1)).reshape(B, F)
+        hq_o = O.quantize_q8_K(h_gpu.reshape(-1))
+        y_o = O.q2k_mul_mat(blk[2], H, F, hq_o, B, n_threads=os.cpu_count())
+        ok = bool(np.all(np.abs(h_gpu - h_o) <= 1e-5 * np.abs(h_o) + 1e-30) and
+                  np.array_equal(y_gpu.view(np.uint32), y_o.view(np.uint32)))
+
+        def mlp_cpu(n, B=B, xq_o=xq_o):
+            g_ = O.q2k_mul_mat(blk[0], F, H, xq_o, B, n_threads=n)
+            u_ = O.q2k_mul_mat(blk[1], F, H, xq_o, B, n_threads=n)
+            h_ = O.silu_mul(g_.reshape(-1), u_.reshape(-1))
+            O.q2k_mul_mat(blk[2], H, F, O.quantize_q8_K(h_), B, n_threads=n)
+
+        out[f"config3_swiglu_b{B}"] = {
+            "workload": f"SwiGLU MLP decode, batch {B}: hidden 4096, ffn 11008, W_gate/W_up[11008,4096] and "
+                        f"W_down[4096,11008] ~N(0,0.02) Q2_K, x ~N(0,1); gate/up (silu*mul) and down as one "
+                        f"q2k_program launch; {copies} rotating weight copies ({copies * per_copy / 2**20:.0f} MB)",
+            "value": nbytes / (ms / 1e3) / 1e9, "unit": "GB/s", "us_per_call": ms * 1e3,
+            "tokens_per_s": B / (ms / 1e3), "matches_oracle": ok,
+            "roofline": {"bound": "hbm", "kernel": "q2k_program_kernel", "achieved": nbytes / (lms / 1e3) / 1e9,
+                         "peak": peak, "unit": "GB/s", "frac": nbytes / (lms / 1e3) / 1e9 / peak,
+                         "peak_kind": peak_kind, "traffic": None, "algorithmic_bytes_per_launch": nbytes,
+                         "median_launch_us": lms * 1e3},
+            "cpu_baseline": cpu_baseline_pair(mlp_cpu, cpu_s, lambda sec: nbytes / sec / 1e9, "GB/s",
+                                              f"the oracle's generic-C dots of the same MLP, batch {B}"),
+        }
+        for pr in progs:
+            pr.free()
+    del gu_m, dn_m
+
+    # ---- 4: prefill mul_mat [512,4096] x W[11008,4096] on tcgen05
+    rows, k, cols = 11008, 4096, 512
+    copies = max(2, -(-4 * 126 * 2**20 // (rows * (k // 256) * 84)))
+    wblocks0 = Q.quantize_q2k(torch.randn((rows, k), generator=g, device=dev) * 0.02)
+    mats = [Q.Q2KMatrix(wblocks0, rows, k)] + [
+        Q.Q2KMatrix(Q.quantize_q2k(torch.randn((rows, k), generator=g, device=dev) * 0.02), rows, k)
+        for _ in range(copies - 1)]
+    xa = torch.randn((cols, k), generator=g, device=dev)
+    xqa = Q.quantize_q8k(xa)
+    ya = torch.empty((cols, rows), device=dev)
+    it = {"i": 0}
+
+    def gemm_step():
+        mats[it["i"] % copies].mul_mat_tc(xqa, cols, out=ya)
+        it["i"] += 1
+
+    ms = graph_time(gemm_step, stream, copies, steps, warm)
+    ops = 2 * rows * k * cols
+    lms = per_launch_ms(lambda i: mats[i % copies].mul_mat_tc(xqa, cols, out=ya), stream, 8)
+    tpeak, tkind = tensor_peak()
+    i8peak = 2 * tpeak
+    mats[0].mul_mat_tc(xqa, cols, out=ya)
+    torch.cuda.synchronize()
+    w0 = wblocks0.cpu().numpy().reshape(-1).view(O.BLOCK_Q2_K)
+    xq_all = xqa.cpu().numpy().reshape(cols, -1)
+    sample_rows = [0, 1, 137, 255, 256, 511]
+    exp = O.q2k_mul_mat(w0, rows, k, np.ascontiguousarray(xq_all[sample_rows]).reshape(-1).view(O.BLOCK_Q8_K),
+                        len(sample_rows), n_threads=os.cpu_count())
+    exact = bool(np.array_equal(ya.cpu().numpy()[sample_rows].view(np.uint32), exp.view(np.uint32)))
+    cs = 16                                      # CPU sample: 16 of the 512 activation rows
+    xq_s = np.ascontiguousarray(xq_all[:cs]).reshape(-1).view(O.BLOCK_Q8_K)
+    s_ops = 2 * rows * k * cs
+    out["config4_prefill"] = {
+        "workload": "Q2_K prefill mul_mat: activations [512,4096] ~N(0,1) (Q8_K per row) x W[11008,4096] "
+                    f"~N(0,0.02) Q2_K -> fp32 [512,11008] on tcgen05 (kind::i8 + kind::f16); {copies} rotating "
+                    "weight copies",
+        "value": ops / (ms / 1e3) / 1e12, "unit": "TOPS", "us_per_call": ms * 1e3,
+        "bit_exact_vs_oracle_sampled_rows": exact,
+        "roofline": {"bound": "tensor", "kernel": "q2k_gemm_tc_kernel (+ operand prepass)",
+                     "achieved": ops / (lms / 1e3) / 1e12, "peak": i8peak, "unit": "TOPS",
+                     "frac": ops / (lms / 1e3) / 1e12 / i8peak,
+                     "peak_kind": f"int8 dense taken as 2 x the {tkind} bf16 GEMM rate ({tpeak:.1f} TFLOP/s)",
+                     "frac_of_bf16_peak": ops / (lms / 1e3) / 1e12 / tpeak,
+                     "traffic": None, "ops_per_launch": ops, "median_launch_us": lms * 1e3},
+        "cpu_baseline": cpu_baseline_pair(lambda n: O.q2k_mul_mat(w0, rows, k, xq_s, cs, n_threads=n), cpu_s,
+                                          lambda sec: s_ops / sec / 1e12, "TOPS",
+                                          f"the oracle's generic-C dot on {cs} of the 512 activation rows "
+                                          "(same W), scaled per op"),
+    }
+    del mats
+    torch.cuda.synchronize()
+    return out
 
 
 def stack_bytes_per_token(L, H, F, V):
@@ -218,6 +528,7 @@ def run_reference(args):
         return 0
     from oracle import oracle as O
     O.build()
+    O.select(native=True)            # the -march=native build of this host
     threads = os.cpu_count() or 1
     dims = dict(hidden=4096, ffn=11008, vocab=32000, n_layers=32)
     tok_bytes = stack_bytes_per_token(32, 4096, 11008, 32000)
@@ -239,9 +550,12 @@ def run_reference(args):
         "config": {"workload": "llama2-7b-shape Q2_K linear stack decode, batch 1 (one layer per step)",
                    "global_batch": 1, "parallelism": f"cpu threads {threads}"},
         "cpu_baseline": {"value": value, "unit": "GB/s", "cores": threads, "kind": "port",
+                         "cpu_model": O.cpu_model(), "nproc": threads,
+                         "build": "gcc -O3 -march=native -ffp-contract=off -fopenmp",
                          "sample": "each step: whole layers (qkv 12288x4096, o 4096x4096, gate+up 22016x4096, "
                                    "down 4096x11008 GEMVs, batch 1) repeated for ~1 s, generic-C Q2_KxQ8_K "
-                                   "dot, OpenMP rows"},
+                                   "dot, OpenMP rows; random Q2_K blocks of the same shapes (the dot's work "
+                                   "does not depend on the values)"},
         "e2e": {"value": value, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -554,22 +868,27 @@ def run_ours(args):
     elif gemvs:
         roofline = gemv_roofline(gemvs, stream, dev, peak, peak_kind)
 
-    # ---- CPU baseline (rank 0, one GPU only)
+    # ---- CPU baseline (rank 0, one GPU only): one thread and every host
+    # thread, the oracle built with -march=native on this host
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        threads = os.cpu_count() or 1
-        sample = CpuLayerSample(4096, 11008, threads)
-        sample.run_once()
-        gbs, per_layer, reps = sample.timed(args.cpu_seconds)
-        cpu = {"value": gbs, "unit": "GB/s", "cores": threads, "kind": "port",
-               "sample": f"{reps} x one full decode layer (qkv, o, gate+up, down GEMVs, batch 1) through the "
-                         f"oracle's generic-C Q2_KxQ8_K dot, {per_layer * 1e3:.1f} ms per layer"}
+        sample = CpuLayerSample(4096, 11008, 1)
+        cpu = cpu_baseline_pair(lambda n: sample.run_once(n), args.cpu_seconds / 2,
+                                lambda sec: sample.layer_bytes / sec / 1e9, "GB/s",
+                                "whole decode layers (qkv 12288x4096, o 4096x4096, gate+up 22016x4096, down "
+                                "4096x11008 GEMVs, batch 1) repeated for the sample time through the oracle's "
+                                "generic-C Q2_KxQ8_K dot; random Q2_K blocks of the same shapes (the dot's work "
+                                "does not depend on the values)")
+    configs = None
+    if rank == 0 and world == 1 and args.workload == "decode" and not args.no_configs:
+        configs = run_configs(dev, stream, args, peak, peak_kind)
 
     if rank == 0:
         line = {
             "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
-            "scaling": "strong", "vs_baseline": None, "dtype": "int8xu2", "data": "synthetic",
+            "scaling": "strong" if args.workload == "decode" else "weak",
+            "vs_baseline": None, "dtype": "int8xu2", "data": "synthetic",
             "tokens_per_s": (1e3 / ms) if args.workload == "decode" else
             ((args.prefill_tokens * 1e3 / ms) if args.workload == "prefill" else None),
             "pct_of_hbm_peak": value / (peak * world) * 100,
@@ -577,7 +896,8 @@ def run_ours(args):
                        "global_batch": args.prefill_tokens if args.workload == "prefill" else 1, "seq_len": 1,
                        "parallelism": (f"row-shard tp{world}, " + ("all-gather fused into each GEMV (NVLink "
                                        "peer stores + signals)" if stack.quant == "peer" else "NCCL all-gather")
-                                       if args.workload == "decode" else f"row-shard tp{world}")
+                                       if args.workload == "decode" else
+                                       f"{world} independent replicas (each GPU runs the whole workload)")
                        if world > 1 else "single GPU",
                        "l2": "inputs larger than L2 (2.17 GB of weights per step)" if args.workload == "decode"
                        else "inputs larger than L2 (rotating distinct weight copies)",
@@ -592,6 +912,8 @@ def run_ours(args):
             "roofline": roofline,
             "cpu_baseline": cpu,
         }
+        if configs:
+            line["configs"] = configs
         print(json.dumps(line), flush=True)
     if graph is not None:
         del graph

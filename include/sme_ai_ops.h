@@ -285,7 +285,10 @@ sme_ai_status sme_ai_self_attention_core_f32_device(const float *q, const float 
  * calls share the one array: calls whose work overlaps on the GPU (different
  * streams, or different host threads on one device) race on it and must be
  * serialized by the caller.  Nothing in the array needs to start at zero:
- * each call writes every hidden value before reading it. */
+ * each call writes every hidden value before reading it.  The looked-up
+ * address is kept for the life of the process: after a cudaDeviceReset the
+ * library's module (and the array with it) is loaded anew, so this entry
+ * point must not be called on a device that was reset after its first call. */
 sme_ai_status sme_ai_swiglu_packed_f16f32_noalloc(const sme_ai_fp16 *input, uint64_t batch,
                                                   const sme_ai_packed_linear_weight *gate_weight,
                                                   const float *gate_bias,

@@ -68,6 +68,18 @@ int smeai_device_ready(void);
 /* Text of the last error raised on the calling thread ("" if none). */
 const char *smeai_last_error(void);
 
+/* Limits of the kernels' bounded waits for kernels launched after this call:
+ * local_ns for waits on this GPU's own work (default 2 s), peer_ns for waits
+ * on rows other GPUs store (default 10 s); 0 keeps the default.  Production
+ * code leaves the defaults; tests shorten a limit to make a wait run out
+ * (a kernel captured in a CUDA graph keeps the limits of its capture). */
+void smeai_set_wait_timeouts(uint64_t local_ns, uint64_t peer_ns);
+
+/* Test hook: the library's next n device allocations fail as cudaMalloc does
+ * when the device is out of memory (the entry points then return
+ * SME_AI_ALLOC_FAILED / -2).  0 turns it off. */
+void smeai_debug_fail_next_allocs(int n);
+
 /* Reads and clears the current device's error word.  Kernels never trap or
  * spin forever: a wait that exceeds its time bound sets bit 0 (timeout) here
  * and the kernel returns early, leaving its outputs incomplete.  Returns 0,
@@ -90,6 +102,11 @@ int smeai_q8k_quantize(const float *x_dev, int64_t ld_x, int64_t n_cols, int64_t
  * (sme_ai_library/src/sme_ai_ops.c:1060-1092), fused into one kernel. */
 int smeai_rms_q8k_quantize(const float *x_dev, int64_t ld_x, int64_t n_cols, int64_t k, float eps,
                            void *y_q8k_dev, void *stream);
+/* The same with the RMSNorm weight of the reference's sme_ai_rmsnorm_f32
+ * (sme_ai_ops.c:1084-1086): x * inv_rms, then times weight[j] (k floats on the
+ * device; NULL = none), each product rounded once, then Q8_K. */
+int smeai_rms_q8k_quantize_w(const float *x_dev, int64_t ld_x, int64_t n_cols, int64_t k, const float *weight_dev,
+                             float eps, void *y_q8k_dev, void *stream);
 
 /* y[c*ldy + r] = sum_k W[r,k] * X[c,k]  for r < n_rows, c < n_cols: the
  * result of ggml's mul_mat for a Q2_K src0 and Q8_K-quantized src1 (dst
@@ -114,6 +131,10 @@ int smeai_q2k_mul_mat_tc(const void *w_dev, const void *x_q8k_dev, int64_t n_col
 #define SMEAI_EPI_SILU_MUL 2
 int smeai_q2k_mul_mat_ex(const void *w_dev, const void *x_q8k_dev, int64_t n_cols, float *y_dev, size_t ldy,
                          int epilogue, const float *resid_dev, size_t ld_resid, void *stream);
+/* The same epilogues on the tensor-core GEMM (any n_cols >= 1; the prefill
+ * path): bit-identical to smeai_q2k_mul_mat_ex on the same inputs. */
+int smeai_q2k_mul_mat_tc_ex(const void *w_dev, const void *x_q8k_dev, int64_t n_cols, float *y_dev, size_t ldy,
+                            int epilogue, const float *resid_dev, size_t ld_resid, void *stream);
 
 /* ---- decode program: a chain of dependent GEMVs as ONE persistent kernel ----
  * Phase p reads the complete output of phase p-1 (its input buffer is, or
@@ -139,6 +160,7 @@ typedef struct smeai_q2k_phase {
   int epilogue;        /* SMEAI_EPI_* */
   const float *resid;  /* SMEAI_EPI_RESIDUAL; may alias y */
   size_t ld_resid;
+  const float *norm_w; /* SMEAI_IN_F32_RMS: RMSNorm weight (k floats), or NULL */
 } smeai_q2k_phase;
 int smeai_q2k_program_create(const smeai_q2k_phase *phases, int n_phases, int64_t n_cols, float rms_eps,
                              void **prog_out);
@@ -157,6 +179,12 @@ int smeai_q2k_mul_mat_f32(const void *w_dev, const float *x_dev, int64_t n_cols,
 int smeai_q2k_mul_mat_f32_ex(const void *w_dev, const float *x_dev, size_t ld_x, int64_t n_cols, float *y_dev,
                              size_t ldy, int epilogue, const float *resid_dev, size_t ld_resid, float rms_eps,
                              void *stream);
+/* The same with an RMSNorm weight (k floats on the device, NULL = none; needs
+ * rms_eps >= 0): bit-identical to smeai_rms_q8k_quantize_w followed by
+ * smeai_q2k_mul_mat_ex. */
+int smeai_q2k_mul_mat_f32_norm(const void *w_dev, const float *x_dev, size_t ld_x, int64_t n_cols, float *y_dev,
+                               size_t ldy, int epilogue, const float *resid_dev, size_t ld_resid, float rms_eps,
+                               const float *norm_w_dev, void *stream);
 
 /* Row-sharded GEMV with its all-gather fused in (multi-GPU decode, one process
  * per GPU).  Each rank holds a row shard of W; this call computes the shard's
@@ -183,7 +211,7 @@ typedef struct {
 } smeai_peer_exchange;
 int smeai_q2k_mul_mat_f32_peer(const void *w_dev, const float *x_dev, size_t ld_x, int64_t n_cols, float *y_dev,
                                size_t ldy, int epilogue, const float *resid_dev, size_t ld_resid, float rms_eps,
-                               const smeai_peer_exchange *ex, void *stream);
+                               const float *norm_w_dev, const smeai_peer_exchange *ex, void *stream);
 /* End of a step: wait (bounded) until *sig reaches (*epoch + 1) * count, then
  * advance *epoch (queued on stream; one thread). */
 int smeai_peer_step_end(const unsigned *sig, unsigned count, unsigned *epoch, void *stream);

@@ -33,7 +33,21 @@ COMBINE_FUSED, COMBINE_SEPARATE = 0, 1
 Q3K_GGML, Q3K_BLOCK_ORDER = 0, 1
 ACT_NONE, ACT_RELU, ACT_GELU, ACT_SILU = 0, 1, 2, 3
 
-_lib = None
+NATIVE_PATH = os.path.join(HERE, "_build", "native", "libsmeai_oracle.so")
+NATIVE_CPU = os.path.join(HERE, "_build", "native", "cpu.txt")
+
+_libs = {}
+_native = False
+
+
+def cpu_model() -> str:
+    try:
+        for line in open("/proc/cpuinfo"):
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
 
 
 def build() -> str:
@@ -44,12 +58,39 @@ def build() -> str:
     return LIB_PATH
 
 
+def build_native() -> str:
+    """The CPU-baseline copy compiled with -march=native on THIS host (rebuilt
+    when the source changed or the host's CPU model differs from the one it
+    was built on)."""
+    src = os.path.join(HERE, "smeai_oracle.c")
+    model = cpu_model()
+    stale = (not os.path.exists(NATIVE_PATH)) or os.path.getmtime(NATIVE_PATH) < os.path.getmtime(src)
+    try:
+        stale = stale or open(NATIVE_CPU).read().strip() != model
+    except OSError:
+        stale = True
+    if stale:
+        subprocess.run(["make", "-C", HERE, "-s", "native"], check=True)
+        with open(NATIVE_CPU, "w") as f:
+            f.write(model + "\n")
+    return NATIVE_PATH
+
+
+def select(native: bool) -> None:
+    """Route the wrappers below to the -march=native build (the CPU baseline)
+    or to the portable build (the tests)."""
+    global _native
+    if native:
+        build_native()
+    _native = bool(native)
+
+
 def lib() -> ctypes.CDLL:
-    global _lib
-    if _lib is None:
-        if not os.path.exists(LIB_PATH):
-            build()
-        L = ctypes.CDLL(LIB_PATH)
+    path = NATIVE_PATH if _native else LIB_PATH
+    if path not in _libs:
+        if not os.path.exists(path):
+            build_native() if _native else build()
+        L = ctypes.CDLL(path)
         P, U64, I64, I = ctypes.c_void_p, ctypes.c_uint64, ctypes.c_int64, ctypes.c_int
         F = ctypes.c_float
         sig = {
@@ -79,14 +120,15 @@ def lib() -> ctypes.CDLL:
             "orc_rms_inv": (F, [P, I64, F]),
             "orc_rms_sumsq": (F, [P, I64]),
             "orc_rmsnorm_quantize_q8_K": (None, [P, P, I64, F, I]),
+            "orc_rmsnorm_w_quantize_q8_K": (None, [P, P, P, I64, F, I]),
             "orc_silu_mul": (None, [P, P, P, I64]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(L, name)
             fn.restype = res
             fn.argtypes = args
-        _lib = L
-    return _lib
+        _libs[path] = L
+    return _libs[path]
 
 
 def _p(a: np.ndarray):
@@ -301,10 +343,16 @@ def rms_sumsq(x):
     return lib().orc_rms_sumsq(_p(x), x.size)
 
 
-def rmsnorm_quantize_q8_K(x, eps, rounding=ROUND_FUSED):
+def rmsnorm_quantize_q8_K(x, eps, rounding=ROUND_FUSED, weight=None):
+    """RMSNorm (times `weight` when given: sme_ai_rmsnorm_f32's weight operand), then Q8_K."""
     x = np.ascontiguousarray(x, np.float32)
     out = np.zeros(x.size // QK_K, BLOCK_Q8_K)
-    lib().orc_rmsnorm_quantize_q8_K(_p(x), _p(out), x.size, eps, rounding)
+    if weight is None:
+        lib().orc_rmsnorm_quantize_q8_K(_p(x), _p(out), x.size, eps, rounding)
+    else:
+        weight = np.ascontiguousarray(weight, np.float32)
+        assert weight.size == x.size
+        lib().orc_rmsnorm_w_quantize_q8_K(_p(x), _p(weight), _p(out), x.size, eps, rounding)
     return out
 
 

@@ -862,12 +862,22 @@ float orc_rms_inv(const float *x, int64_t k, float eps) {
     return 1.0f / sqrtf(mean + eps);
 }
 
-void orc_rmsnorm_quantize_q8_K(const float *x, orc_block_q8_K *y, int64_t k, float eps, int rounding) {
+/* With the reference's weight operand (sme_ai_ops.c:1084-1086): y = x * inv,
+ * then y * weight[j] -- two multiplies, each rounded; weight NULL = none. */
+void orc_rmsnorm_w_quantize_q8_K(const float *x, const float *weight, orc_block_q8_K *y, int64_t k, float eps,
+                                 int rounding) {
     float inv = orc_rms_inv(x, k, eps);
     float *tmp = (float *) malloc((size_t) k * sizeof(float));
-    for (int64_t i = 0; i < k; ++i) tmp[i] = x[i] * inv;
+    for (int64_t i = 0; i < k; ++i) {
+        tmp[i] = x[i] * inv;
+        if (weight) tmp[i] = tmp[i] * weight[i];
+    }
     orc_quantize_row_q8_K(tmp, y, k, rounding);
     free(tmp);
+}
+
+void orc_rmsnorm_quantize_q8_K(const float *x, orc_block_q8_K *y, int64_t k, float eps, int rounding) {
+    orc_rmsnorm_w_quantize_q8_K(x, NULL, y, k, eps, rounding);
 }
 
 /* h = silu(g) * u with silu(g) = g / (1 + expf(-g)), sme_ai_ops.c:879-887

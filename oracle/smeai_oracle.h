@@ -147,6 +147,8 @@ float orc_rms_group_sumsq(const float *x);      /* one 32-value group */
 float orc_rms_sumsq(const float *x, int64_t k);  /* k a multiple of 32 */
 float orc_rms_inv(const float *x, int64_t k, float eps);
 void orc_rmsnorm_quantize_q8_K(const float *x, orc_block_q8_K *y, int64_t k, float eps, int rounding);
+void orc_rmsnorm_w_quantize_q8_K(const float *x, const float *weight, orc_block_q8_K *y, int64_t k, float eps,
+                                 int rounding);
 void orc_silu_mul(const float *g, const float *u, float *h, int64_t n);
 
 #ifdef __cplusplus

@@ -84,12 +84,13 @@ int gemm_scratch(cudaStream_t s, size_t bytes, void** out) {
 // Activation rows at which mul_mat switches from the GEMV to the tensor cores.
 constexpr int64_t kGemmMinCols = 16;
 
-int mul_mat_tc(const Q2KWeight& w, const void* xq, int64_t n_cols, float* y, int64_t ldy, cudaStream_t s) {
+int mul_mat_tc(const Q2KWeight& w, const void* xq, int64_t n_cols, float* y, int64_t ldy, cudaStream_t s,
+               int epi = kEpiStore, const float* resid = nullptr, int64_t ld_resid = 0) {
   const size_t need = q2k_gemm_scratch_bytes(n_cols, w.nb);
   void* scratch = nullptr;
   const int st = gemm_scratch(s, need, &scratch);
   if (st) return st;
-  return q2k_gemm_tc(w, xq, n_cols, y, ldy, scratch, need, s);
+  return q2k_gemm_tc(w, xq, n_cols, y, ldy, scratch, need, s, epi, resid, ld_resid);
 }
 
 }  // namespace
@@ -107,6 +108,10 @@ int smeai_take_device_error(unsigned* code) {
   }
   return device_error_take(code);
 }
+
+void smeai_set_wait_timeouts(uint64_t local_ns, uint64_t peer_ns) { set_wait_timeouts(local_ns, peer_ns); }
+
+void smeai_debug_fail_next_allocs(int n) { fail_next_allocs(n); }
 
 // ---- ggml-shaped entry points ------------------------------------------------
 
@@ -237,6 +242,15 @@ int smeai_rms_q8k_quantize(const float* x_dev, int64_t ld_x, int64_t n_cols, int
   return rms_q8k_quantize(x_dev, ld_x, n_cols, k, eps, y_q8k_dev, as_stream(stream));
 }
 
+int smeai_rms_q8k_quantize_w(const float* x_dev, int64_t ld_x, int64_t n_cols, int64_t k, const float* weight_dev,
+                             float eps, void* y_q8k_dev, void* stream) {
+  if (!x_dev || !y_q8k_dev) {
+    set_last_error("smeai_rms_q8k_quantize_w: NULL pointer");
+    return kBadArgument;
+  }
+  return rms_q8k_quantize(x_dev, ld_x, n_cols, k, eps, y_q8k_dev, as_stream(stream), weight_dev);
+}
+
 int smeai_q2k_mul_mat(const void* w_dev, int64_t n_rows, int64_t k, const void* x_q8k_dev, int64_t n_cols,
                       float* y_dev, size_t ldy, void* stream) {
   const Handle* h = as_fmt(w_dev, kFmtQ2K, "smeai_q2k_mul_mat");
@@ -255,6 +269,14 @@ int smeai_q2k_mul_mat_tc(const void* w_dev, const void* x_q8k_dev, int64_t n_col
   const Handle* h = as_fmt(w_dev, kFmtQ2K, "smeai_q2k_mul_mat_tc");
   if (!h) return kBadArgument;
   return mul_mat_tc(h->w, x_q8k_dev, n_cols, y_dev, (int64_t)ldy, as_stream(stream));
+}
+
+int smeai_q2k_mul_mat_tc_ex(const void* w_dev, const void* x_q8k_dev, int64_t n_cols, float* y_dev, size_t ldy,
+                            int epilogue, const float* resid_dev, size_t ld_resid, void* stream) {
+  const Handle* h = as_fmt(w_dev, kFmtQ2K, "smeai_q2k_mul_mat_tc_ex");
+  if (!h) return kBadArgument;
+  return mul_mat_tc(h->w, x_q8k_dev, n_cols, y_dev, (int64_t)ldy, as_stream(stream), epilogue, resid_dev,
+                    (int64_t)ld_resid);
 }
 
 int smeai_q2k_mul_mat_ex(const void* w_dev, const void* x_q8k_dev, int64_t n_cols, float* y_dev, size_t ldy,
@@ -286,6 +308,7 @@ int smeai_q2k_program_create(const smeai_q2k_phase* phases, int n_phases, int64_
     d.epi = phases[p].epilogue;
     d.resid = phases[p].resid;
     d.ld_resid = (int64_t)phases[p].ld_resid;
+    d.norm_w = phases[p].norm_w;
   }
   Q2KProgram* pr = nullptr;
   const int st = q2k_program_create(ph.data(), n_phases, (int)n_cols, rms_eps, &pr);
@@ -314,15 +337,26 @@ int smeai_q2k_mul_mat_f32(const void* w_dev, const float* x_dev, int64_t n_cols,
 int smeai_q2k_mul_mat_f32_ex(const void* w_dev, const float* x_dev, size_t ld_x, int64_t n_cols, float* y_dev,
                              size_t ldy, int epilogue, const float* resid_dev, size_t ld_resid, float rms_eps,
                              void* stream) {
-  const Handle* h = as_fmt(w_dev, kFmtQ2K, "smeai_q2k_mul_mat_f32_ex");
+  return smeai_q2k_mul_mat_f32_norm(w_dev, x_dev, ld_x, n_cols, y_dev, ldy, epilogue, resid_dev, ld_resid, rms_eps,
+                                    nullptr, stream);
+}
+
+int smeai_q2k_mul_mat_f32_norm(const void* w_dev, const float* x_dev, size_t ld_x, int64_t n_cols, float* y_dev,
+                               size_t ldy, int epilogue, const float* resid_dev, size_t ld_resid, float rms_eps,
+                               const float* norm_w_dev, void* stream) {
+  const Handle* h = as_fmt(w_dev, kFmtQ2K, "smeai_q2k_mul_mat_f32_norm");
   if (!h) return kBadArgument;
+  if (norm_w_dev && rms_eps < 0.f) {
+    set_last_error("smeai_q2k_mul_mat_f32_norm: an RMSNorm weight needs rms_eps >= 0");
+    return kBadArgument;
+  }
   return q2k_gemv_any(h->w, rms_eps >= 0.f ? kInF32Rms : kInF32, x_dev, (int64_t)ld_x, rms_eps, n_cols, y_dev,
-                      (int64_t)ldy, epilogue, resid_dev, (int64_t)ld_resid, as_stream(stream));
+                      (int64_t)ldy, epilogue, resid_dev, (int64_t)ld_resid, as_stream(stream), nullptr, norm_w_dev);
 }
 
 int smeai_q2k_mul_mat_f32_peer(const void* w_dev, const float* x_dev, size_t ld_x, int64_t n_cols, float* y_dev,
                                size_t ldy, int epilogue, const float* resid_dev, size_t ld_resid, float rms_eps,
-                               const smeai_peer_exchange* ex, void* stream) {
+                               const float* norm_w_dev, const smeai_peer_exchange* ex, void* stream) {
   const Handle* h = as_fmt(w_dev, kFmtQ2K, "smeai_q2k_mul_mat_f32_peer");
   if (!h) return kBadArgument;
   if (!ex) {
@@ -344,7 +378,7 @@ int smeai_q2k_mul_mat_f32_peer(const void* w_dev, const float* x_dev, size_t ld_
   e.wait_count = ex->wait_count;
   e.epoch = ex->epoch;
   return q2k_gemv_any(h->w, rms_eps >= 0.f ? kInF32Rms : kInF32, x_dev, (int64_t)ld_x, rms_eps, n_cols, y_dev,
-                      (int64_t)ldy, epilogue, resid_dev, (int64_t)ld_resid, as_stream(stream), &e);
+                      (int64_t)ldy, epilogue, resid_dev, (int64_t)ld_resid, as_stream(stream), &e, norm_w_dev);
 }
 
 int smeai_peer_step_end(const unsigned* sig, unsigned count, unsigned* epoch, void* stream) {
@@ -358,7 +392,7 @@ int smeai_ipc_alloc(size_t bytes, void** ptr, void* handle64) {
   }
   static_assert(sizeof(cudaIpcMemHandle_t) == 64, "CUDA IPC handles are 64 bytes");
   void* p = nullptr;
-  if (cudaMalloc(&p, bytes) != cudaSuccess) {
+  if (device_malloc((void**)&p, bytes) != cudaSuccess) {
     cudaGetLastError();
     set_last_error("smeai_ipc_alloc: cudaMalloc of %zu bytes failed", bytes);
     return kAllocFailed;

@@ -262,7 +262,10 @@ void ew_act(float* data, uint64_t count, int act) {
 // (524288 fp16 values = 1 MiB).  Every GPU that loads the library holds the
 // array until the process exits.  In host code `g_noalloc_hidden` is only a
 // stand-in symbol, not a device address: the address is fetched once per
-// device with cudaGetSymbolAddress and passed to the kernels.
+// device with cudaGetSymbolAddress and passed to the kernels.  The cached
+// address is never looked up again, so it is valid only while the context it
+// came from lives (a cudaDeviceReset loads the module anew; the public header
+// says the entry point must not be used on a device reset after its first call).
 constexpr uint64_t kNoAllocHiddenElems = 512u * 1024u;
 static __device__ __align__(256) __half g_noalloc_hidden[kNoAllocHiddenElems];
 
@@ -318,10 +321,10 @@ sme_ai_status sme_ai_workspace_init(sme_ai_workspace* ws, uint64_t max_batch, ui
   ws->a_pairs = reinterpret_cast<float*>(p);
   const uint64_t hid = max_batch * max_out_features;
   bool ok = cudaStreamCreateWithFlags(&p->stream, cudaStreamNonBlocking) == cudaSuccess;
-  ok = ok && cudaMalloc(&ws->tmp_f32, hid * 4) == cudaSuccess;
-  ok = ok && cudaMalloc(&ws->tmp2_f32, hid * 4) == cudaSuccess;
-  ok = ok && cudaMalloc(&ws->tmp_f16, hid * 2) == cudaSuccess;
-  ok = ok && cudaMalloc(&ws->b_pack, ws->max_k_pad * ws->max_n_pad * 2) == cudaSuccess;
+  ok = ok && device_malloc((void**)&ws->tmp_f32, hid * 4) == cudaSuccess;
+  ok = ok && device_malloc((void**)&ws->tmp2_f32, hid * 4) == cudaSuccess;
+  ok = ok && device_malloc((void**)&ws->tmp_f16, hid * 2) == cudaSuccess;
+  ok = ok && device_malloc((void**)&ws->b_pack, ws->max_k_pad * ws->max_n_pad * 2) == cudaSuccess;
   if (!ok) {
     cudaGetLastError();
     sme_ai_workspace_destroy(ws);
@@ -359,7 +362,7 @@ static sme_ai_status packed_init(sme_ai_packed_linear_weight* packed, const void
   p->is_f32 = f32 ? 1 : 0;
   p->ldb = (int64_t)packed->n_pad;
   const size_t esz = f32 ? 4 : 2;
-  if (cudaMalloc(&p->dev, packed->k_pad * packed->n_pad * esz) != cudaSuccess) {
+  if (device_malloc((void**)&p->dev, packed->k_pad * packed->n_pad * esz) != cudaSuccess) {
     cudaGetLastError();
     delete p;
     return SME_AI_ALLOC_FAILED;

@@ -40,6 +40,18 @@ const char* last_error();
     }                                                                          \
   } while (0)
 
+// Limits of the kernels' bounded waits, read when a kernel is launched and
+// passed to it as a parameter.  Waits on this GPU's own work (mbarriers,
+// counters of the running grid) default to 2 s; waits on another GPU's rows
+// default to 10 s.  set_wait_timeouts(local, peer) overrides them for later
+// launches (0 keeps the default): tests use a short limit to make a wait run
+// out on purpose.
+constexpr uint64_t kDefaultWaitNs = 2000000000ull;
+constexpr uint64_t kDefaultPeerWaitNs = 10000000000ull;
+void set_wait_timeouts(uint64_t local_ns, uint64_t peer_ns);
+uint64_t wait_timeout_ns();
+uint64_t peer_wait_timeout_ns();
+
 // True when programmatic dependent launch is enabled (default on; the
 // environment variable SMEAI_PDL=0 turns it off for A/B timing).
 bool pdl_enabled();
@@ -165,6 +177,20 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, unsigned parity
   for (;;) {
     for (int i = 0; i < 64; ++i)
       if (mbar_try_wait(bar, parity)) return true;
+    if (global_timer_ns() - t0 > timeout_ns) return false;
+  }
+}
+// The same, also giving up as soon as the device error word is set: a
+// producer whose consumers left early (a wait of theirs gave up) stops
+// instead of waiting out its own limit for slots nobody will free.
+__device__ __forceinline__ bool mbar_wait_or_error(uint64_t* bar, unsigned parity, uint64_t timeout_ns,
+                                                   const unsigned* err) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = global_timer_ns();
+  for (;;) {
+    for (int i = 0; i < 64; ++i)
+      if (mbar_try_wait(bar, parity)) return true;
+    if (*reinterpret_cast<const volatile unsigned*>(err)) return false;
     if (global_timer_ns() - t0 > timeout_ns) return false;
   }
 }

@@ -9,8 +9,10 @@ namespace smeai {
 
 // ---- Q8_K activation quantizer (q8k_quant.cu) ----
 int q8k_quantize(const float* x, int64_t ld_x, int64_t n_rows, int64_t k, void* y, cudaStream_t stream);
+// RMSNorm of each row (times norm_w[k] when norm_w is not null, the
+// reference's weight operand), then Q8_K.
 int rms_q8k_quantize(const float* x, int64_t ld_x, int64_t n_rows, int64_t k, float eps, void* y,
-                     cudaStream_t stream);
+                     cudaStream_t stream, const float* norm_w = nullptr);
 
 // ---- Q2_K weight quantizer / decoder (q2k_quant.cu) ----
 int q2k_quantize(const float* x, int64_t k_total, void* y, cudaStream_t stream);
@@ -94,9 +96,10 @@ struct PeerExchange {
   const unsigned* epoch = nullptr;
 };
 
+// norm_w: the RMSNorm weight of a kInF32Rms input (null: none).
 int q2k_gemv_any(const Q2KWeight& w, int in_mode, const void* x, int64_t ld_x, float eps, int64_t n_cols,
                  float* y, int64_t ldy, int epilogue, const float* resid, int64_t ld_resid, cudaStream_t stream,
-                 const PeerExchange* ex = nullptr);
+                 const PeerExchange* ex = nullptr, const float* norm_w = nullptr);
 // End of a step on one rank: wait (bounded) until *sig reaches
 // (*epoch + 1) * count, then advance *epoch.
 int peer_step_end(const unsigned* sig, unsigned count, unsigned* epoch, cudaStream_t stream);
@@ -119,6 +122,7 @@ struct ProgPhase {
   int epi = kEpiStore;
   const float* resid = nullptr;
   int64_t ld_resid = 0;
+  const float* norm_w = nullptr;  // RMSNorm weight of a kInF32Rms input (null: none)
 };
 struct Q2KProgram;
 int q2k_program_create(const ProgPhase* phases, int n_phases, int n_cols, float rms_eps, Q2KProgram** out);
@@ -131,8 +135,12 @@ void q2k_program_shape(const Q2KProgram* prog, int* grid, int* consumers, int* s
 // Q8_K rows, store epilogue, bit-identical to q2k_gemv.  Needs a 256-byte
 // aligned scratch of q2k_gemm_scratch_bytes(n_cols, nb) bytes.
 size_t q2k_gemm_scratch_bytes(int64_t n_cols, int nb);
+// epi: kEpiStore, kEpiResidual (y = resid + W x; resid may alias y) or
+// kEpiSiluMul (rows interleave gate/up; y gets n_rows / 2 values per token),
+// the arithmetic of the GEMV's epilogues.
 int q2k_gemm_tc(const Q2KWeight& w, const void* xq, int64_t n_cols, float* y, int64_t ldy, void* scratch,
-                size_t scratch_bytes, cudaStream_t stream);
+                size_t scratch_bytes, cudaStream_t stream, int epi = kEpiStore, const float* resid = nullptr,
+                int64_t ld_resid = 0);
 
 // Per-(row, super-block) integer sums (isum, summs), [n_rows][nb] each, for a
 // single activation row -- the exactness check of the GEMV's integer core.

@@ -67,6 +67,9 @@ struct GemmParams {
   int64_t n_cols;
   float* y;
   int64_t ldy;
+  int epi;                // kEpiStore, kEpiResidual (y = resid + acc), kEpiSiluMul (interleaved gate/up rows)
+  const float* resid;
+  int64_t ld_resid;
   unsigned* err;
 };
 
@@ -522,12 +525,28 @@ __global__ void __launch_bounds__(kThreads, 1) q2k_gemm_tc_kernel(const GemmPara
       tc_fence_before();
       mbar_arrive(&m.aempty[r]);
     }
-    if (ok && row < p.n_rows) {
+    if (ok && p.epi == kEpiSiluMul) {
+      // rows 2i (gate) and 2i+1 (up) sit in adjacent lanes: the even lane
+      // writes h_i = silu(gate) * up, the arithmetic of the GEMV's epilogue
+#pragma unroll 4
+      for (int c = 0; c < 64; ++c) {
+        const int64_t tok = m0 + half * 64 + c;
+        const float gsum = __uint_as_float((uint32_t)(acc[c >> 1] >> (32 * (c & 1))));
+        const float usum = __shfl_down_sync(0xffffffffu, gsum, 1);
+        if (!(lane & 1) && row + 1 < p.n_rows && tok < p.n_cols) {
+          const float sg = __fdiv_rn(gsum, __fadd_rn(1.0f, expf(-gsum)));
+          p.y[tok * p.ldy + (row >> 1)] = __fmul_rn(sg, usum);
+        }
+      }
+    } else if (ok && row < p.n_rows) {
 #pragma unroll
       for (int c = 0; c < 64; ++c) {
         const int64_t tok = m0 + half * 64 + c;
-        const uint32_t bits = (uint32_t)(acc[c >> 1] >> (32 * (c & 1)));
-        if (tok < p.n_cols) p.y[tok * p.ldy + row] = __uint_as_float(bits);
+        float v = __uint_as_float((uint32_t)(acc[c >> 1] >> (32 * (c & 1))));
+        if (tok < p.n_cols) {
+          if (p.epi == kEpiResidual) v = __fadd_rn(p.resid[tok * p.ld_resid + row], v);
+          p.y[tok * p.ldy + row] = v;
+        }
       }
     }
   }
@@ -577,9 +596,16 @@ size_t q2k_gemm_scratch_bytes(int64_t n_cols, int nb) {
 }
 
 int q2k_gemm_tc(const Q2KWeight& w, const void* xq, int64_t n_cols, float* y, int64_t ldy, void* scratch,
-                size_t scratch_bytes, cudaStream_t stream) {
-  if (!w.tiles || !xq || !y || n_cols <= 0 || ldy < w.n_rows || w.fmt != kFmtQ2K) {
+                size_t scratch_bytes, cudaStream_t stream, int epi, const float* resid, int64_t ld_resid) {
+  const int64_t out_rows = epi == kEpiSiluMul ? w.n_rows / 2 : w.n_rows;
+  if (!w.tiles || !xq || !y || n_cols <= 0 || ldy < out_rows || w.fmt != kFmtQ2K) {
     set_last_error("q2k_gemm_tc: bad arguments (a Q2_K weight is required)");
+    return kBadArgument;
+  }
+  if ((epi != kEpiStore && epi != kEpiResidual && epi != kEpiSiluMul) ||
+      (epi == kEpiResidual && (!resid || ld_resid < out_rows)) || (epi == kEpiSiluMul && (w.n_rows & 1))) {
+    set_last_error("q2k_gemm_tc: bad epilogue (residual needs resid with ld_resid >= rows; silu*mul needs "
+                   "interleaved gate/up row pairs)");
     return kBadArgument;
   }
   if (reinterpret_cast<uintptr_t>(xq) & 3) {
@@ -634,6 +660,9 @@ int q2k_gemm_tc(const Q2KWeight& w, const void* xq, int64_t n_cols, float* y, in
   p.n_cols = n_cols;
   p.y = y;
   p.ldy = ldy;
+  p.epi = epi;
+  p.resid = resid;
+  p.ld_resid = ld_resid;
   p.err = err;
   const dim3 grid((unsigned)((w.n_rows + kTM - 1) / kTM), (unsigned)tiles);
   SMEAI_CUDA_TRY(launch(q2k_gemm_tc_kernel, grid, dim3(kThreads), smem, stream, p));

@@ -32,6 +32,7 @@
 //     producer first waits, bounded, for its copies in flight).
 #include "common.cuh"
 #include "kernels.h"
+#include "runtime.h"
 #include "q8k_device.cuh"
 #include "q2k_core.cuh"
 #include "q3k_core.cuh"
@@ -47,8 +48,6 @@ namespace {
 
 constexpr int kMaxConsumers = 16;
 constexpr int kMaxThreads = (kMaxConsumers + 1) * 32;
-constexpr uint64_t kWaitTimeoutNs = 2000000000ull;  // 2 s
-constexpr uint64_t kPeerTimeoutNs = 10000000000ull; // 10 s: another GPU's step
 
 __device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
   unsigned v;
@@ -60,12 +59,17 @@ __device__ __forceinline__ uint64_t now_ns() {
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
   return t;
 }
-// Bounded wait until *sig reaches (*epoch + 1) * count (wrap-safe); false on timeout.
-__device__ bool peer_wait(const unsigned* sig, const unsigned* epoch, unsigned count) {
+// Bounded wait until *sig reaches (*epoch + 1) * count (wrap-safe); false on
+// timeout, and false at once when this device's error word is already set: a
+// step in which one wait gave up cannot complete, so every later wait of the
+// step returns immediately instead of running out its own limit.
+__device__ bool peer_wait(const unsigned* sig, const unsigned* epoch, unsigned count, const unsigned* err,
+                          uint64_t timeout_ns) {
   const unsigned target = (ld_acquire_sys(epoch) + 1u) * count;
   const uint64_t t0 = now_ns();
   while ((int)(ld_acquire_sys(sig) - target) < 0) {
-    if (now_ns() - t0 > kPeerTimeoutNs) return false;
+    if (*reinterpret_cast<const volatile unsigned*>(err)) return false;
+    if (now_ns() - t0 > timeout_ns) return false;
     __nanosleep(64);
   }
   return true;
@@ -87,6 +91,7 @@ struct GemvParams {
   const void* x;     // Q8_K blocks (kInQ8K) or fp32 rows
   int64_t ld_x;      // fp32 row stride in floats
   float eps;         // RMSNorm epsilon (kInF32Rms)
+  const float* norm_w;  // RMSNorm weight (kInF32Rms), or null
   float* y;
   int64_t ldy;
   const float* resid;
@@ -94,6 +99,8 @@ struct GemvParams {
   int32_t* isum_out;
   int32_t* summs_out;
   unsigned* err;
+  uint64_t timeout_ns;       // bounded waits on this GPU's own work
+  uint64_t peer_timeout_ns;  // bounded wait on other GPUs' rows
   int stages;        // ring depth (a power of two)
   int log2_stages;
   PeerExchange ex;   // cross-GPU output exchange (n_dst = n_sig = 0 and no wait_sig: off)
@@ -249,7 +256,7 @@ __global__ void __launch_bounds__(kMaxThreads) q2k_gemv_kernel(const GemvParams 
       bool ok = true;
       for (; i < n_stages; ++i) {
         const int s = i & smask;
-        if (i >= S && !mbar_wait_bounded(&m.empty[s], (unsigned)(((i >> lgS) - 1) & 1), kWaitTimeoutNs)) {
+        if (i >= S && !mbar_wait_or_error(&m.empty[s], (unsigned)(((i >> lgS) - 1) & 1), p.timeout_ns, p.err)) {
           ok = false;
           break;
         }
@@ -262,7 +269,7 @@ __global__ void __launch_bounds__(kMaxThreads) q2k_gemv_kernel(const GemvParams 
       if (!ok) {
         raise_device_error(p.err, kDevErrTimeout);
         for (int j = (i > S ? i - S : 0); j < i; ++j)
-          mbar_wait_bounded(&m.full[j & smask], (unsigned)((j >> lgS) & 1), kWaitTimeoutNs);
+          mbar_wait_bounded(&m.full[j & smask], (unsigned)((j >> lgS) & 1), p.timeout_ns);
       }
     }
     return;
@@ -275,7 +282,7 @@ __global__ void __launch_bounds__(kMaxThreads) q2k_gemv_kernel(const GemvParams 
   if (peer_in) {  // the input holds rows other GPUs store: wait for all of them
     int ok = 1;
     if (cw == 0 && lane == 0) {
-      ok = peer_wait(p.ex.wait_sig, p.ex.epoch, p.ex.wait_count) ? 1 : 0;
+      ok = peer_wait(p.ex.wait_sig, p.ex.epoch, p.ex.wait_count, p.err, p.peer_timeout_ns) ? 1 : 0;
       if (!ok) raise_device_error(p.err, kDevErrTimeout);
     }
     int all;  // the consumer warps meet (named barrier 1) and learn the waiter's result
@@ -310,7 +317,7 @@ __global__ void __launch_bounds__(kMaxThreads) q2k_gemv_kernel(const GemvParams 
       }
       mbar_arrive_warp(&m.rms[0]);
       if (cw == 0) {
-        if (!mbar_wait_bounded(&m.rms[0], 0, kWaitTimeoutNs)) {
+        if (!mbar_wait_bounded(&m.rms[0], 0, p.timeout_ns)) {
           raise_device_error(p.err, kDevErrTimeout);
           return;
         }
@@ -321,7 +328,7 @@ __global__ void __launch_bounds__(kMaxThreads) q2k_gemv_kernel(const GemvParams 
         }
         mbar_arrive_warp(&m.rms[1]);
       }
-      if (!mbar_wait_bounded(&m.rms[1], 0, kWaitTimeoutNs)) {
+      if (!mbar_wait_bounded(&m.rms[1], 0, p.timeout_ns)) {
         raise_device_error(p.err, kDevErrTimeout);
         return;
       }
@@ -336,6 +343,12 @@ __global__ void __launch_bounds__(kMaxThreads) q2k_gemv_kernel(const GemvParams 
           const float inv = m.rsum[t * (8 * nb + 1) + 8 * nb];
 #pragma unroll
           for (int k = 0; k < 8; ++k) v[k] = __fmul_rn(v[k], inv);
+          if (p.norm_w) {
+            float g[8];
+            load8(p.norm_w + b * QK_K + lane * 8, g);
+#pragma unroll
+            for (int k = 0; k < 8; ++k) v[k] = __fmul_rn(v[k], g[k]);
+          }
         }
         store_q8k_smem(q8k_quantize_lane(v), act, t * nb + b);
       }
@@ -347,7 +360,7 @@ __global__ void __launch_bounds__(kMaxThreads) q2k_gemv_kernel(const GemvParams 
   for (int j = 0; j < ng; ++j) {
     const int buf = j & 1;
     float* terms = m.terms + (size_t)buf * T * nb * 32;
-    if (!SUMS && j >= 2 && !mbar_wait_bounded(&m.tfree[buf], (unsigned)(((j >> 1) - 1) & 1), kWaitTimeoutNs)) {
+    if (!SUMS && j >= 2 && !mbar_wait_bounded(&m.tfree[buf], (unsigned)(((j >> 1) - 1) & 1), p.timeout_ns)) {
       raise_device_error(p.err, kDevErrTimeout);
       return;
     }
@@ -357,7 +370,7 @@ __global__ void __launch_bounds__(kMaxThreads) q2k_gemv_kernel(const GemvParams 
       const int i = j * nchunks + c;
       const int s = i & smask;
       const int b = c * kConsumers + cw;
-      if (!mbar_wait_bounded(&m.full[s], (unsigned)((i >> lgS) & 1), kWaitTimeoutNs)) {
+      if (!mbar_wait_bounded(&m.full[s], (unsigned)((i >> lgS) & 1), p.timeout_ns)) {
         raise_device_error(p.err, kDevErrTimeout);
         return;
       }
@@ -373,7 +386,7 @@ __global__ void __launch_bounds__(kMaxThreads) q2k_gemv_kernel(const GemvParams 
     if constexpr (!SUMS) {
       mbar_arrive_warp(&m.grp[buf]);
       if (cw == (j % kConsumers)) {
-        if (!mbar_wait_bounded(&m.grp[buf], (unsigned)((j >> 1) & 1), kWaitTimeoutNs)) {
+        if (!mbar_wait_bounded(&m.grp[buf], (unsigned)((j >> 1) & 1), p.timeout_ns)) {
           raise_device_error(p.err, kDevErrTimeout);
           return;
         }
@@ -387,7 +400,7 @@ __global__ void __launch_bounds__(kMaxThreads) q2k_gemv_kernel(const GemvParams 
     if (p.ex.n_sig) {
       mbar_arrive_warp(m.done);
       if (cw == 0 && lane == 0) {
-        if (mbar_wait_bounded(m.done, 0u, kWaitTimeoutNs)) peer_signal(p.ex, (unsigned)ng);
+        if (mbar_wait_bounded(m.done, 0u, p.timeout_ns)) peer_signal(p.ex, (unsigned)ng);
         else raise_device_error(p.err, kDevErrTimeout);
       }
     }
@@ -508,6 +521,8 @@ int launch_gemv(const Q2KWeight& w, GemvParams p, cudaStream_t stream) {
     set_last_error("q2k_gemv: device error word unavailable");
     return kCudaError;
   }
+  p.timeout_ns = wait_timeout_ns();
+  p.peer_timeout_ns = peer_wait_timeout_ns();
   const size_t smem = smem_total_bytes(T, w.nb, pl.stages, pl.consumers, F::kTile);
   static unsigned configured = 0;  // per template instance, one bit per device
   int dev = 0;
@@ -602,7 +617,7 @@ int q2k_repack(const void* w_blocks_dev, int64_t n_rows, int64_t k, Q2KWeight* o
   }
   const size_t bytes = q2k_tile_bytes(n_rows, k);
   uint8_t* tiles = nullptr;
-  if (cudaMalloc(&tiles, bytes) != cudaSuccess) {
+  if (device_malloc((void**)&tiles, bytes) != cudaSuccess) {
     cudaGetLastError();
     set_last_error("q2k_repack: cudaMalloc of %zu bytes failed", bytes);
     return kAllocFailed;
@@ -614,7 +629,7 @@ int q2k_repack(const void* w_blocks_dev, int64_t n_rows, int64_t k, Q2KWeight* o
 
 int q2k_gemv_any(const Q2KWeight& w, int in_mode, const void* x, int64_t ld_x, float eps, int64_t n_cols,
                  float* y, int64_t ldy, int epilogue, const float* resid, int64_t ld_resid, cudaStream_t stream,
-                 const PeerExchange* ex) {
+                 const PeerExchange* ex, const float* norm_w) {
   if (!w.tiles || !x || !y || n_cols <= 0) {
     set_last_error("q2k_gemv: bad arguments");
     return kBadArgument;
@@ -677,6 +692,7 @@ int q2k_gemv_any(const Q2KWeight& w, int in_mode, const void* x, int64_t ld_x, f
                             : static_cast<const void*>(static_cast<const float*>(x) + c0 * ld_x);
     p.ld_x = ld_x;
     p.eps = eps;
+    p.norm_w = in_mode == kInF32Rms ? norm_w : nullptr;
     p.y = y + c0 * ldy;
     p.ldy = ldy;
     p.resid = resid ? resid + c0 * ld_resid : nullptr;
@@ -698,8 +714,16 @@ int q2k_gemv_any(const Q2KWeight& w, int in_mode, const void* x, int64_t ld_x, f
 }
 
 namespace {
-__global__ void peer_step_end_kernel(const unsigned* sig, unsigned count, unsigned* epoch, unsigned* err) {
-  if (!peer_wait(sig, epoch, count)) raise_device_error(err, kDevErrTimeout);
+// The epoch advances only when the step completed: after a timeout the
+// error word stays set and the step counter keeps its value, so late signals
+// of the failed step can never satisfy a wait of the next one (the host must
+// see the error and rebuild the exchange before running another step).
+__global__ void peer_step_end_kernel(const unsigned* sig, unsigned count, unsigned* epoch, unsigned* err,
+                                     uint64_t timeout_ns) {
+  if (!peer_wait(sig, epoch, count, err, timeout_ns)) {
+    raise_device_error(err, kDevErrTimeout);
+    return;
+  }
   *epoch = *epoch + 1u;
 }
 }  // namespace
@@ -714,7 +738,7 @@ int peer_step_end(const unsigned* sig, unsigned count, unsigned* epoch, cudaStre
     set_last_error("peer_step_end: device error word unavailable");
     return kCudaError;
   }
-  peer_step_end_kernel<<<1, 1, 0, stream>>>(sig, count, epoch, err);
+  peer_step_end_kernel<<<1, 1, 0, stream>>>(sig, count, epoch, err, peer_wait_timeout_ns());
   SMEAI_CUDA_TRY(cudaGetLastError());
   return kOk;
 }

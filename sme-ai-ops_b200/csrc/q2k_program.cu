@@ -1,42 +1,46 @@
 // q2k_program.cu -- a decode step (a chain of dependent Q2_K GEMVs) as ONE
-// persistent cooperative kernel.
+// persistent cooperative kernel whose phases hand their activations to one
+// another through tagged words instead of grid-wide barriers.
 //
 // Batch-1 decode of a Llama-shape stack is ~129 GEMVs (qkv, o, gate/up, down
 // per layer, then lm_head), each reading the complete output of an earlier
-// one (after an RMSNorm, a silu*mul, or a plain re-quantization to Q8_K).  As
-// separate launches every link costs a grid drain, a launch and a refill of
-// the weight stream.  Here one CTA per SM runs the whole chain:
+// one (after an RMSNorm, a silu*mul, or a plain re-quantization to Q8_K).
+// One CTA per SM runs the whole chain:
 //   * warp 0, lane 0 (producer) streams this CTA's weight tiles of EVERY
 //     phase, in program order, into a shared-memory ring with cp.async.bulk.
 //     Weights do not depend on activations, so the stream runs ahead across
 //     phase boundaries as far as the ring reaches;
+//   * row groups are dealt to CTAs round-robin (CTA c takes groups c, c + C,
+//     c + 2C, ...), so a phase's outputs complete in rounds from its first
+//     rows to its last and the next phase's early input blocks are ready
+//     before the phase ends;
 //   * the consumer warps process the CTA's row groups of each phase exactly
 //     as q2k_gemv_kernel does (q2k_core.cuh: same integer core, same ordered
 //     float sum, same epilogues), so every output is bit-identical to the
 //     separate launches;
-//   * the finisher warp of each row group writes the outputs and, when a
-//     later phase reads them through an RMSNorm, the group's sum of squares
-//     (its 32 rows folded in the fixed order of the CPU restatement); the
-//     CTA's last finisher of a phase publishes its rows with one release add
-//     on the phase's completion counter;
-//   * before phase p, one lane of the CTA waits (acquire loads, bounded by
-//     wall time and by the launch's abort word) until phase p-1's counter
-//     reaches its group count, while the other warps sleep on an mbarrier;
-//     meanwhile its warp copies phase p's descriptor into shared memory, so
-//     no field is read through the (then stale) L1 on the critical path;
-//     then every warp issues one round of loads -- its own activation blocks,
-//     the producer's group sums (an RMSNorm input: each warp folds them to
-//     the same 1/rms, no cross-warp barrier), the residual of the groups it
-//     will finish -- and quantizes its blocks to Q8_K in shared memory with
-//     the standalone quantizer's helpers (same bits);
-//   * activation slots in shared memory belong to one warp in every phase, so
-//     a warp that runs ahead into the next phase cannot touch a slower warp's
-//     operands;
-//   * the last CTA to leave puts the counters back to zero for the next launch.
-// All CTAs must be resident at once for the cross-CTA waits: the launch is
-// cooperative (the runtime refuses a grid that cannot be co-resident).  Every
-// wait is bounded; on expiry the kernel records kDevErrTimeout, sets the
-// launch's abort word so the other CTAs stop waiting, and returns.
+//   * HANDOFF.  Besides the caller-visible fp32 output, every finished value
+//     is stored as one 8-byte word {value, launch tag} into a program-owned
+//     buffer of its phase (written once per launch, so no phase ever
+//     overwrites data a slower CTA still reads).  An 8-byte aligned store is
+//     single-copy atomic, so a reader that sees the current tag in a word sees
+//     that word's value: no fence, no counter.  A consumer warp polls exactly
+//     the input words it needs -- its own 256-value blocks, and for an
+//     RMSNorm input the 32-row group sums of squares the producer's finishers
+//     publish the same way -- and the load that sees the tag IS the load of
+//     the data.  A warp starts a phase as soon as its blocks exist, while
+//     other warps and CTAs may still be finishing the previous phase;
+//   * inputs written before the launch (the first phase's activations, a
+//     residual of outside data) are copied into tagged buffers by all CTAs
+//     at the start, followed by the kernel's one grid-wide barrier, so no
+//     phase can overwrite caller memory another CTA has yet to read;
+//   * the tag is the launch count + 1 (a device word advanced by CTA 0 after
+//     the barrier, when every CTA has read it), and the tagged buffers are
+//     double-buffered by the tag's parity.
+// All CTAs must be resident at once: the launch is cooperative (the runtime
+// refuses a grid that cannot be co-resident).  Every wait is bounded; on
+// expiry the kernel records kDevErrTimeout, stores the launch's tag into the
+// abort word so every other waiter of the launch gives up at once, and
+// returns (the program must then be reset before its next run).
 #include <stdio.h>
 #include <stdlib.h>
 
@@ -52,40 +56,65 @@ namespace smeai {
 
 namespace {
 
-constexpr uint64_t kTimeoutNs = 2000000000ull;  // 2 s
 constexpr int kMaxWarps = 17;                    // producer + up to 16 consumers
-constexpr uint32_t kProgramMagic = 0x51325047u;  // "Q2PG"
+constexpr uint32_t kProgramMagic = 0x51325048u;  // "Q2PH"
+constexpr uint64_t kAbortCheckNs = 20000;        // waits shorter than this never read the abort word
+// Replicas of every group-sum array: the finisher's lanes 0..kSumReps-1 each
+// store one, and a warp reads replica (cta + warp) % kSumReps, so the few
+// cache lines every warp of the grid needs for an RMSNorm are spread over
+// kSumReps places instead of one.
+constexpr int kSumReps = 16;
 
+// Descriptor of one phase.  The *_ll pointers address the tagged buffers of
+// set 0; the kernel adds the set offset of its launch.  Token t, row r of a
+// tagged buffer is word [t * ld + r].
 struct PhaseDev {
   const uint8_t* tiles;
-  const void* x;            // Q8_K rows, or fp32 rows
-  const float* x_part;      // group sums of squares of the input rows (RMS input from a phase), or null
-  float* y;
-  float* y_part;            // group sums of squares of the output (a later phase's RMS input), or null
-  const float* resid;
+  const uint8_t* xq;         // kInQ8K: Q8_K blocks (caller memory), contiguous token rows
+  const uint64_t* x_ll;      // fp32 input as tagged words
+  const uint64_t* xs_ll;     // kInF32Rms: 32-value group sums of squares of the input, tagged,
+                             // [token][replica][ld_xsll]
+  const float* norm_w;       // kInF32Rms: RMSNorm weight, or null
+  float* y;                  // caller-visible output
+  uint64_t* y_ll;            // tagged output
+  uint64_t* ys_ll;           // tagged group sums of squares of the output (a later RMS input), or null,
+                             // [token][replica][ld_ysll]
+  const uint64_t* r_ll;      // tagged residual, or null
+  int64_t ld_xll, ld_xsll, ldy, ld_yll, ld_ysll, ld_rll;
   int64_t n_rows;
   int64_t n_groups;
-  int64_t ld_x;             // token stride of x (floats)
-  int64_t ld_xpart;         // token stride of x_part
-  int64_t ldy;
-  int64_t n_part;           // token stride of y_part (32-row groups of the output)
-  int64_t ld_resid;
   int nb;
   int in_mode;
   int epi;
   int pad;
 };
 
+// Inputs written before the launch, copied into tagged buffers at its start.
+struct CopyDev {
+  const float* src;
+  int64_t ld_src;
+  uint64_t* dst;             // tagged, set 0
+  int64_t ld_dst;
+  uint64_t* sums;            // tagged group sums of squares (set 0), [token][replica][ld_sums], or null
+  int64_t ld_sums;
+  int64_t len;               // values per token
+  int64_t units;             // T * ceil(len / 32): one 32-value group of one token each
+};
+
 struct ProgParams {
   const PhaseDev* phases;
+  const CopyDev* copies;
   int n_phases;
+  int n_copies;
   int nb_max;
   float eps;
   int stages;
   int log2_stages;
-  int l2_ahead;     // ring stages prefetched into L2 ahead of the ring loads
-  unsigned* ctr;    // [0, n_phases): row groups finished; [n_phases]: CTAs done; [n_phases + 1]: abort
+  unsigned* ctl;        // [0] launches completed (the tag is ctl[0] + 1), [1] barrier arrivals, [2] abort tag
   unsigned* err;
+  uint64_t timeout_ns;  // every bounded wait
+  int64_t set_bytes;    // distance between the two sets of tagged buffers
+  int tbufs;            // row-group terms buffers: 2 (double-buffered) or 1 when two do not fit
 };
 
 struct PSmem {
@@ -93,17 +122,11 @@ struct PSmem {
   int4* qs;
   int* bs;
   float* d;
-  float* terms;
-  PhaseDev* pd;       // [2] descriptors of the CTA's current and previous phase
+  float* terms;       // [tbufs][T * nb_max][32]
   uint64_t* full;
   uint64_t* empty;
   uint64_t* grp;      // [2] all consumer warps wrote a row group's terms
   uint64_t* tfree;    // [2] the finisher has consumed them
-  uint64_t* done;
-  uint64_t* inready;  // the CTA's poller saw the previous phase complete
-  uint64_t* invready; // the poller has put 1/rms of every token in inv[]
-  unsigned* gate_fail;
-  float* inv;         // [8]
 };
 
 __host__ __device__ __forceinline__ size_t al16(size_t v) { return (v + 15) & ~(size_t)15; }
@@ -111,23 +134,23 @@ __host__ __device__ __forceinline__ size_t al16(size_t v) { return (v + 15) & ~(
 // Q8_K activation slot of warp cw's i-th super-block (b = cw + i * W) and
 // token t.  Slots belong to one warp in every phase: a warp that has moved
 // on to the next phase's prologue cannot overwrite an activation a slower
-// warp of its CTA still reads (the slot would otherwise move with k).
+// warp of its CTA still reads.
 __device__ __forceinline__ int act_slot(int cw, int W, int T, int i, int t) { return cw + W * (t + T * i); }
-// slots to allocate: W warps x T tokens x the most blocks one warp gets
 __host__ __device__ __forceinline__ size_t act_slots(int T, int nb_max, int W) {
   return (size_t)W * T * ((nb_max + W - 1) / W);
 }
 
-__host__ __device__ __forceinline__ size_t prog_fixed_bytes(int T, int nb_max, int W) {
+__host__ __device__ __forceinline__ size_t prog_fixed_bytes(int T, int nb_max, int W, int tbufs) {
   const size_t slots = act_slots(T, nb_max, W);
-  return al16(slots * 256) + al16(slots * 32) + al16(slots * 4) + al16((size_t)2 * T * nb_max * 128) +
-         al16(2 * sizeof(PhaseDev)) + 8 * 7 + 16 + 32;
+  return al16(slots * 256) + al16(slots * 32) + al16(slots * 4) + al16((size_t)tbufs * T * nb_max * 128) + 8 * 4 +
+         16;
 }
-__host__ __device__ __forceinline__ size_t prog_smem_bytes(int T, int nb_max, int stages, int consumers) {
-  return (size_t)stages * consumers * kTileBytes + prog_fixed_bytes(T, nb_max, consumers) + (size_t)stages * 16;
+__host__ __device__ __forceinline__ size_t prog_smem_bytes(int T, int nb_max, int stages, int consumers, int tbufs) {
+  return (size_t)stages * consumers * kTileBytes + prog_fixed_bytes(T, nb_max, consumers, tbufs) +
+         (size_t)stages * 16;
 }
 
-__device__ __forceinline__ PSmem pcarve(uint8_t* base, int T, int nb_max, int stages, int consumers) {
+__device__ __forceinline__ PSmem pcarve(uint8_t* base, int T, int nb_max, int stages, int consumers, int tbufs) {
   PSmem m;
   size_t o = 0;
   const size_t slots = act_slots(T, nb_max, consumers);
@@ -140,19 +163,34 @@ __device__ __forceinline__ PSmem pcarve(uint8_t* base, int T, int nb_max, int st
   m.d = reinterpret_cast<float*>(base + o);
   o += al16(slots * 4);
   m.terms = reinterpret_cast<float*>(base + o);
-  o += al16((size_t)2 * T * nb_max * 128);
-  m.pd = reinterpret_cast<PhaseDev*>(base + o);
-  o += al16(2 * sizeof(PhaseDev));
+  o += al16((size_t)tbufs * T * nb_max * 128);
   m.full = reinterpret_cast<uint64_t*>(base + o);
   m.empty = m.full + stages;
   m.grp = m.empty + stages;
   m.tfree = m.grp + 2;
-  m.done = m.tfree + 2;
-  m.inready = m.done + 1;
-  m.invready = m.inready + 1;
-  m.gate_fail = reinterpret_cast<unsigned*>(m.invready + 1);
-  m.inv = reinterpret_cast<float*>(m.gate_fail + 4);
   return m;
+}
+
+// ---- tagged words ------------------------------------------------------------
+__device__ __forceinline__ uint64_t ll_pack(float v, unsigned tag) {
+  return ((uint64_t)tag << 32) | (uint64_t)__float_as_uint(v);
+}
+__device__ __forceinline__ bool ll_has(uint64_t w, unsigned tag) { return (unsigned)(w >> 32) == tag; }
+__device__ __forceinline__ float ll_val(uint64_t w) { return __uint_as_float((unsigned)w); }
+__device__ __forceinline__ void ll_st(uint64_t* p, uint64_t w) {
+  asm volatile("st.relaxed.gpu.global.b64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+}
+__device__ __forceinline__ uint64_t ll_ld(const uint64_t* p) {
+  uint64_t w;
+  asm volatile("ld.relaxed.gpu.global.b64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
+  return w;
+}
+__device__ __forceinline__ void ll_ld2(const uint64_t* p, uint64_t& a, uint64_t& b) {
+  asm volatile("ld.relaxed.gpu.global.v2.b64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
+}
+template <typename Ptr>
+__device__ __forceinline__ Ptr set_ptr(Ptr p, int64_t off) {
+  return reinterpret_cast<Ptr>(reinterpret_cast<uintptr_t>(p) + off);
 }
 
 __device__ __forceinline__ unsigned ld_acquire_gpu(const unsigned* p) {
@@ -168,134 +206,213 @@ __device__ __forceinline__ unsigned ld_relaxed_gpu(const unsigned* p) {
 __device__ __forceinline__ void red_release_gpu_add(unsigned* p, unsigned v) {
   asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
+__device__ __forceinline__ void st_relaxed_gpu(unsigned* p, unsigned v) {
+  asm volatile("st.relaxed.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
 
-// Wait until *ctr >= target; false on timeout or when the launch is aborted.
-__device__ bool wait_count(const unsigned* ctr, unsigned target, const unsigned* abort_word) {
-  if (ld_acquire_gpu(ctr) >= target) return true;
+// Record a timeout and make every other waiter of this launch give up.
+__device__ __forceinline__ void fail(const ProgParams& P, unsigned tag) {
+  raise_device_error(P.err, kDevErrTimeout);
+  st_relaxed_gpu(P.ctl + 2, tag);
+}
+
+// mbarrier wait bounded by the time limit that also gives up at once when
+// the launch has been aborted.
+__device__ __forceinline__ bool pwait(uint64_t* bar, unsigned parity, const ProgParams& P, unsigned tag) {
+  if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = global_timer_ns();
   for (;;) {
-    for (int k = 0; k < 32; ++k)
-      if (ld_acquire_gpu(ctr) >= target) return true;
-    if (ld_relaxed_gpu(abort_word)) return false;
-    if (global_timer_ns() - t0 > kTimeoutNs) return false;
+    for (int i = 0; i < 64; ++i)
+      if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t el = global_timer_ns() - t0;
+    if (el > kAbortCheckNs && ld_relaxed_gpu(P.ctl + 2) == tag) return false;
+    if (el > P.timeout_ns) {
+      fail(P, tag);
+      return false;
+    }
   }
 }
 
-__device__ __forceinline__ void fail(const ProgParams& P) {
-  raise_device_error(P.err, kDevErrTimeout);
-  atomicExch(P.ctr + P.n_phases + 1, 1u);
+// Bounded wait state of one warp's poll loop.  The abort word and the clock
+// are read only every 8th retry, and the abort word only after the wait has
+// lasted kAbortCheckNs: every waiting warp of the grid reads the same abort
+// word, and in a healthy launch no wait lasts that long.
+struct Poll {
+  uint64_t t0 = 0;
+  int iter = 0;
+  // Called after a poll found something missing: false when the launch was
+  // aborted or the time limit ran out.
+  __device__ __forceinline__ bool again(const ProgParams& P, unsigned tag) {
+    if (iter++ == 0) t0 = global_timer_ns();
+    if ((iter & 7) == 0) {
+      const uint64_t el = global_timer_ns() - t0;
+      if (el > kAbortCheckNs && ld_relaxed_gpu(P.ctl + 2) == tag) return false;
+      if (el > P.timeout_ns) {
+        fail(P, tag);
+        return false;
+      }
+    }
+    __nanosleep(64);
+    return true;
+  }
+};
+
+// Eight consecutive tagged values of this lane (a 2 KB block per warp).
+struct LL8 {
+  uint64_t w[8];
+};
+__device__ __forceinline__ void ll_load8(const uint64_t* p, LL8& r) {
+#pragma unroll
+  for (int k = 0; k < 8; k += 2) ll_ld2(p + k, r.w[k], r.w[k + 1]);
+}
+__device__ __forceinline__ bool ll_ready8(const LL8& r, unsigned tag) {
+  bool ok = true;
+#pragma unroll
+  for (int k = 0; k < 8; ++k) ok &= ll_has(r.w[k], tag);
+  return ok;
+}
+// Wait until every word of the warp's block carries `tag` (r holds a first
+// load).  While something is missing only one word per lane is re-read, then
+// the whole block once more.
+__device__ __forceinline__ bool ll_wait8(const uint64_t* p, LL8& r, unsigned tag, const ProgParams& P) {
+  if (__all_sync(0xffffffffu, ll_ready8(r, tag))) return true;
+  Poll pl;
+  for (;;) {
+    if (!pl.again(P, tag)) return false;
+    if (!__all_sync(0xffffffffu, ll_has(ll_ld(p + 7), tag))) continue;
+    ll_load8(p, r);
+    if (__all_sync(0xffffffffu, ll_ready8(r, tag))) return true;
+  }
 }
 
-// RMSNorm total of one token's input row of nb super-blocks computed from the
-// row itself (an input not produced inside the program), in the fixed order:
-// each lane folds its own 32-value groups, then the lanes are folded.
-__device__ __forceinline__ float rms_total_plain(const float* row, int nb) {
+// RMSNorm total of one token from the producer's G tagged group sums, in the
+// fixed order (lane l adds groups l, l + 32, ... ascending, then the lanes
+// fold at distances 16, 8, 4, 2, 1).  false on timeout / abort.
+__device__ bool ll_rms_total(const uint64_t* sums, int G, unsigned tag, const ProgParams& P, float& total) {
   const int lane = threadIdx.x & 31;
   float acc = 0.f;
-  for (int g = lane; g < nb * 8; g += 32) {
-    const float* gp = row + (int64_t)g * 32;
-    float a[32];
+  for (int g0 = 0; g0 < G; g0 += 32 * 8) {
+    uint64_t w[8];
 #pragma unroll
-    for (int i = 0; i < 32; i += 4) {
-      const float4 q = __ldcg(reinterpret_cast<const float4*>(gp + i));
-      a[i] = __fmul_rn(q.x, q.x);
-      a[i + 1] = __fmul_rn(q.y, q.y);
-      a[i + 2] = __fmul_rn(q.z, q.z);
-      a[i + 3] = __fmul_rn(q.w, q.w);
+    for (int j = 0; j < 8; ++j) {
+      const int g = g0 + lane + 32 * j;
+      w[j] = g < G ? ll_ld(sums + g) : ((uint64_t)tag << 32);
+    }
+    Poll pl;
+    for (;;) {
+      bool ok = true;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) ok &= ll_has(w[j], tag);
+      if (__all_sync(0xffffffffu, ok)) break;
+      if (!pl.again(P, tag)) return false;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int g = g0 + lane + 32 * j;
+        if (g < G && !ll_has(w[j], tag)) w[j] = ll_ld(sums + g);
+      }
     }
 #pragma unroll
-    for (int width = 16; width >= 1; width >>= 1)
-#pragma unroll
-      for (int l = 0; l < width; ++l) a[l] = __fadd_rn(a[l], a[l + width]);
-    acc = __fadd_rn(acc, a[0]);
+    for (int j = 0; j < 8; ++j)
+      if (g0 + lane + 32 * j < G) acc = __fadd_rn(acc, ll_val(w[j]));
   }
 #pragma unroll
   for (int off = 16; off >= 1; off >>= 1) acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, off));
-  return acc;
+  total = acc;
+  return true;
 }
 
-// fp32 activation prologue: warp cw quantizes its super-blocks b = cw (mod W)
-// of every token to Q8_K in shared memory (after an RMSNorm of each row for
-// kInF32Rms), with the arithmetic of rms_q8k_quantize_kernel /
-// q8k_quantize_kernel.  The block loads (and, by the caller, the residual
-// loads) go out first; for an RMSNorm input warp 0 alone then reads the
-// producer's group sums -- one read per CTA, not one per warp, of lines every
-// CTA wants -- folds 1/rms of every token into inv[] and releases the other
-// warps.  When the warp's blocks fit (T x blocks <= kRegItems) they are all
-// in flight at once.  (17 warps leave 96 registers a thread: 3 blocks of 8
-// values for one token, 2 for two, otherwise one block at a time.)
+// Activation prologue of warp cw for one phase: its super-blocks
+// b = cw (mod W) of every token, read from the producer's tagged words as
+// soon as they exist, RMS-normalized (times the norm weight) when the phase
+// asks for it, and quantized to Q8_K in shared memory with the standalone
+// quantizer's helpers (same bits).  The first loads of all the warp's blocks
+// go out together (when they fit in registers: T x blocks <= kRegItems), the
+// group sums are folded while they are in flight.
 template <int T>
-__device__ __forceinline__ bool prologue_f32(const ProgParams& P, const PSmem& m, const ActSmem& act,
-                                             const PhaseDev& D, int cw, int W, int lane, int& nrms) {
+__device__ __forceinline__ bool prologue(const ProgParams& P, const ActSmem& act, const PhaseDev& D, int cw,
+                                         int W, int lane, unsigned tag, int64_t so) {
   const int nb = D.nb;
+  if (D.in_mode == kInQ8K) {  // caller memory, complete before the launch
+    const uint32_t* src = reinterpret_cast<const uint32_t*>(D.xq);
+    for (int b = cw; b < nb; b += W) {
+#pragma unroll 1
+      for (int t = 0; t < T; ++t)
+        copy_q8k_smem(src + ((int64_t)t * nb + b) * Q8K_BLOCK_WORDS, act, act_slot(cw, W, T, b / W, t), lane);
+    }
+    return true;
+  }
   constexpr int kRegItems = T == 1 ? 3 : (T == 2 ? 2 : 1);
   const bool rms = D.in_mode == kInF32Rms;
-  const float* x = static_cast<const float*>(D.x);
+  const uint64_t* x = set_ptr(D.x_ll, so);
   const int nbw = cw < nb ? (nb - cw + W - 1) / W : 0;  // blocks of this warp
   const int items = nbw * T;                            // item = i * T + t, block cw + i * W
+  auto src = [&](int it) { return x + (it % T) * D.ld_xll + (cw + (it / T) * W) * QK_K + lane * 8; };
+  LL8 r[kRegItems];
   const bool inreg = items <= kRegItems;
-  float v[kRegItems][8];
   if (inreg) {
 #pragma unroll
     for (int it = 0; it < kRegItems; ++it)
-      if (it < items) load8_cg(x + (it % T) * D.ld_x + (cw + (it / T) * W) * QK_K + lane * 8, v[it]);
+      if (it < items) ll_load8(src(it), r[it]);
   }
   float inv[T];
   if (rms) {
-    if (cw == 0) {
+    const int rep = (int)((blockIdx.x + cw) % kSumReps);
+    const uint64_t* s = set_ptr(D.xs_ll, so) + rep * D.ld_xsll;
 #pragma unroll 1
-      for (int t = 0; t < T; ++t) {
-        const float total = D.x_part ? rms_fold_groups_cg(D.x_part + t * D.ld_xpart, nb * 8)
-                                     : rms_total_plain(x + t * D.ld_x, nb);
-        if (lane == 0) m.inv[t] = rms_inv_from_sum(total, nb * QK_K, P.eps);
-      }
-      mbar_arrive_warp(m.invready);
+    for (int t = 0; t < T; ++t) {
+      float total;
+      if (!ll_rms_total(s + t * kSumReps * D.ld_xsll, nb * 8, tag, P, total)) return false;
+      inv[t] = rms_inv_from_sum(total, nb * QK_K, P.eps);
     }
-    if (!mbar_wait_bounded(m.invready, (unsigned)(nrms & 1), kTimeoutNs)) {
-      fail(P);
-      return false;
-    }
-    ++nrms;
-#pragma unroll
-    for (int t = 0; t < T; ++t) inv[t] = m.inv[t];
   }
-  auto quant = [&](int it, float (&u)[8]) {
-    const int t = it % T;
+  auto quant = [&](int it, LL8& w) -> bool {
+    if (!ll_wait8(src(it), w, tag, P)) return false;
+    const int t = it % T, b = cw + (it / T) * W;
+    float u[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) u[k] = ll_val(w.w[k]);
     if (rms) {
 #pragma unroll
       for (int k = 0; k < 8; ++k) u[k] = __fmul_rn(u[k], inv[t]);
+      if (D.norm_w) {
+        const float4 g0 = __ldg(reinterpret_cast<const float4*>(D.norm_w + b * QK_K + lane * 8));
+        const float4 g1 = __ldg(reinterpret_cast<const float4*>(D.norm_w + b * QK_K + lane * 8 + 4));
+        u[0] = __fmul_rn(u[0], g0.x);
+        u[1] = __fmul_rn(u[1], g0.y);
+        u[2] = __fmul_rn(u[2], g0.z);
+        u[3] = __fmul_rn(u[3], g0.w);
+        u[4] = __fmul_rn(u[4], g1.x);
+        u[5] = __fmul_rn(u[5], g1.y);
+        u[6] = __fmul_rn(u[6], g1.z);
+        u[7] = __fmul_rn(u[7], g1.w);
+      }
     }
     store_q8k_smem(q8k_quantize_lane(u), act, act_slot(cw, W, T, it / T, t));
+    return true;
   };
   if (inreg) {
 #pragma unroll
     for (int it = 0; it < kRegItems; ++it)
-      if (it < items) quant(it, v[it]);
+      if (it < items && !quant(it, r[it])) return false;
   } else {
     for (int it = 0; it < items; ++it) {
-      float u[8];
-      load8_cg(x + (it % T) * D.ld_x + (cw + (it / T) * W) * QK_K + lane * 8, u);
-      quant(it, u);
+      LL8 w;
+      ll_load8(src(it), w);
+      if (!quant(it, w)) return false;
     }
   }
   return true;
 }
 
-// Residual of one row group, T tokens, this lane's row.
-template <int T>
-__device__ __forceinline__ void load_resid(const PhaseDev& D, int64_t group, int lane, float (&r)[T]) {
-  const int64_t orow = group * 32 + lane;
-#pragma unroll
-  for (int t = 0; t < T; ++t) r[t] = orow < D.n_rows ? __ldcg(D.resid + t * D.ld_resid + orow) : 0.f;
-}
-
 // Ordered sum of one row group's super-block terms and the phase's epilogue
-// (the arithmetic of finish_group in q2k_gemv.cu); then the group sums of
-// squares when a later phase reads this output through an RMSNorm.
+// (the arithmetic of finish_group in q2k_gemv.cu); the caller-visible store,
+// the tagged store, and the group sums of squares when a later phase reads
+// this output through an RMSNorm.
 template <int T>
-__device__ __forceinline__ void finish_group_prog(const float* terms, const PhaseDev& D, int64_t group, int lane,
-                                                  const float (&r)[T]) {
+__device__ __forceinline__ bool finish_group_prog(const ProgParams& P, const float* terms, const PhaseDev& D,
+                                                  int64_t group, int lane, unsigned tag, int64_t so) {
   const int nb = D.nb;
+  uint64_t* yl = set_ptr(D.y_ll, so);
   if (D.epi == kEpiSiluMul) {
     if (lane < 16) {
       const int64_t orow = group * 16 + lane;
@@ -309,80 +426,130 @@ __device__ __forceinline__ void finish_group_prog(const float* terms, const Phas
         }
         if (2 * orow < D.n_rows) {
           const float sg = __fdiv_rn(g, __fadd_rn(1.0f, expf(-g)));
-          D.y[t * D.ldy + orow] = __fmul_rn(sg, u);
+          const float h = __fmul_rn(sg, u);
+          D.y[t * D.ldy + orow] = h;
+          ll_st(yl + t * D.ld_yll + orow, ll_pack(h, tag));
         }
       }
     }
-  } else {
-    const int64_t orow = group * 32 + lane;
+    return true;
+  }
+  const int64_t orow = group * 32 + lane;
+  const bool live = orow < D.n_rows;
+  float r[T];
+  if (D.epi == kEpiResidual) {  // issue the residual loads before the sums
+    const uint64_t* rl = set_ptr(D.r_ll, so);
+    uint64_t w[T];
 #pragma unroll
-    for (int t = 0; t < T; ++t) {
-      const float* tr = terms + (size_t)t * nb * 32 + lane;
-      float s = 0.f;
-      int b = 0;
-      for (; b + 8 <= nb; b += 8) {
-        float v[8];
+    for (int t = 0; t < T; ++t) w[t] = live ? ll_ld(rl + t * D.ld_rll + orow) : ((uint64_t)tag << 32);
+    Poll pl;
+    for (;;) {
+      bool ok = true;
 #pragma unroll
-        for (int k = 0; k < 8; ++k) v[k] = tr[(b + k) * 32];
+      for (int t = 0; t < T; ++t) ok &= ll_has(w[t], tag);
+      if (__all_sync(0xffffffffu, ok)) break;
+      if (!pl.again(P, tag)) return false;
 #pragma unroll
-        for (int k = 0; k < 8; ++k) s = __fadd_rn(s, v[k]);
+      for (int t = 0; t < T; ++t)
+        if (live && !ll_has(w[t], tag)) w[t] = ll_ld(rl + t * D.ld_rll + orow);
+    }
+#pragma unroll
+    for (int t = 0; t < T; ++t) r[t] = ll_val(w[t]);
+  }
+  uint64_t* ysl = D.ys_ll ? set_ptr(D.ys_ll, so) : nullptr;
+#pragma unroll
+  for (int t = 0; t < T; ++t) {
+    const float* tr = terms + (size_t)t * nb * 32 + lane;
+    float s = 0.f;
+    int b = 0;
+    for (; b + 8 <= nb; b += 8) {
+      float v[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) v[k] = tr[(b + k) * 32];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) s = __fadd_rn(s, v[k]);
+    }
+    for (; b < nb; ++b) s = __fadd_rn(s, tr[b * 32]);
+    if (live) {
+      if (D.epi == kEpiResidual) s = __fadd_rn(r[t], s);
+      D.y[t * D.ldy + orow] = s;
+      ll_st(yl + t * D.ld_yll + orow, ll_pack(s, tag));
+    }
+    if (ysl) {
+      const float ss = group_sumsq_lane(live ? s : 0.f);
+      if (lane < kSumReps) ll_st(ysl + (t * kSumReps + lane) * D.ld_ysll + group, ll_pack(ss, tag));
+    }
+  }
+  return true;
+}
+
+// Walks this CTA's ring stages in program order: phase, row group (c, c + C,
+// ...), chunk of up to W consecutive super-blocks (incrementally: the
+// producer thread does no division per stage).
+struct StageCursor {
+  int ph = 0, n_phases = 0;
+  int64_t g = 0, ng = 0, C = 1;
+  int c = 0, nchunks = 0, nb = 0, W = 0;
+  const uint8_t* tiles = nullptr;
+
+  __device__ void load_phase(const ProgParams& P, int64_t cta) {
+    for (; ph < n_phases; ++ph) {
+      const PhaseDev& D = P.phases[ph];
+      if (cta < D.n_groups) {
+        nb = D.nb;
+        nchunks = (nb + W - 1) / W;
+        ng = D.n_groups;
+        tiles = D.tiles;
+        g = cta;
+        c = 0;
+        return;
       }
-      for (; b < nb; ++b) s = __fadd_rn(s, tr[b * 32]);
-      const bool live = orow < D.n_rows;
-      if (live) {
-        if (D.epi == kEpiResidual) s = __fadd_rn(r[t], s);
-        D.y[t * D.ldy + orow] = s;
-      }
-      if (D.y_part) {
-        const float ss = group_sumsq_lane(live ? s : 0.f);
-        if (lane == 0) D.y_part[t * D.n_part + group] = ss;
-      }
+    }
+  }
+  __device__ void start(const ProgParams& P, int64_t cta, int64_t nctas, int w) {
+    W = w;
+    C = nctas;
+    n_phases = P.n_phases;
+    ph = 0;
+    load_phase(P, cta);
+  }
+  __device__ bool valid() const { return ph < n_phases; }
+  __device__ const uint8_t* src() const { return tiles + ((size_t)g * nb + (size_t)c * W) * kTileBytes; }
+  __device__ unsigned bytes() const { return (unsigned)(min(W, nb - c * W) * kTileBytes); }
+  __device__ void advance(const ProgParams& P, int64_t cta) {
+    if (++c < nchunks) return;
+    c = 0;
+    g += C;
+    if (g < ng) return;
+    ++ph;
+    load_phase(P, cta);
+  }
+};
+
+// Copy the launch's outside inputs into their tagged buffers: one warp per
+// 32-value group of one token, with the group's sum of squares when an
+// RMSNorm reads it (the finishers' fold: one value per lane).
+__device__ void copy_inputs(const ProgParams& P, unsigned tag, int64_t so, int64_t gw, int64_t nw, int lane) {
+  int j = 0;
+  int64_t base = 0;
+  for (int64_t u = gw;; u += nw) {
+    while (j < P.n_copies && u >= base + P.copies[j].units) {
+      base += P.copies[j].units;
+      ++j;
+    }
+    if (j >= P.n_copies) return;
+    const CopyDev& cp = P.copies[j];
+    const int64_t per_tok = (cp.len + 31) / 32;
+    const int64_t t = (u - base) / per_tok, grp = (u - base) - t * per_tok;
+    const int64_t i = grp * 32 + lane;
+    const float v = i < cp.len ? cp.src[t * cp.ld_src + i] : 0.f;
+    if (i < cp.len) ll_st(set_ptr(cp.dst, so) + t * cp.ld_dst + i, ll_pack(v, tag));
+    if (cp.sums) {
+      const float ss = group_sumsq_lane(v);
+      if (lane < kSumReps) ll_st(set_ptr(cp.sums, so) + (t * kSumReps + lane) * cp.ld_sums + grp, ll_pack(ss, tag));
     }
   }
 }
-
-// Walks this CTA's ring stages in program order: phase, row group, chunk of
-// up to W consecutive super-blocks (incrementally: the producer thread does
-// no division per stage).
-struct StageCursor {
-  int ph = 0, n_phases = 0;
-  int64_t g = 0, ng = 0;  // row group within the CTA's range, groups in the range
-  int c = 0, nchunks = 0, nb = 0, W = 0;
-  const uint8_t* base = nullptr;
-  int64_t index = 0;      // stages walked so far (the ring's running index)
-
-  __device__ void load_phase(const ProgParams& P, int64_t cta, int64_t C) {
-    for (; ph < n_phases; ++ph) {
-      const PhaseDev& D = P.phases[ph];
-      const int64_t g0 = cta * D.n_groups / C, g1 = (cta + 1) * D.n_groups / C;
-      nb = D.nb;
-      nchunks = (nb + W - 1) / W;
-      ng = g1 - g0;
-      base = D.tiles + g0 * nb * (int64_t)kTileBytes;
-      g = 0;
-      c = 0;
-      if (ng > 0) return;
-    }
-  }
-  __device__ void start(const ProgParams& P, int64_t cta, int64_t C, int w) {
-    W = w;
-    n_phases = P.n_phases;
-    ph = 0;
-    index = 0;
-    load_phase(P, cta, C);
-  }
-  __device__ bool valid() const { return ph < n_phases; }
-  __device__ const uint8_t* src() const { return base + ((size_t)g * nb + (size_t)c * W) * kTileBytes; }
-  __device__ unsigned bytes() const { return (unsigned)(min(W, nb - c * W) * kTileBytes); }
-  __device__ void advance(const ProgParams& P, int64_t cta, int64_t C) {
-    ++index;
-    if (++c < nchunks) return;
-    c = 0;
-    if (++g < ng) return;
-    ++ph;
-    load_phase(P, cta, C);
-  }
-};
 
 template <int T>
 __global__ void __launch_bounds__(kMaxWarps * 32, 1) q2k_program_kernel(const ProgParams P) {
@@ -392,8 +559,10 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1) q2k_program_kernel(const Pr
   const int S = P.stages, lgS = P.log2_stages, smask = S - 1;
   const int64_t C = gridDim.x, cta = blockIdx.x;
   const int stage_bytes = W * kTileBytes;
-  const PSmem m = pcarve(smem, T, P.nb_max, S, W);
-  const unsigned* abort_word = P.ctr + P.n_phases + 1;
+  const PSmem m = pcarve(smem, T, P.nb_max, S, W, P.tbufs);
+  // every thread reads the launch count before the CTA's first sync, i.e.
+  // before its CTA can arrive at the grid barrier after which CTA 0 advances it
+  const unsigned tag = ld_relaxed_gpu(P.ctl) + 1u;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
@@ -404,32 +573,21 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1) q2k_program_kernel(const Pr
       mbar_init(&m.grp[b], W);
       mbar_init(&m.tfree[b], 1);
     }
-    mbar_init(m.done, W);
-    mbar_init(m.inready, 1);
-    mbar_init(m.invready, 1);
-    *m.gate_fail = 0u;
     mbar_fence_init();
   }
   __syncthreads();
+  const int64_t so = (int64_t)(tag & 1u) * P.set_bytes;
 
   if (warp == 0) {
-    // ---- producer: every phase's tiles of this CTA, in program order, into
-    // the ring; and, l2_ahead stages further on, prefetches of the same tiles
-    // into L2, so HBM keeps streaming while the consumers sit at a phase
-    // boundary with the ring full (the ring loads then hit L2)
+    // ---- producer: every phase's tiles of this CTA, in program order
     if (lane == 0) {
-      StageCursor issue, pref;
+      StageCursor issue;
       issue.start(P, cta, C, W);
-      pref.start(P, cta, C, W);
       bool ok = true;
       int64_t i = 0;
-      for (; issue.valid(); issue.advance(P, cta, C), ++i) {
-        while (P.l2_ahead > 0 && pref.valid() && pref.index < i + P.l2_ahead) {
-          bulk_prefetch_l2(pref.src(), pref.bytes());
-          pref.advance(P, cta, C);
-        }
+      for (; issue.valid(); issue.advance(P, cta), ++i) {
         const int s = (int)(i & smask);
-        if (i >= S && !mbar_wait_bounded(&m.empty[s], (unsigned)(((i >> lgS) - 1) & 1), kTimeoutNs)) {
+        if (i >= S && !pwait(&m.empty[s], (unsigned)(((i >> lgS) - 1) & 1), P, tag)) {
           ok = false;
           break;
         }
@@ -437,9 +595,9 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1) q2k_program_kernel(const Pr
         bulk_copy_g2s(m.ring + (size_t)s * stage_bytes, issue.src(), issue.bytes(), &m.full[s]);
       }
       if (!ok) {
-        fail(P);
+        fail(P, tag);
         for (int64_t j = (i > S ? i - S : 0); j < i; ++j)
-          mbar_wait_bounded(&m.full[j & smask], (unsigned)((j >> lgS) & 1), kTimeoutNs);
+          mbar_wait_bounded(&m.full[j & smask], (unsigned)((j >> lgS) & 1), P.timeout_ns);
       }
     }
     return;
@@ -448,80 +606,56 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1) q2k_program_kernel(const Pr
   // ---- consumers
   const int cw = warp - 1;
   const ActSmem act = {m.qs, m.bs, m.d};
-  int64_t i = 0;  // ring stage, in step with the producer
-  int jj = 0;     // row groups processed by this CTA (terms double buffer, finisher rota)
-  int nwait = 0;  // phases this CTA took part in (inready parity, descriptor slot)
-  int nrms = 0;   // RMSNorm inputs read (invready parity)
-  for (int ph = 0; ph < P.n_phases; ++ph) {
-    const int nb = P.phases[ph].nb;
-    const int64_t ngr = P.phases[ph].n_groups;
-    const int64_t g0 = cta * ngr / C, g1 = (cta + 1) * ngr / C;
-    if (g0 == g1) continue;
-    const int nchunks = (nb + W - 1) / W;
 
-    // phase ph reads phase ph-1's complete output (and, through it, every
-    // earlier phase's): one lane waits, the other warps sleep on inready.
-    // Meanwhile warp 0 brings the phase's descriptor into shared memory (the
-    // gate's acquire leaves this SM's L1 stale, so reading it in place would
-    // cost an L2 round trip before the first activation load and again in
-    // every finisher).  The slot alternates per phase this CTA takes part
-    // in: the slot written here was last read in the CTA's phase before the
-    // previous one, which ended before the previous gate opened.
-    PhaseDev& Ds = m.pd[nwait & 1];
-    if (cw == 0) {
-      constexpr int kWords = (int)(sizeof(PhaseDev) / 4);
-      static_assert(sizeof(PhaseDev) % 4 == 0 && kWords <= 32, "phase descriptor copy");
-      if (lane < kWords)
-        reinterpret_cast<uint32_t*>(&Ds)[lane] = __ldcg(reinterpret_cast<const uint32_t*>(P.phases + ph) + lane);
-      if (ph > 0 && lane == 0 && !wait_count(P.ctr + ph - 1, (unsigned)P.phases[ph - 1].n_groups, abort_word)) {
-        fail(P);
-        *m.gate_fail = 1u;
+  // outside inputs -> tagged buffers, then the one grid-wide barrier: after
+  // it no CTA reads caller memory a phase may overwrite
+  copy_inputs(P, tag, so, cta * W + cw, C * W, lane);
+  asm volatile("bar.sync 1, %0;" ::"r"(W * 32) : "memory");
+  if (cw == 0) {
+    int ok = 1;
+    if (lane == 0) {
+      red_release_gpu_add(P.ctl + 1, 1u);
+      const unsigned target = tag * (unsigned)C;
+      if ((int)(ld_acquire_gpu(P.ctl + 1) - target) < 0) {
+        const uint64_t t0 = global_timer_ns();
+        for (int k = 0; (int)(ld_acquire_gpu(P.ctl + 1) - target) < 0; ++k) {
+          if ((k & 15) == 15 && (ld_relaxed_gpu(P.ctl + 2) == tag || global_timer_ns() - t0 > P.timeout_ns)) {
+            fail(P, tag);
+            ok = 0;
+            break;
+          }
+        }
       }
-      mbar_arrive_warp(m.inready);
-    }
-    if (!mbar_wait_bounded(m.inready, (unsigned)(nwait & 1), kTimeoutNs)) {
-      fail(P);
-      return;
-    }
-    ++nwait;
-    if (*reinterpret_cast<volatile unsigned*>(m.gate_fail)) return;
-    const PhaseDev& D = Ds;
-
-    // one round of loads: the residual of the first row group this warp will
-    // finish, and the activation prologue (this warp's super-blocks)
-    const int64_t jfirst = ((cw - jj) % W + W) % W;  // local index of that group
-    float res[T];
-#pragma unroll
-    for (int t = 0; t < T; ++t) res[t] = 0.f;
-    if (D.epi == kEpiResidual && jfirst < g1 - g0) load_resid<T>(D, g0 + jfirst, lane, res);
-    if (D.in_mode == kInQ8K) {
-      const uint32_t* src = static_cast<const uint32_t*>(D.x);
-      for (int b = cw; b < nb; b += W) {
-#pragma unroll 1
-        for (int t = 0; t < T; ++t)
-          copy_q8k_smem(src + ((int64_t)t * nb + b) * Q8K_BLOCK_WORDS, act, act_slot(cw, W, T, b / W, t), lane);
-      }
-    } else if (!prologue_f32<T>(P, m, act, D, cw, W, lane, nrms)) {
-      return;
+      if (ok && cta == 0) st_relaxed_gpu(P.ctl, tag);  // every CTA has read the count: advance it
     }
     __syncwarp();
+  }
+  asm volatile("bar.sync 1, %0;" ::"r"(W * 32) : "memory");
+  if (ld_relaxed_gpu(P.ctl + 2) == tag) return;
 
-    // this CTA's row groups of the phase
-    for (int64_t g = g0; g < g1; ++g, ++jj) {
-      const int buf = jj & 1;
+  int64_t i = 0;  // ring stage, in step with the producer
+  int jj = 0;     // row groups processed by this CTA (terms buffers, finisher rota)
+  for (int ph = 0; ph < P.n_phases; ++ph) {
+    const PhaseDev& D = P.phases[ph];
+    const int64_t ngr = D.n_groups;
+    if (cta >= ngr) continue;
+    const int nb = D.nb;
+    const int nchunks = (nb + W - 1) / W;
+    if (!prologue<T>(P, act, D, cw, W, lane, tag, so)) return;
+    __syncwarp();
+
+    // this CTA's row groups of the phase: cta, cta + C, ...
+    for (int64_t g = cta; g < ngr; g += C, ++jj) {
+      // terms buffer of this group and how many times it was used before
+      const int buf = P.tbufs == 2 ? (jj & 1) : 0;
+      const int use = P.tbufs == 2 ? (jj >> 1) : jj;
       float* terms = m.terms + (size_t)buf * T * P.nb_max * 32;
-      if (jj >= 2 && !mbar_wait_bounded(&m.tfree[buf], (unsigned)(((jj >> 1) - 1) & 1), kTimeoutNs)) {
-        fail(P);
-        return;
-      }
+      if (use >= 1 && !pwait(&m.tfree[buf], (unsigned)((use - 1) & 1), P, tag)) return;
       const int64_t row = g * 32 + lane;
       for (int c = 0; c < nchunks; ++c, ++i) {
         const int s = (int)(i & smask);
         const int b = c * W + cw;
-        if (!mbar_wait_bounded(&m.full[s], (unsigned)((i >> lgS) & 1), kTimeoutNs)) {
-          fail(P);
-          return;
-        }
+        if (!pwait(&m.full[s], (unsigned)((i >> lgS) & 1), P, tag)) return;
         if (b >= nb) {  // the group's last chunk is short
           mbar_arrive_warp(&m.empty[s]);
           continue;
@@ -533,38 +667,10 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1) q2k_program_kernel(const Pr
       }
       mbar_arrive_warp(&m.grp[buf]);
       if (cw == (jj % W)) {
-        if (!mbar_wait_bounded(&m.grp[buf], (unsigned)((jj >> 1) & 1), kTimeoutNs)) {
-          fail(P);
-          return;
-        }
-        if (D.epi == kEpiResidual && g != g0 + jfirst) load_resid<T>(D, g, lane, res);
-        finish_group_prog<T>(terms, D, g, lane, res);
+        if (!pwait(&m.grp[buf], (unsigned)(use & 1), P, tag)) return;
+        const bool ok = finish_group_prog<T>(P, terms, D, g, lane, tag, so);
         mbar_arrive_warp(&m.tfree[buf]);
-        if (g == g1 - 1) {
-          // The CTA's last row group of the phase: its grp wait followed every
-          // earlier finisher's stores (each finisher arrives on the next
-          // group's barrier after its own), and __syncwarp orders this warp's
-          // lanes, so one release add publishes all of the CTA's rows.
-          __syncwarp();
-          if (lane == 0) red_release_gpu_add(P.ctr + ph, (unsigned)(g1 - g0));
-        }
-      }
-    }
-  }
-
-  // ---- exit: the last CTA out resets the counters for the next launch
-  mbar_arrive_warp(m.done);
-  if (cw == 0) {
-    const bool ok = mbar_wait_bounded(m.done, 0, kTimeoutNs);
-    if (lane == 0) {
-      if (!ok) {
-        fail(P);
-      } else if (!ld_relaxed_gpu(abort_word)) {
-        unsigned* exit_ctr = P.ctr + P.n_phases;
-        if (atomicAdd(exit_ctr, 1u) == (unsigned)(C - 1)) {
-          for (int k = 0; k < P.n_phases; ++k) atomicExch(P.ctr + k, 0u);
-          atomicExch(exit_ctr, 0u);
-        }
+        if (!ok) return;
       }
     }
   }
@@ -575,20 +681,21 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1) q2k_program_kernel(const Pr
 struct Q2KProgram {
   uint32_t magic = kProgramMagic;
   int n_phases = 0;
+  int n_copies = 0;
   int T = 0;
   int nb_max = 0;
   int consumers = 0;
   int stages = 0;
+  int tbufs = 2;
   int grid = 0;
   size_t smem = 0;
   float eps = 0.f;
   int device = 0;
   PhaseDev* d_phases = nullptr;
-  unsigned* d_ctr = nullptr;
-  int64_t counter_words = 0;
-  float* d_parts = nullptr;  // every group-sum array
-  size_t parts_bytes = 0;
-  int l2_ahead = 0;
+  CopyDev* d_copies = nullptr;
+  unsigned* d_ctl = nullptr;
+  uint64_t* d_ll = nullptr;  // both sets of tagged buffers
+  size_t set_bytes = 0;
 };
 
 namespace {
@@ -604,6 +711,23 @@ Range rows_range(const void* base, int64_t ld, int64_t cols, int64_t len, size_t
   r.hi = r.lo + (size_t)((cols - 1) * ld + len) * elem;
   return r;
 }
+
+int64_t round_up(int64_t v, int64_t a) { return (v + a - 1) / a * a; }
+
+// A region of fp32 token rows read by some phase: produced by phase `src`
+// (at row offset r0 of its output), or written before the launch (src < 0).
+struct Source {
+  int src = -1;
+  int64_t r0 = 0;
+  int ext = -1;  // index into the outside-input list when src < 0
+};
+
+struct Ext {
+  const float* ptr;
+  int64_t ld, len;
+  bool sums;
+  int64_t off_ll = 0, off_sums = 0, ld_ll = 0, ld_sums = 0;  // word offsets in a set
+};
 
 }  // namespace
 
@@ -623,9 +747,6 @@ int q2k_program_create(const ProgPhase* phases, int n_phases, int n_cols, float 
   const int n = n_phases;
   std::vector<int64_t> out_rows((size_t)n);
   std::vector<Range> yr((size_t)n);
-  std::vector<int> x_src((size_t)n, -1);
-  std::vector<int64_t> x_r0((size_t)n, 0);
-  std::vector<char> need_part((size_t)n, 0);
   int nb_max = 0;
   for (int p = 0; p < n; ++p) {
     const ProgPhase& s = phases[p];
@@ -638,10 +759,12 @@ int q2k_program_create(const ProgPhase* phases, int n_phases, int n_cols, float 
       set_last_error("q2k_program: phase %d: unknown input mode %d", p, s.in_mode);
       return kBadArgument;
     }
-    if (s.in_mode == kInQ8K ? (reinterpret_cast<uintptr_t>(s.x) & 3) != 0
-                            : ((reinterpret_cast<uintptr_t>(s.x) & 15) != 0 || s.ld_x < w.k || (s.ld_x & 3))) {
-      set_last_error("q2k_program: phase %d: Q8_K input must be 4-byte aligned; fp32 input 16-byte aligned with "
-                     "ld_x >= k and a multiple of 4", p);
+    if (s.in_mode == kInQ8K ? (reinterpret_cast<uintptr_t>(s.x) & 3) != 0 : (s.ld_x < w.k)) {
+      set_last_error("q2k_program: phase %d: Q8_K input must be 4-byte aligned; fp32 input needs ld_x >= k", p);
+      return kBadArgument;
+    }
+    if (s.norm_w && (s.in_mode != kInF32Rms || (reinterpret_cast<uintptr_t>(s.norm_w) & 15))) {
+      set_last_error("q2k_program: phase %d: an RMSNorm weight needs the RMS input mode and 16-byte alignment", p);
       return kBadArgument;
     }
     if (s.epi != kEpiStore && s.epi != kEpiResidual && s.epi != kEpiSiluMul) {
@@ -661,55 +784,121 @@ int q2k_program_create(const ProgPhase* phases, int n_phases, int n_cols, float 
       set_last_error("q2k_program: phase %d: leading dimension smaller than the output rows", p);
       return kBadArgument;
     }
-    // An RMSNorm input that an earlier phase wrote (the latest one whose
-    // output overlaps it) takes its sum of squares from that phase's group
-    // sums: the rows must be a 32-row aligned slice of a store or residual
-    // output with the same token stride.
-    if (s.in_mode == kInF32Rms) {
-      const Range want = rows_range(s.x, s.ld_x, T, w.k, 4);
-      for (int q = p - 1; q >= 0; --q) {
-        if (!yr[(size_t)q].overlaps(want)) continue;
-        const ProgPhase& src = phases[q];
-        const intptr_t off = reinterpret_cast<intptr_t>(s.x) - reinterpret_cast<intptr_t>(src.y);
-        if (s.ld_x != src.ldy || off < 0 || off % 128 || off / 4 + w.k > out_rows[(size_t)q] ||
-            src.epi == kEpiSiluMul) {
-          set_last_error("q2k_program: phase %d: an RMSNorm input written by phase %d must be a 32-row aligned "
-                         "slice of its store or residual output with the same row stride", p, q);
-          return kBadArgument;
-        }
-        x_src[(size_t)p] = q;
-        x_r0[(size_t)p] = off / 4;
-        need_part[(size_t)q] = 1;
-        break;
-      }
-    }
     yr[(size_t)p] = rows_range(s.y, s.ldy, T, out_rows[(size_t)p], 4);
     nb_max = nb_max > w.nb ? nb_max : w.nb;
   }
-  std::vector<size_t> part_off((size_t)n, 0);
-  std::vector<int64_t> n_part((size_t)n, 0);
-  size_t parts = 0;
+
+  // Where each fp32 input and residual comes from: the latest earlier phase
+  // whose output overlaps it (it must then be a slice of that output with the
+  // same token stride), or the caller's memory before the launch.
+  std::vector<Ext> ext;
+  auto find_src = [&](int p, const void* ptr, int64_t ld, int64_t len, bool rms, const char* what,
+                      Source& src) -> int {
+    const Range want = rows_range(ptr, ld, T, len, 4);
+    for (int q = p - 1; q >= 0; --q) {
+      if (!yr[(size_t)q].overlaps(want)) continue;
+      const ProgPhase& sq = phases[q];
+      const intptr_t off = reinterpret_cast<intptr_t>(ptr) - reinterpret_cast<intptr_t>(sq.y);
+      if (ld != sq.ldy || off < 0 || off % 128 || off / 4 + len > out_rows[(size_t)q] ||
+          (rms && sq.epi == kEpiSiluMul)) {
+        set_last_error("q2k_program: phase %d: a %s written by phase %d must be a 32-row aligned slice of its "
+                       "output with the same row stride (and, for an RMSNorm input, not a silu*mul output)",
+                       p, what, q);
+        return kBadArgument;
+      }
+      src.src = q;
+      src.r0 = off / 4;
+      return kOk;
+    }
+    const float* f = static_cast<const float*>(ptr);
+    for (size_t e = 0; e < ext.size(); ++e)
+      if (ext[e].ptr == f && ext[e].ld == ld && ext[e].len == len) {
+        ext[e].sums = ext[e].sums || rms;
+        src.ext = (int)e;
+        return kOk;
+      }
+    ext.push_back(Ext{f, ld, len, rms});
+    src.ext = (int)ext.size() - 1;
+    return kOk;
+  };
+  std::vector<Source> xin((size_t)n), rin((size_t)n);
+  std::vector<char> need_sums((size_t)n, 0);
   for (int p = 0; p < n; ++p) {
-    n_part[(size_t)p] = (out_rows[(size_t)p] + 31) / 32;
-    if (need_part[(size_t)p]) {
-      part_off[(size_t)p] = parts;
-      parts += al16((size_t)T * n_part[(size_t)p] * 4);
+    const ProgPhase& s = phases[p];
+    const Q2KWeight& w = *s.w;
+    if (s.in_mode != kInQ8K) {
+      int st = find_src(p, s.x, s.ld_x, w.k, s.in_mode == kInF32Rms, "input", xin[(size_t)p]);
+      if (st) return st;
+      if (s.in_mode == kInF32Rms && xin[(size_t)p].src >= 0) need_sums[(size_t)xin[(size_t)p].src] = 1;
+    } else {
+      const Range q8 = rows_range(s.x, w.nb * (int64_t)Q8K_BLOCK_BYTES, T, w.nb * (int64_t)Q8K_BLOCK_BYTES, 1);
+      for (int q = 0; q < n; ++q)
+        if (yr[(size_t)q].overlaps(q8)) {
+          set_last_error("q2k_program: phase %d's Q8_K input overlaps phase %d's output", p, q);
+          return kBadArgument;
+        }
+    }
+    if (s.epi == kEpiResidual) {
+      int st = find_src(p, s.resid, s.ld_resid, out_rows[(size_t)p], false, "residual", rin[(size_t)p]);
+      if (st) return st;
+    }
+    if (s.norm_w) {
+      const Range nw = rows_range(s.norm_w, 0, 1, w.k, 4);
+      for (int q = 0; q < n; ++q)
+        if (yr[(size_t)q].overlaps(nw)) {
+          set_last_error("q2k_program: phase %d's RMSNorm weight overlaps phase %d's output", p, q);
+          return kBadArgument;
+        }
     }
   }
+
+  // tagged buffers of one set (word offsets): phase outputs, their group
+  // sums, the outside inputs (and their group sums)
+  std::vector<int64_t> off_y((size_t)n), ld_yll((size_t)n), off_ys((size_t)n, -1), ld_ys((size_t)n, 0);
+  int64_t words = 0;
+  for (int p = 0; p < n; ++p) {
+    ld_yll[(size_t)p] = round_up(out_rows[(size_t)p], 32);
+    off_y[(size_t)p] = words;
+    words += T * ld_yll[(size_t)p];
+    if (need_sums[(size_t)p]) {
+      ld_ys[(size_t)p] = round_up((out_rows[(size_t)p] + 31) / 32, 2);
+      off_ys[(size_t)p] = words;
+      words += (int64_t)T * kSumReps * ld_ys[(size_t)p];
+    }
+  }
+  for (Ext& e : ext) {
+    e.ld_ll = round_up(e.len, 32);
+    e.off_ll = words;
+    words += T * e.ld_ll;
+    if (e.sums) {
+      e.ld_sums = round_up((e.len + 31) / 32, 2);
+      e.off_sums = words;
+      words += (int64_t)T * kSumReps * e.ld_sums;
+    }
+  }
+  const size_t set_bytes = (size_t)round_up(words * 8, 256);
+
   // launch shape: 16 consumer warps (8 when the activation planes of 8 tokens
   // leave too little room) and the deepest power-of-two ring that fits
   int sms = 0, optin = 0;
   SMEAI_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
   SMEAI_CUDA_TRY(cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev));
-  int consumers = 0, stages = 0;
-  for (int W : {16, 8}) {
-    for (int S = 8; S >= 2; S >>= 1)
-      if (prog_smem_bytes(T, nb_max, S, W) <= (size_t)optin) {
-        stages = S;
+  // (a single terms buffer as the last resort: 8 tokens of a k = 11008 input)
+  int consumers = 0, stages = 0, tbufs = 0;
+  for (int tb : {2, 1}) {
+    for (int W : {16, 8}) {
+      for (int S = 8; S >= 2; S >>= 1)
+        if (prog_smem_bytes(T, nb_max, S, W, tb) <= (size_t)optin) {
+          stages = S;
+          break;
+        }
+      if (stages) {
+        consumers = W;
         break;
       }
+    }
     if (stages) {
-      consumers = W;
+      tbufs = tb;
       break;
     }
   }
@@ -717,7 +906,7 @@ int q2k_program_create(const ProgPhase* phases, int n_phases, int n_cols, float 
     set_last_error("q2k_program: k=%d super-blocks x %d tokens does not fit in shared memory", nb_max, T);
     return kBadArgument;
   }
-  const size_t smem = prog_smem_bytes(T, nb_max, stages, consumers);
+  const size_t smem = prog_smem_bytes(T, nb_max, stages, consumers, tbufs);
   void* kern = nullptr;
   switch (T) {
     case 1: kern = reinterpret_cast<void*>(q2k_program_kernel<1>); break;
@@ -734,31 +923,27 @@ int q2k_program_create(const ProgPhase* phases, int n_phases, int n_cols, float 
   }
   Q2KProgram* pr = new Q2KProgram();
   pr->n_phases = n;
+  pr->n_copies = (int)ext.size();
   pr->T = T;
   pr->nb_max = nb_max;
   pr->consumers = consumers;
   pr->stages = stages;
+  pr->tbufs = tbufs;
   pr->grid = sms;  // one CTA per SM: every SM streams
   pr->smem = smem;
   pr->eps = eps;
   pr->device = dev;
-  pr->counter_words = (int64_t)n + 2;
-  pr->parts_bytes = parts;
-  // L2 prefetch of ring stages ahead of the ring loads: off by default
-  // (measured on B200, 7B-shape decode: 0.965 ms per token without, 0.985 ms
-  // with 8 stages ahead -- the ring alone keeps the stream fed, and the extra
-  // requests cost more than they hide).  SMEAI_PROGRAM_L2_AHEAD=n sets it.
-  pr->l2_ahead = 0;
-  if (const char* e = getenv("SMEAI_PROGRAM_L2_AHEAD")) pr->l2_ahead = atoi(e) < 0 ? 0 : atoi(e);
-  if (cudaMalloc(&pr->d_phases, sizeof(PhaseDev) * (size_t)n) != cudaSuccess ||
-      cudaMalloc(&pr->d_ctr, sizeof(unsigned) * (size_t)pr->counter_words) != cudaSuccess ||
-      (parts && cudaMalloc(&pr->d_parts, parts) != cudaSuccess)) {
+  pr->set_bytes = set_bytes;
+  if (device_malloc((void**)&pr->d_phases, sizeof(PhaseDev) * (size_t)n) != cudaSuccess ||
+      device_malloc((void**)&pr->d_copies, sizeof(CopyDev) * (ext.empty() ? 1 : ext.size())) != cudaSuccess ||
+      device_malloc((void**)&pr->d_ctl, sizeof(unsigned) * 4) != cudaSuccess ||
+      device_malloc((void**)&pr->d_ll, 2 * set_bytes) != cudaSuccess) {
     cudaGetLastError();
     q2k_program_free(pr);
     set_last_error("q2k_program: cudaMalloc failed");
     return kAllocFailed;
   }
-  uint8_t* pb = reinterpret_cast<uint8_t*>(pr->d_parts);
+  uint64_t* ll = pr->d_ll;
   std::vector<PhaseDev> hp((size_t)n);
   for (int p = 0; p < n; ++p) {
     const ProgPhase& s = phases[p];
@@ -766,27 +951,69 @@ int q2k_program_create(const ProgPhase* phases, int n_phases, int n_cols, float 
     PhaseDev& d = hp[(size_t)p];
     d = PhaseDev{};
     d.tiles = w.tiles;
-    d.x = s.x;
+    d.in_mode = s.in_mode;
+    d.norm_w = s.norm_w;
     d.y = s.y;
-    d.resid = s.resid;
+    d.ldy = s.ldy;
+    d.y_ll = ll + off_y[(size_t)p];
+    d.ld_yll = ld_yll[(size_t)p];
+    if (off_ys[(size_t)p] >= 0) {
+      d.ys_ll = ll + off_ys[(size_t)p];
+      d.ld_ysll = ld_ys[(size_t)p];
+    }
     d.n_rows = w.n_rows;
     d.n_groups = w.n_groups;
-    d.ld_x = s.ld_x;
-    d.ldy = s.ldy;
-    d.n_part = n_part[(size_t)p];
-    d.ld_resid = s.ld_resid;
     d.nb = w.nb;
-    d.in_mode = s.in_mode;
     d.epi = s.epi;
-    if (need_part[(size_t)p]) d.y_part = reinterpret_cast<float*>(pb + part_off[(size_t)p]);
-    const int q = x_src[(size_t)p];
-    if (q >= 0) {
-      d.x_part = reinterpret_cast<const float*>(pb + part_off[(size_t)q]) + x_r0[(size_t)p] / 32;
-      d.ld_xpart = n_part[(size_t)q];
+    if (s.in_mode == kInQ8K) {
+      d.xq = static_cast<const uint8_t*>(s.x);
+    } else {
+      const Source& src = xin[(size_t)p];
+      if (src.src >= 0) {
+        d.x_ll = ll + off_y[(size_t)src.src] + src.r0;
+        d.ld_xll = ld_yll[(size_t)src.src];
+        if (s.in_mode == kInF32Rms) {
+          d.xs_ll = ll + off_ys[(size_t)src.src] + src.r0 / 32;
+          d.ld_xsll = ld_ys[(size_t)src.src];
+        }
+      } else {
+        const Ext& e = ext[(size_t)src.ext];
+        d.x_ll = ll + e.off_ll;
+        d.ld_xll = e.ld_ll;
+        if (s.in_mode == kInF32Rms) {
+          d.xs_ll = ll + e.off_sums;
+          d.ld_xsll = e.ld_sums;
+        }
+      }
+    }
+    if (s.epi == kEpiResidual) {
+      const Source& src = rin[(size_t)p];
+      if (src.src >= 0) {
+        d.r_ll = ll + off_y[(size_t)src.src] + src.r0;
+        d.ld_rll = ld_yll[(size_t)src.src];
+      } else {
+        d.r_ll = ll + ext[(size_t)src.ext].off_ll;
+        d.ld_rll = ext[(size_t)src.ext].ld_ll;
+      }
     }
   }
+  std::vector<CopyDev> hc(ext.size());
+  for (size_t e = 0; e < ext.size(); ++e) {
+    CopyDev& c = hc[e];
+    c.src = ext[e].ptr;
+    c.ld_src = ext[e].ld;
+    c.dst = ll + ext[e].off_ll;
+    c.ld_dst = ext[e].ld_ll;
+    c.sums = ext[e].sums ? ll + ext[e].off_sums : nullptr;
+    c.ld_sums = ext[e].ld_sums;
+    c.len = ext[e].len;
+    c.units = (int64_t)T * ((ext[e].len + 31) / 32);
+  }
   if (cudaMemcpy(pr->d_phases, hp.data(), sizeof(PhaseDev) * (size_t)n, cudaMemcpyHostToDevice) != cudaSuccess ||
-      cudaMemset(pr->d_ctr, 0, sizeof(unsigned) * (size_t)pr->counter_words) != cudaSuccess) {
+      (!hc.empty() &&
+       cudaMemcpy(pr->d_copies, hc.data(), sizeof(CopyDev) * hc.size(), cudaMemcpyHostToDevice) != cudaSuccess) ||
+      cudaMemset(pr->d_ctl, 0, sizeof(unsigned) * 4) != cudaSuccess ||
+      cudaMemset(pr->d_ll, 0, 2 * set_bytes) != cudaSuccess) {
     const cudaError_t e = cudaGetLastError();
     q2k_program_free(pr);
     set_last_error("q2k_program: %s", cudaGetErrorString(e));
@@ -803,18 +1030,22 @@ int q2k_program_run(Q2KProgram* pr, cudaStream_t stream) {
   }
   ProgParams P;
   P.phases = pr->d_phases;
+  P.copies = pr->d_copies;
   P.n_phases = pr->n_phases;
+  P.n_copies = pr->n_copies;
   P.nb_max = pr->nb_max;
   P.eps = pr->eps;
   P.stages = pr->stages;
   P.log2_stages = 31 - __builtin_clz((unsigned)pr->stages);
-  P.l2_ahead = pr->l2_ahead;
-  P.ctr = pr->d_ctr;
+  P.ctl = pr->d_ctl;
   P.err = device_error_ptr();
   if (!P.err) {
     set_last_error("q2k_program_run: device error word unavailable");
     return kCudaError;
   }
+  P.timeout_ns = wait_timeout_ns();
+  P.set_bytes = (int64_t)pr->set_bytes;
+  P.tbufs = pr->tbufs;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)pr->grid);
   cfg.blockDim = dim3((unsigned)((pr->consumers + 1) * 32));
@@ -846,15 +1077,17 @@ int q2k_program_reset(Q2KProgram* pr, cudaStream_t stream) {
     set_last_error("q2k_program_reset: not a program handle");
     return kBadArgument;
   }
-  SMEAI_CUDA_TRY(cudaMemsetAsync(pr->d_ctr, 0, sizeof(unsigned) * (size_t)pr->counter_words, stream));
+  SMEAI_CUDA_TRY(cudaMemsetAsync(pr->d_ctl, 0, sizeof(unsigned) * 4, stream));
+  SMEAI_CUDA_TRY(cudaMemsetAsync(pr->d_ll, 0, 2 * pr->set_bytes, stream));
   return kOk;
 }
 
 void q2k_program_free(Q2KProgram* pr) {
   if (!pr || pr->magic != kProgramMagic) return;
   if (pr->d_phases) cudaFree(pr->d_phases);
-  if (pr->d_ctr) cudaFree(pr->d_ctr);
-  if (pr->d_parts) cudaFree(pr->d_parts);
+  if (pr->d_copies) cudaFree(pr->d_copies);
+  if (pr->d_ctl) cudaFree(pr->d_ctl);
+  if (pr->d_ll) cudaFree(pr->d_ll);
   pr->magic = 0;
   delete pr;
 }

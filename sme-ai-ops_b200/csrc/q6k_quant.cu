@@ -2,6 +2,7 @@
 // layout of q6k_core.cuh, and the block decoder (ggml dequantize_row_q6_K).
 #include "common.cuh"
 #include "kernels.h"
+#include "runtime.h"
 #include "q6k_core.cuh"
 
 namespace smeai {
@@ -94,7 +95,7 @@ int q6k_repack(const void* w_blocks_dev, int64_t n_rows, int64_t k, Q2KWeight* o
   }
   const size_t bytes = q6k_tile_bytes(n_rows, k);
   uint8_t* tiles = nullptr;
-  if (cudaMalloc(&tiles, bytes) != cudaSuccess) {
+  if (device_malloc((void**)&tiles, bytes) != cudaSuccess) {
     cudaGetLastError();
     set_last_error("q6k_repack: cudaMalloc of %zu bytes failed", bytes);
     return kAllocFailed;

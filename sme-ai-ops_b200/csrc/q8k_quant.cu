@@ -1,6 +1,7 @@
 // q8k_quant.cu -- standalone activation quantizer (fp32 -> ggml block_q8_K),
 // optionally preceded by an RMSNorm of the whole row
-// (sme_ai_library/src/sme_ai_ops.c:1060-1092: x / sqrt(mean(x^2) + eps)).
+// (sme_ai_library/src/sme_ai_ops.c:1060-1092: x / sqrt(mean(x^2) + eps), then
+// times weight[j] when a weight is given -- two roundings, as there).
 // The arithmetic lives in q8k_device.cuh; one warp quantizes one block.
 #include "common.cuh"
 #include "kernels.h"
@@ -26,7 +27,7 @@ __global__ void q8k_quantize_kernel(const float* __restrict__ x, int64_t ld_x, i
 
 // RMSNorm + quantization, one CTA per row.
 __global__ void rms_q8k_quantize_kernel(const float* __restrict__ x, int64_t ld_x, int nb, float eps,
-                                        uint8_t* __restrict__ y) {
+                                        const float* __restrict__ norm_w, uint8_t* __restrict__ y) {
   extern __shared__ float sm_gsum[];  // 8 group sums per block, then 1/rms
   pdl_trigger();
   pdl_wait();
@@ -51,6 +52,12 @@ __global__ void rms_q8k_quantize_kernel(const float* __restrict__ x, int64_t ld_
     load8(xr + b * QK_K + lane * 8, v);
 #pragma unroll
     for (int i = 0; i < 8; ++i) v[i] = __fmul_rn(v[i], inv);
+    if (norm_w) {
+      float g[8];
+      load8(norm_w + b * QK_K + lane * 8, g);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) v[i] = __fmul_rn(v[i], g[i]);
+    }
     q8k_store_global(q8k_quantize_lane(v), y + (row * nb + b) * Q8K_BLOCK_BYTES);
   }
 }
@@ -72,7 +79,7 @@ int q8k_quantize(const float* x, int64_t ld_x, int64_t n_rows, int64_t k, void* 
 }
 
 int rms_q8k_quantize(const float* x, int64_t ld_x, int64_t n_rows, int64_t k, float eps, void* y,
-                     cudaStream_t stream) {
+                     cudaStream_t stream, const float* norm_w) {
   if (k <= 0 || k % QK_K != 0 || n_rows <= 0 || ld_x < k || n_rows > 0x7fffffff) {
     set_last_error("rms_q8k_quantize: k must be a positive multiple of 256");
     return kBadArgument;
@@ -80,7 +87,7 @@ int rms_q8k_quantize(const float* x, int64_t ld_x, int64_t n_rows, int64_t k, fl
   const int nb = (int)(k / QK_K);
   const int threads = nb >= 16 ? 512 : (nb >= 8 ? 256 : 128);
   SMEAI_CUDA_TRY(launch(rms_q8k_quantize_kernel, dim3((unsigned)n_rows), dim3(threads), (size_t)(8 * nb + 1) * 4,
-                        stream, x, ld_x, nb, eps, static_cast<uint8_t*>(y)));
+                        stream, x, ld_x, nb, eps, norm_w, static_cast<uint8_t*>(y)));
   return kOk;
 }
 

@@ -4,6 +4,8 @@
 #include <stdlib.h>
 #include <string.h>
 
+#include <atomic>
+
 #include "common.cuh"
 #include "runtime.h"
 
@@ -21,6 +23,37 @@ void set_last_error(const char* fmt, ...) {
 }
 
 const char* last_error() { return g_last_error; }
+
+namespace {
+std::atomic<int> g_fail_allocs{0};
+std::atomic<uint64_t> g_wait_ns{0}, g_peer_wait_ns{0};
+}  // namespace
+
+void fail_next_allocs(int n) { g_fail_allocs.store(n < 0 ? 0 : n); }
+
+cudaError_t device_malloc(void** p, size_t bytes) {
+  int left = g_fail_allocs.load();
+  while (left > 0 && !g_fail_allocs.compare_exchange_weak(left, left - 1)) {
+  }
+  if (left > 0) {
+    *p = nullptr;
+    return cudaErrorMemoryAllocation;
+  }
+  return cudaMalloc(p, bytes);
+}
+
+void set_wait_timeouts(uint64_t local_ns, uint64_t peer_ns) {
+  g_wait_ns.store(local_ns);
+  g_peer_wait_ns.store(peer_ns);
+}
+uint64_t wait_timeout_ns() {
+  const uint64_t v = g_wait_ns.load();
+  return v ? v : kDefaultWaitNs;
+}
+uint64_t peer_wait_timeout_ns() {
+  const uint64_t v = g_peer_wait_ns.load();
+  return v ? v : kDefaultPeerWaitNs;
+}
 
 bool pdl_enabled() {
   static int enabled = -1;
@@ -94,7 +127,7 @@ int DeviceBuffer::reserve(size_t bytes) {
   ptr = nullptr;
   cap = 0;
   size_t want = bytes < 256 ? 256 : bytes;
-  if (cudaMalloc(&ptr, want) != cudaSuccess) {
+  if (device_malloc(&ptr, want) != cudaSuccess) {
     cudaGetLastError();
     ptr = nullptr;
     set_last_error("cudaMalloc of %zu bytes failed", want);

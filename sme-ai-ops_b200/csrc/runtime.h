@@ -9,6 +9,13 @@ namespace smeai {
 bool device_ready();
 bool is_device_pointer(const void* p);
 
+// Every device allocation of the library goes through device_malloc.  The
+// test hook fail_next_allocs(n) makes the next n calls fail as cudaMalloc
+// does when the device is out of memory, so the entry points' ALLOC_FAILED
+// paths can be exercised without exhausting a real GPU.
+cudaError_t device_malloc(void** p, size_t bytes);
+void fail_next_allocs(int n);
+
 // A growable device allocation (never shrinks).
 struct DeviceBuffer {
   void* ptr = nullptr;

@@ -57,7 +57,8 @@ class Q2KPhase(ctypes.Structure):
     """smeai_q2k_phase: one GEMV of a decode program."""
     _fields_ = [("w", ctypes.c_void_p), ("input", ctypes.c_int), ("x", ctypes.c_void_p),
                 ("ld_x", ctypes.c_size_t), ("y", ctypes.c_void_p), ("ldy", ctypes.c_size_t),
-                ("epilogue", ctypes.c_int), ("resid", ctypes.c_void_p), ("ld_resid", ctypes.c_size_t)]
+                ("epilogue", ctypes.c_int), ("resid", ctypes.c_void_p), ("ld_resid", ctypes.c_size_t),
+                ("norm_w", ctypes.c_void_p)]
 
 
 class PeerExchange(ctypes.Structure):
@@ -80,6 +81,8 @@ def _declare(L: ctypes.CDLL) -> None:
         "smeai_device_ready": (I, []),
         "smeai_last_error": (ctypes.c_char_p, []),
         "smeai_take_device_error": (I, [ctypes.POINTER(ctypes.c_uint)]),
+        "smeai_set_wait_timeouts": (None, [U64, U64]),
+        "smeai_debug_fail_next_allocs": (None, [I]),
         "smeai_q2k_repack": (I, [P, I64, I64, ctypes.POINTER(ctypes.c_void_p)]),
         "dequantize_row_q3_K": (None, [P, P, I64]),
         "ggml_vec_dot_q3_K_q8_K": (None, [I, P, SZ, P, SZ, P, SZ, I]),
@@ -122,12 +125,15 @@ def _declare(L: ctypes.CDLL) -> None:
         "smeai_q2k_weight_bytes": (SZ, [P]),
         "smeai_q8k_quantize": (I, [P, I64, I64, I64, P, P]),
         "smeai_rms_q8k_quantize": (I, [P, I64, I64, I64, F, P, P]),
+        "smeai_rms_q8k_quantize_w": (I, [P, I64, I64, I64, P, F, P, P]),
         "smeai_q2k_mul_mat": (I, [P, I64, I64, P, I64, P, SZ, P]),
         "smeai_q2k_mul_mat_ex": (I, [P, P, I64, P, SZ, I, P, SZ, P]),
         "smeai_q2k_mul_mat_tc": (I, [P, P, I64, P, SZ, P]),
+        "smeai_q2k_mul_mat_tc_ex": (I, [P, P, I64, P, SZ, I, P, SZ, P]),
         "smeai_q2k_mul_mat_f32": (I, [P, P, I64, P, SZ, P]),
         "smeai_q2k_mul_mat_f32_ex": (I, [P, P, SZ, I64, P, SZ, I, P, SZ, F, P]),
-        "smeai_q2k_mul_mat_f32_peer": (I, [P, P, SZ, I64, P, SZ, I, P, SZ, F, ctypes.POINTER(PeerExchange), P]),
+        "smeai_q2k_mul_mat_f32_norm": (I, [P, P, SZ, I64, P, SZ, I, P, SZ, F, P, P]),
+        "smeai_q2k_mul_mat_f32_peer": (I, [P, P, SZ, I64, P, SZ, I, P, SZ, F, P, ctypes.POINTER(PeerExchange), P]),
         "smeai_peer_step_end": (I, [P, ctypes.c_uint, P, P]),
         "smeai_ipc_alloc": (I, [SZ, ctypes.POINTER(ctypes.c_void_p), P]),
         "smeai_ipc_free": (None, [P]),

@@ -29,14 +29,21 @@ def quantize_q8k(x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tens
     return out
 
 
-def rms_quantize_q8k(x: torch.Tensor, eps: float, out: torch.Tensor | None = None) -> torch.Tensor:
+def rms_quantize_q8k(x: torch.Tensor, eps: float, out: torch.Tensor | None = None,
+                     norm_w: torch.Tensor | None = None) -> torch.Tensor:
+    """RMSNorm of each row (times norm_w when given), then Q8_K."""
     x2 = x.reshape(-1, x.shape[-1])
     n, k = x2.shape
     assert x2.dtype == torch.float32 and x2.is_cuda and x2.stride(1) == 1
     if out is None:
         out = torch.empty((n, k // QK_K * Q8K_BLOCK_BYTES), dtype=torch.uint8, device=x.device)
-    check(lib().smeai_rms_q8k_quantize(_ptr(x2), x2.stride(0), n, k, ctypes.c_float(eps), _ptr(out),
-                                        cur_stream()), "rms_q8k_quantize")
+    if norm_w is None:
+        check(lib().smeai_rms_q8k_quantize(_ptr(x2), x2.stride(0), n, k, ctypes.c_float(eps), _ptr(out),
+                                            cur_stream()), "rms_q8k_quantize")
+    else:
+        assert norm_w.dtype == torch.float32 and norm_w.is_cuda and norm_w.numel() == k and norm_w.is_contiguous()
+        check(lib().smeai_rms_q8k_quantize_w(_ptr(x2), x2.stride(0), n, k, _ptr(norm_w), ctypes.c_float(eps),
+                                              _ptr(out), cur_stream()), "rms_q8k_quantize_w")
     return out
 
 
@@ -105,12 +112,20 @@ class Q2KMatrix:
         check(st, "q2k_mul_mat")
         return out
 
-    def mul_mat_tc(self, xq: torch.Tensor, n_cols: int, out: torch.Tensor | None = None) -> torch.Tensor:
-        """The tensor-core GEMM path (any number of activation rows)."""
+    def mul_mat_tc(self, xq: torch.Tensor, n_cols: int, out: torch.Tensor | None = None,
+                   epilogue: int = EPI_STORE, resid: torch.Tensor | None = None) -> torch.Tensor:
+        """The tensor-core GEMM path (any number of activation rows), with the
+        GEMV's epilogues."""
+        out_rows = self.n_rows // 2 if epilogue == EPI_SILU_MUL else self.n_rows
         if out is None:
-            out = torch.empty((n_cols, self.n_rows), dtype=torch.float32, device=xq.device)
-        check(lib().smeai_q2k_mul_mat_tc(self.handle, _ptr(xq), n_cols, _ptr(out), out.stride(0), cur_stream()),
-              "q2k_mul_mat_tc")
+            out = torch.empty((n_cols, out_rows), dtype=torch.float32, device=xq.device)
+        if epilogue == EPI_STORE:
+            check(lib().smeai_q2k_mul_mat_tc(self.handle, _ptr(xq), n_cols, _ptr(out), out.stride(0),
+                                             cur_stream()), "q2k_mul_mat_tc")
+        else:
+            ldr = 0 if resid is None else resid.stride(0)
+            check(lib().smeai_q2k_mul_mat_tc_ex(self.handle, _ptr(xq), n_cols, _ptr(out), out.stride(0), epilogue,
+                                                _ptr(resid), ldr, cur_stream()), "q2k_mul_mat_tc_ex")
         return out
 
     def mul_mat_f32(self, x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
@@ -124,9 +139,10 @@ class Q2KMatrix:
 
     def mul_mat_f32_ex(self, x: torch.Tensor, n_cols: int, out: torch.Tensor | None = None,
                        epilogue: int = EPI_STORE, resid: torch.Tensor | None = None,
-                       rms_eps: float | None = None) -> torch.Tensor:
+                       rms_eps: float | None = None, norm_w: torch.Tensor | None = None) -> torch.Tensor:
         """fp32 activations [n_cols, >=k] (row stride x.stride(0)), quantized to
-        Q8_K (after an RMSNorm when rms_eps is given) inside the GEMV."""
+        Q8_K (after an RMSNorm when rms_eps is given, times norm_w when given)
+        inside the GEMV."""
         out_rows = self.n_rows // 2 if epilogue == EPI_SILU_MUL else self.n_rows
         if out is None:
             out = torch.empty((n_cols, out_rows), dtype=torch.float32, device=x.device)
@@ -135,13 +151,14 @@ class Q2KMatrix:
         ldy = out.stride(0) if out.dim() == 2 else out_rows
         ldr = 0 if resid is None else (resid.stride(0) if resid.dim() == 2 else out_rows)
         eps = -1.0 if rms_eps is None else float(rms_eps)
-        check(lib().smeai_q2k_mul_mat_f32_ex(self.handle, _ptr(x), ld_x, n_cols, _ptr(out), ldy, epilogue,
-                                             _ptr(resid), ldr, ctypes.c_float(eps), cur_stream()),
-              "q2k_mul_mat_f32_ex")
+        check(lib().smeai_q2k_mul_mat_f32_norm(self.handle, _ptr(x), ld_x, n_cols, _ptr(out), ldy, epilogue,
+                                               _ptr(resid), ldr, ctypes.c_float(eps), _ptr(norm_w), cur_stream()),
+              "q2k_mul_mat_f32_norm")
         return out
 
     def mul_mat_f32_peer(self, x: torch.Tensor, n_cols: int, out: torch.Tensor, ex, epilogue: int = EPI_STORE,
-                         resid: torch.Tensor | None = None, rms_eps: float | None = None) -> torch.Tensor:
+                         resid: torch.Tensor | None = None, rms_eps: float | None = None,
+                         norm_w: torch.Tensor | None = None) -> torch.Tensor:
         """mul_mat_f32_ex with the fused cross-GPU exchange `ex` (a PeerExchange)."""
         out_rows = self.n_rows // 2 if epilogue == EPI_SILU_MUL else self.n_rows
         assert x.dtype == torch.float32 and x.stride(-1) == 1
@@ -150,8 +167,8 @@ class Q2KMatrix:
         ldr = 0 if resid is None else (resid.stride(0) if resid.dim() == 2 else out_rows)
         eps = -1.0 if rms_eps is None else float(rms_eps)
         check(lib().smeai_q2k_mul_mat_f32_peer(self.handle, _ptr(x), ld_x, n_cols, _ptr(out), ldy, epilogue,
-                                               _ptr(resid), ldr, ctypes.c_float(eps), ctypes.byref(ex),
-                                               cur_stream()), "q2k_mul_mat_f32_peer")
+                                               _ptr(resid), ldr, ctypes.c_float(eps), _ptr(norm_w),
+                                               ctypes.byref(ex), cur_stream()), "q2k_mul_mat_f32_peer")
         return out
 
     def block_sums(self, xq: torch.Tensor):
@@ -313,7 +330,8 @@ def dequantize_q6k(blocks: torch.Tensor, k_total: int) -> torch.Tensor:
 class Q2KProgram:
     """A chain of GEMV phases run as one persistent kernel
     (smeai_q2k_program_*).  phases: dicts with keys w (Q2KMatrix), x (tensor),
-    input (IN_Q8K / IN_F32 / IN_F32_RMS), y (tensor), epilogue, resid.  Phase p
+    input (IN_Q8K / IN_F32 / IN_F32_RMS), y (tensor), epilogue, resid, norm_w
+    (the RMSNorm weight of an IN_F32_RMS input).  Phase p
     must read phase p-1's complete output.  The tensors must stay alive (and
     in place) while the program exists."""
 
@@ -336,7 +354,9 @@ class Q2KProgram:
             arr[i].epilogue = epi
             arr[i].resid = 0 if resid is None else resid.data_ptr()
             arr[i].ld_resid = 0 if resid is None else (resid.stride(0) if resid.dim() == 2 else out_rows)
-            self._keep += [w, x, y, resid]
+            nw = ph.get("norm_w")
+            arr[i].norm_w = 0 if nw is None else nw.data_ptr()
+            self._keep += [w, x, y, resid, nw]
         h = ctypes.c_void_p()
         check(lib().smeai_q2k_program_create(arr, len(phases), n_cols, ctypes.c_float(rms_eps), ctypes.byref(h)),
               "q2k_program_create")

@@ -1,16 +1,18 @@
 """Llama-2-7B-shape Q2_K linear stack (the decode/prefill benchmark workload).
 
-Per layer, with the inputs of every linear re-quantized to Q8_K:
-    xq  = Q8_K(rmsnorm(x))
+Per layer, with the inputs of every linear re-quantized to Q8_K (rmsnorm
+includes the layer's norm weight, as sme_ai_rmsnorm_f32 and llama's
+attn_norm / ffn_norm / output_norm do):
+    xq  = Q8_K(rmsnorm(x) * attn_norm)
     qkv = [Wq; Wk; Wv] xq                       (one fused GEMV, 3 x 4096 rows)
     v   = qkv[v]   -- attention over a single position returns v itself, so
                       the attention math is skipped without changing shapes
     x   = x + Wo Q8_K(v)                        (residual fused in the epilogue)
-    h   = silu(Wg xq') * (Wu xq'),  xq' = Q8_K(rmsnorm(x))
+    h   = silu(Wg xq') * (Wu xq'),  xq' = Q8_K(rmsnorm(x) * ffn_norm)
                                                 (gate/up rows interleaved, one GEMV
                                                  with the silu*mul epilogue)
     x   = x + Wd Q8_K(h)
-then logits = Wlm Q8_K(rmsnorm(x)).
+then logits = Wlm Q8_K(rmsnorm(x) * output_norm).
 
 Multi-GPU: every weight is row-sharded over the ranks (32-row aligned slices
 of each of Wq/Wk/Wv/Wo/Wg/Wu/Wd/Wlm); activations are replicated and each
@@ -74,7 +76,8 @@ def gemv_bytes(rows: int, k: int, cols: int, out_rows: int | None = None) -> int
 
 class Q2KDecodeStack:
     def __init__(self, n_layers=32, hidden=4096, ffn=11008, vocab=32000, batch=1, rank=0, world=1,
-                 device=None, seed=0, std=0.02, eps=1e-5, group=None, keep_blocks=False, quant="separate"):
+                 device=None, seed=0, std=0.02, eps=1e-5, group=None, keep_blocks=False, quant="separate",
+                 norm_weights=True):
         self.L, self.H, self.F, self.V = n_layers, hidden, ffn, vocab
         self.B, self.rank, self.world, self.eps, self.group = batch, rank, world, eps, group
         # where each linear's input is quantized to Q8_K: "fused" = inside the
@@ -87,8 +90,11 @@ class Q2KDecodeStack:
         # all ranks' copies of the next input and signals them in the same kernel
         # (the all-gather fused in, over CUDA-IPC peer memory); the next GEMV waits
         # for every rank's rows.  Falls back to "separate" + NCCL when a shard is
-        # not 32-row aligned or the peers cannot be mapped.
-        assert quant in ("fused", "separate", "mixed", "program", "peer")
+        # not 32-row aligned or the peers cannot be mapped.  "tc" (prefill, any
+        # batch): every linear on the tensor-core GEMM with the same epilogues,
+        # the quantizers as separate kernels -- same bits as the GEMV placements;
+        # on N GPUs its slices are all-gathered over NCCL.
+        assert quant in ("fused", "separate", "mixed", "program", "peer", "tc")
         if quant in ("program", "peer") and world > 1:
             aligned = all((shard_range(hidden, q, world)[1] - shard_range(hidden, q, world)[0]) % 32 == 0
                           for q in range(world))
@@ -125,6 +131,15 @@ class Q2KDecodeStack:
             self.layers.append((wqkv, wo, wgu, wd))
             self.weight_bytes += wqkv.n_rows * wqkv.nb * 84 + wo.n_rows * wo.nb * 84 + \
                 wgu.n_rows * wgu.nb * 84 + wd.n_rows * wd.nb * 84
+        # RMSNorm weights (attn_norm, ffn_norm per layer, output_norm): seeded
+        # draws around 1, replicated on every rank; None = no weight
+        self.attn_norm, self.ffn_norm, self.out_norm = [None] * n_layers, [None] * n_layers, None
+        if norm_weights:
+            gn = torch.Generator(device=self.dev).manual_seed(seed * 7919 + 31)
+            nw = lambda: 1.0 + 0.1 * torch.randn(hidden, generator=gn, device=self.dev)
+            self.attn_norm = [nw() for _ in range(n_layers)]
+            self.ffn_norm = [nw() for _ in range(n_layers)]
+            self.out_norm = nw()
         lm_b = self._draw(seed, n_layers, 7, vocab, hidden, self.v_lo, self.v_hi, std)
         self.lm = Q.Q2KMatrix(lm_b, vs, hidden)
         self.lm_blocks = lm_b if keep_blocks else None
@@ -205,26 +220,34 @@ class Q2KDecodeStack:
         from . import check, lib
         B, e = self.B, self.eps
         xs = self.x[:, self.h_lo:self.h_hi]
-        for (wqkv, wo, wgu, wd), (eq, eo, egu, ed) in zip(self.layers, self.ex):
-            wqkv.mul_mat_f32_peer(self.x, B, self.qkv, eq, rms_eps=e)
+        for li, ((wqkv, wo, wgu, wd), (eq, eo, egu, ed)) in enumerate(zip(self.layers, self.ex)):
+            wqkv.mul_mat_f32_peer(self.x, B, self.qkv, eq, rms_eps=e, norm_w=self.attn_norm[li])
             wo.mul_mat_f32_peer(self.v_full, B, xs, eo, EPI_RESIDUAL, resid=xs)
-            wgu.mul_mat_f32_peer(self.x, B, self.h_full[:, self.f_lo:self.f_hi], egu, EPI_SILU_MUL, rms_eps=e)
+            wgu.mul_mat_f32_peer(self.x, B, self.h_full[:, self.f_lo:self.f_hi], egu, EPI_SILU_MUL, rms_eps=e,
+                                 norm_w=self.ffn_norm[li])
             wd.mul_mat_f32_peer(self.h_full, B, xs, ed, EPI_RESIDUAL, resid=xs)
-        self.lm.mul_mat_f32_peer(self.x, B, self.logits[:, self.v_lo:self.v_hi], self.ex_lm, rms_eps=e)
+        self.lm.mul_mat_f32_peer(self.x, B, self.logits[:, self.v_lo:self.v_hi], self.ex_lm, rms_eps=e,
+                                 norm_w=self.out_norm)
         sig, count, epoch = self.end
         check(lib().smeai_peer_step_end(sig, count, epoch, Q.cur_stream()), "peer_step_end")
         return self.logits
 
     # --------------------------------------------------------------- one token
-    def _lin(self, m, x, out, epilogue=EPI_STORE, resid=None, rms=False, qbuf=None):
-        """One linear: y = W Q8_K([rmsnorm] x) with the stack's quantization placement."""
+    def _lin(self, m, x, out, epilogue=EPI_STORE, resid=None, rms=False, qbuf=None, norm_w=None):
+        """One linear: y = W Q8_K([rmsnorm * norm_w] x) with the stack's quantization placement."""
         fused = self.quant == "fused" or (self.quant == "mixed" and rms)
-        if fused:
+        if self.quant == "tc":
+            if rms:
+                Q.rms_quantize_q8k(x, self.eps, out=qbuf, norm_w=norm_w)
+            else:
+                Q.quantize_q8k(x, out=qbuf)
+            m.mul_mat_tc(qbuf, self.B, out=out, epilogue=epilogue, resid=resid)
+        elif fused:
             m.mul_mat_f32_ex(x, self.B, out=out, epilogue=epilogue, resid=resid,
-                             rms_eps=self.eps if rms else None)
+                             rms_eps=self.eps if rms else None, norm_w=norm_w if rms else None)
         else:
             if rms:
-                Q.rms_quantize_q8k(x, self.eps, out=qbuf)
+                Q.rms_quantize_q8k(x, self.eps, out=qbuf, norm_w=norm_w)
             else:
                 Q.quantize_q8k(x, out=qbuf)
             m.mul_mat(qbuf, self.B, out=out, epilogue=epilogue, resid=resid)
@@ -242,25 +265,26 @@ class Q2KDecodeStack:
         if self.quant == "peer":
             return self._step_peer()
         L = self._lin
-        for wqkv, wo, wgu, wd in self.layers:
-            L(wqkv, self.x, self.qkv, rms=True, qbuf=self.xq)
+        for li, (wqkv, wo, wgu, wd) in enumerate(self.layers):
+            an, fn = self.attn_norm[li], self.ffn_norm[li]
+            L(wqkv, self.x, self.qkv, rms=True, qbuf=self.xq, norm_w=an)
             v_loc = self.qkv[:, 2 * hs:3 * hs]
             if one:
                 L(wo, v_loc, self.x, EPI_RESIDUAL, self.x, qbuf=self.vq)
-                L(wgu, self.x, self.h_full, EPI_SILU_MUL, rms=True, qbuf=self.xq)
+                L(wgu, self.x, self.h_full, EPI_SILU_MUL, rms=True, qbuf=self.xq, norm_w=fn)
                 L(wd, self.h_full, self.x, EPI_RESIDUAL, self.x, qbuf=self.hq)
             else:
                 self._gather(self.v_full, v_loc.contiguous(), self.h_lo, self.h_hi)
                 L(wo, self.v_full, self.x_loc, EPI_RESIDUAL, self.x[:, self.h_lo:self.h_hi], qbuf=self.vq)
                 self._gather(self.x, self.x_loc, self.h_lo, self.h_hi)
-                L(wgu, self.x, self.h_loc, EPI_SILU_MUL, rms=True, qbuf=self.xq)
+                L(wgu, self.x, self.h_loc, EPI_SILU_MUL, rms=True, qbuf=self.xq, norm_w=fn)
                 self._gather(self.h_full, self.h_loc, self.f_lo, self.f_hi)
                 L(wd, self.h_full, self.x_loc, EPI_RESIDUAL, self.x[:, self.h_lo:self.h_hi], qbuf=self.hq)
                 self._gather(self.x, self.x_loc, self.h_lo, self.h_hi)
         if one:
-            L(self.lm, self.x, self.logits, rms=True, qbuf=self.xq)
+            L(self.lm, self.x, self.logits, rms=True, qbuf=self.xq, norm_w=self.out_norm)
         else:
-            L(self.lm, self.x, self.lg_loc, rms=True, qbuf=self.xq)
+            L(self.lm, self.x, self.lg_loc, rms=True, qbuf=self.xq, norm_w=self.out_norm)
             self._gather(self.logits, self.lg_loc, self.v_lo, self.v_hi)
         return self.logits
 
@@ -268,18 +292,24 @@ class Q2KDecodeStack:
         from . import IN_F32, IN_F32_RMS
         hs = self.hs
         phases = []
-        for wqkv, wo, wgu, wd in self.layers:
+        for li, (wqkv, wo, wgu, wd) in enumerate(self.layers):
             phases += [
-                dict(w=wqkv, x=self.x, input=IN_F32_RMS, y=self.qkv),
+                dict(w=wqkv, x=self.x, input=IN_F32_RMS, y=self.qkv, norm_w=self.attn_norm[li]),
                 dict(w=wo, x=self.qkv[:, 2 * hs:3 * hs], input=IN_F32, y=self.x, epilogue=EPI_RESIDUAL,
                      resid=self.x),
-                dict(w=wgu, x=self.x, input=IN_F32_RMS, y=self.h_full, epilogue=EPI_SILU_MUL),
+                dict(w=wgu, x=self.x, input=IN_F32_RMS, y=self.h_full, epilogue=EPI_SILU_MUL,
+                     norm_w=self.ffn_norm[li]),
                 dict(w=wd, x=self.h_full, input=IN_F32, y=self.x, epilogue=EPI_RESIDUAL, resid=self.x),
             ]
-        phases.append(dict(w=self.lm, x=self.x, input=IN_F32_RMS, y=self.logits))
+        phases.append(dict(w=self.lm, x=self.x, input=IN_F32_RMS, y=self.logits, norm_w=self.out_norm))
         return Q.Q2KProgram(phases, self.B, rms_eps=self.eps)
 
     # --------------------------------------------------------------- accounting
+    def ops_per_step(self) -> int:
+        """Integer multiply-adds x 2 of every linear in a step on this rank
+        (the tensor-core roofline's unit)."""
+        return sum(2 * self.B * m.n_rows * m.k for _, m in self.gemv_list())
+
     def launches_per_step(self) -> int:
         """Kernels of this library per step: one GEMV per linear (the batch is
         split into launches of 8, 4, 2, 1 tokens) plus one quantizer per
@@ -288,6 +318,8 @@ class Q2KDecodeStack:
             return 1
         if self.quant == "peer":
             return self.L * 4 + 2          # the GEMVs and the step-end kernel
+        if self.quant == "tc":             # per linear: quantizer, operand prepass, GEMM
+            return (self.L * 4 + 1) * 3
         chunks = self.B // 8 + bin(self.B % 8).count("1")
         per_layer = {"fused": 0, "separate": 4, "mixed": 2}[self.quant]
         return (self.L * 4 + 1) * chunks + self.L * per_layer + (1 if self.quant == "separate" else 0)

@@ -66,6 +66,27 @@ def test_rms_q8k_bit_exact(cuda, oracle, rows, k):
         assert np.array_equal(got[r], exp), r
 
 
+@pytest.mark.parametrize("rows,k", [(1, 4096), (3, 11008), (2, 512)])
+def test_rms_q8k_weighted_bit_exact(cuda, oracle, rows, k):
+    """RMSNorm with the reference's weight operand (sme_ai_rmsnorm_f32:
+    (x * inv_rms) * weight[j], each product rounded), then Q8_K."""
+    rng = np.random.default_rng(k + 3 * rows)
+    x = rng.standard_normal((rows, k)).astype(np.float32) * 3
+    w = (1.0 + 0.25 * rng.standard_normal(k)).astype(np.float32)
+    w[:7] = 0.0                                  # zero weights: quants 0 there
+    w[7] = -2.5                                  # a negative weight flips the sign
+    got = Q.rms_quantize_q8k(torch.from_numpy(x).to(cuda), 1e-5,
+                             norm_w=torch.from_numpy(w).to(cuda)).cpu().numpy().reshape(rows, -1)
+    for r in range(rows):
+        exp = q8k_bytes(oracle.rmsnorm_quantize_q8_K(x[r], 1e-5, weight=w))
+        assert np.array_equal(got[r], exp), r
+    # a unit weight gives the unweighted blocks
+    ones = torch.ones(k, device=cuda)
+    a = Q.rms_quantize_q8k(torch.from_numpy(x).to(cuda), 1e-5, norm_w=ones)
+    b = Q.rms_quantize_q8k(torch.from_numpy(x).to(cuda), 1e-5)
+    assert torch.equal(a, b)
+
+
 def test_q2k_quantize_bit_exact(cuda, oracle):
     rng = np.random.default_rng(4)
     x = (rng.standard_normal(64 * 4096) * 0.02).astype(np.float32)
@@ -286,6 +307,10 @@ def test_fused_prologue_bit_identical(cuda, rows, k, cols):
     r = torch.randn((cols, rows), generator=g, device=cuda)
     y_res = m.mul_mat_f32_ex(x, cols, out=r.clone(), epilogue=S.EPI_RESIDUAL, resid=r, rms_eps=1e-5)
     assert torch.equal(y_res, r + y_two)
+    nw = 1.0 + 0.3 * torch.randn(k, generator=g, device=cuda)       # RMSNorm weight
+    y_two = m.mul_mat(Q.rms_quantize_q8k(x.contiguous(), 1e-5, norm_w=nw), cols)
+    y_one = m.mul_mat_f32_ex(x, cols, rms_eps=1e-5, norm_w=nw)
+    assert torch.equal(y_one, y_two)
     assert torch.equal(m.mul_mat_f32(x.contiguous()), m.mul_mat(Q.quantize_q8k(x.contiguous()), cols))
 
 

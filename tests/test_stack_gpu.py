@@ -15,16 +15,17 @@ def oracle_stack(O, st: Q2KDecodeStack, x0: np.ndarray):
     B2 = lambda t: t.cpu().numpy().reshape(-1).view(O.BLOCK_Q2_K)
     H, F, V = st.H, st.F, st.V
     x = x0.astype(np.float32).copy()
-    for blk in st.blocks:
-        xq = O.rmsnorm_quantize_q8_K(x, st.eps)
+    nw = lambda t: None if t is None else t.cpu().numpy()
+    for li, blk in enumerate(st.blocks):
+        xq = O.rmsnorm_quantize_q8_K(x, st.eps, weight=nw(st.attn_norm[li]))
         v = O.q2k_mul_mat(B2(blk["v"]), H, H, xq, 1, n_threads=8)[0]
         x = (x + O.q2k_mul_mat(B2(blk["o"]), H, H, O.quantize_q8_K(v), 1, n_threads=8)[0]).astype(np.float32)
-        xq = O.rmsnorm_quantize_q8_K(x, st.eps)
+        xq = O.rmsnorm_quantize_q8_K(x, st.eps, weight=nw(st.ffn_norm[li]))
         g = O.q2k_mul_mat(B2(blk["g"]), F, H, xq, 1, n_threads=8)[0]
         u = O.q2k_mul_mat(B2(blk["u"]), F, H, xq, 1, n_threads=8)[0]
         h = O.silu_mul(g, u)
         x = (x + O.q2k_mul_mat(B2(blk["d"]), H, F, O.quantize_q8_K(h), 1, n_threads=8)[0]).astype(np.float32)
-    xq = O.rmsnorm_quantize_q8_K(x, st.eps)
+    xq = O.rmsnorm_quantize_q8_K(x, st.eps, weight=nw(st.out_norm))
     return O.q2k_mul_mat(B2(st.lm_blocks), V, H, xq, 1, n_threads=8)[0]
 
 
@@ -39,6 +40,25 @@ def test_stack_matches_oracle(cuda, oracle):
     # Q8_K code, so the stack is held to a relative bar, not bit identity
     scale = np.abs(exp).max()
     assert np.abs(got - exp).max() <= 1e-3 * scale
+
+
+def test_full_shape_layer_and_lm_head_match_oracle(cuda, oracle):
+    """One layer at the 7B shape (hidden 4096, ffn 11008, RMSNorm weights) and
+    the 32000 x 4096 lm_head, step by step against the oracle; the one-kernel
+    program gives the separate launches' bits."""
+    st = Q2KDecodeStack(n_layers=1, hidden=4096, ffn=11008, vocab=32000, device=cuda, seed=11, keep_blocks=True,
+                        quant="separate")
+    logits = st.step().clone()
+    torch.cuda.synchronize()
+    exp = oracle_stack(oracle, st, st.x0.cpu().numpy()[0])
+    got = logits.cpu().numpy()[0]
+    assert np.isfinite(got).all()
+    scale = np.abs(exp).max()
+    assert np.abs(got - exp).max() <= 1e-3 * scale
+    st.quant = "program"
+    assert torch.equal(st.step(), logits)
+    assert torch.equal(st.step(), logits)
+    st.free()
 
 
 @pytest.mark.parametrize("quant", ["fused", "separate", "mixed", "program"])
@@ -132,3 +152,36 @@ def test_program_rejects_bad_phases(cuda):
         Q.Q2KProgram([dict(w=m, x=x[:2], input=IN_F32, y=y[:2], epilogue=S.EPI_RESIDUAL)], 2)
     with pytest.raises(RuntimeError):      # input rows shorter than k
         Q.Q2KProgram([dict(w=m, x=torch.zeros((2, 256), device=cuda), input=IN_F32, y=y[:2])], 2)
+
+
+@pytest.mark.parametrize("batch", [8, 130])
+def test_prefill_stack_on_tensor_cores_matches_decode_stack(cuda, batch):
+    """The stack over `batch` tokens with every linear on the tcgen05 GEMM
+    (residual and silu*mul in its epilogue) gives the GEMV stack's bits:
+    tokens are independent (attention over one position), and the GEMM, its
+    epilogues and the quantizers equal the decode path's."""
+    kw = dict(n_layers=2, hidden=1024, ffn=2816, vocab=2048, batch=batch, device=cuda, seed=21)
+    ref = Q2KDecodeStack(quant="fused", **kw)
+    a = ref.step().clone()
+    st = Q2KDecodeStack(quant="tc", **kw)
+    b = st.step()
+    torch.cuda.synchronize()
+    assert torch.equal(b, a)
+    assert torch.isfinite(b).all()
+
+
+def test_tc_gemm_epilogues_match_gemv(cuda):
+    from smeai_b200 import q2k as Q
+    g = torch.Generator(device=cuda).manual_seed(8)
+    rows, k, cols = 600, 1024, 37
+    m = Q.Q2KMatrix(Q.quantize_q2k(torch.randn((rows, k), generator=g, device=cuda) * 0.02), rows, k)
+    xq = Q.quantize_q8k(torch.randn((cols, k), generator=g, device=cuda))
+    r = torch.randn((cols, rows), generator=g, device=cuda)
+    assert torch.equal(m.mul_mat_tc(xq, cols), m.mul_mat(xq, cols))
+    assert torch.equal(m.mul_mat_tc(xq, cols, epilogue=S.EPI_RESIDUAL, resid=r),
+                       m.mul_mat(xq, cols, epilogue=S.EPI_RESIDUAL, resid=r))
+    y = r.clone()                                  # in place: resid aliases the output
+    m.mul_mat_tc(xq, cols, out=y, epilogue=S.EPI_RESIDUAL, resid=y)
+    assert torch.equal(y, m.mul_mat(xq, cols, epilogue=S.EPI_RESIDUAL, resid=r))
+    assert torch.equal(m.mul_mat_tc(xq, cols, epilogue=S.EPI_SILU_MUL),
+                       m.mul_mat(xq, cols, epilogue=S.EPI_SILU_MUL))

@@ -17,7 +17,10 @@ import smeai_b200 as S
 
 pytestmark = pytest.mark.gpu
 P = ctypes.c_void_p
-SWIGLU_ATOL = 1e-3   # the bar tests/test_linear_gpu.py holds SwiGLU to
+# Both entry points run the same two kernels in the same order (gate/up with
+# the silu*mul and fp16 rounding of the hidden state, then the down Linear),
+# so their outputs must agree bit for bit.
+LIMIT = 512 * 1024   # fp16 values of the fixed scratch (batch * hidden_features)
 
 
 def _host(a):
@@ -32,7 +35,7 @@ def _half_bits(rng, n, scale=0.5):
     return (rng.uniform(-scale, scale, n).astype(np.float16)).view(np.uint16)
 
 
-@pytest.mark.parametrize("B,K,H,N", [(4, 128, 256, 128), (8, 512, 1376, 512)])
+@pytest.mark.parametrize("B,K,H,N", [(4, 128, 256, 128), (8, 512, 1376, 512), (128, 64, 4096, 64)])
 def test_noalloc_swiglu_matches_allocating_entry(cuda, B, K, H, N):
     L = S.lib()
     rng = np.random.default_rng(B * 1000 + H)
@@ -67,7 +70,7 @@ def test_noalloc_swiglu_matches_allocating_entry(cuda, B, K, H, N):
         stream.synchronize()
         got = y_d.cpu().numpy()
         assert np.isfinite(got).all(), f"call {call}"
-        assert np.abs(got - ref).max() <= SWIGLU_ATOL, f"call {call}"
+        assert np.array_equal(got.view(np.uint32), ref.view(np.uint32)), f"call {call}"
 
     for pw in packed:
         L.sme_ai_packed_linear_weight_destroy(ctypes.byref(pw))
@@ -85,7 +88,7 @@ def test_noalloc_swiglu_rejects_sizes_beyond_its_scratch(cuda):
                                                   k_out) == S.SME_AI_OK
         packed.append(pw)
     pg, pu, pd = packed
-    B = 129                                  # 129 * 4096 > 524288 fp16 values
+    B = LIMIT // H + 1                       # 129 * 4096 > 524288 fp16 values
     x_d = torch.zeros((B, K), dtype=torch.int16, device=cuda)
     y_d = torch.zeros((B, N), device=cuda)
     st = L.sme_ai_swiglu_packed_f16f32_noalloc(_dev(x_d), B, ctypes.byref(pg), None, ctypes.byref(pu), None,
