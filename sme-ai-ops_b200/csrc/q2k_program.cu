@@ -10,10 +10,11 @@
 //     phase, in program order, into a shared-memory ring with cp.async.bulk.
 //     Weights do not depend on activations, so the stream runs ahead across
 //     phase boundaries as far as the ring reaches;
-//   * row groups are dealt to CTAs round-robin (CTA c takes groups c, c + C,
-//     c + 2C, ...), so a phase's outputs complete in rounds from its first
-//     rows to its last and the next phase's early input blocks are ready
-//     before the phase ends;
+//   * row groups are dealt to CTAs round-robin (CTA c takes every C-th group),
+//     so a phase's outputs complete in rounds from its first rows to its last
+//     and the next phase's early input blocks are ready before the phase
+//     ends; the dealing continues from phase to phase, so the CTAs that take
+//     one phase's extra groups are not the ones that take the next one's;
 //   * the consumer warps process the CTA's row groups of each phase exactly
 //     as q2k_gemv_kernel does (q2k_core.cuh: same integer core, same ordered
 //     float sum, same epilogues), so every output is bit-identical to the
@@ -56,7 +57,9 @@ namespace smeai {
 
 namespace {
 
-constexpr int kMaxWarps = 17;                    // producer + up to 16 consumers
+constexpr int kMaxWarps = 19;                    // producer + up to 16 consumers + 2 finishers
+// (19 warps keep the 96-register cap of 17: the four schedulers' 16K-register
+// files hold at most 5 warps each either way)
 constexpr uint32_t kProgramMagic = 0x51325048u;  // "Q2PH"
 constexpr uint64_t kAbortCheckNs = 20000;        // waits shorter than this never read the abort word
 // Replicas of every group-sum array: the finisher's lanes 0..kSumReps-1 each
@@ -83,6 +86,8 @@ struct PhaseDev {
   int64_t ld_xll, ld_xsll, ldy, ld_yll, ld_ysll, ld_rll;
   int64_t n_rows;
   int64_t n_groups;
+  int64_t rot;               // row group g of this phase runs on CTA (g + rot) % grid: the dealing
+                             // continues from the previous phase, so no CTA takes every phase's extra group
   int nb;
   int in_mode;
   int epi;
@@ -127,6 +132,12 @@ struct PSmem {
   uint64_t* empty;
   uint64_t* grp;      // [2] all consumer warps wrote a row group's terms
   uint64_t* tfree;    // [2] the finisher has consumed them
+  // RMSNorm inputs: the first consumer warp to reach the CTA's n-th RMSNorm
+  // phase polls the group sums and publishes 1/rms of every token in slot
+  // n % 4 (a warp can run at most two phases ahead of the slowest one)
+  unsigned* rms_claim;  // highest n + 1 claimed
+  unsigned* rms_ready;  // [4] n + 1 once slot n % 4 holds phase n's values
+  float* rms_inv;       // [4][8]
 };
 
 __host__ __device__ __forceinline__ size_t al16(size_t v) { return (v + 15) & ~(size_t)15; }
@@ -143,7 +154,7 @@ __host__ __device__ __forceinline__ size_t act_slots(int T, int nb_max, int W) {
 __host__ __device__ __forceinline__ size_t prog_fixed_bytes(int T, int nb_max, int W, int tbufs) {
   const size_t slots = act_slots(T, nb_max, W);
   return al16(slots * 256) + al16(slots * 32) + al16(slots * 4) + al16((size_t)tbufs * T * nb_max * 128) + 8 * 4 +
-         16;
+         16 + 16 + 32 + 128;
 }
 __host__ __device__ __forceinline__ size_t prog_smem_bytes(int T, int nb_max, int stages, int consumers, int tbufs) {
   return (size_t)stages * consumers * kTileBytes + prog_fixed_bytes(T, nb_max, consumers, tbufs) +
@@ -168,6 +179,9 @@ __device__ __forceinline__ PSmem pcarve(uint8_t* base, int T, int nb_max, int st
   m.empty = m.full + stages;
   m.grp = m.empty + stages;
   m.tfree = m.grp + 2;
+  m.rms_claim = reinterpret_cast<unsigned*>(m.tfree + 2);
+  m.rms_ready = m.rms_claim + 4;
+  m.rms_inv = reinterpret_cast<float*>(m.rms_ready + 8);
   return m;
 }
 
@@ -252,7 +266,7 @@ struct Poll {
         return false;
       }
     }
-    __nanosleep(64);
+    __nanosleep(256);
     return true;
   }
 };
@@ -272,14 +286,13 @@ __device__ __forceinline__ bool ll_ready8(const LL8& r, unsigned tag) {
   return ok;
 }
 // Wait until every word of the warp's block carries `tag` (r holds a first
-// load).  While something is missing only one word per lane is re-read, then
-// the whole block once more.
+// load): every retry re-reads the whole block, so the retry that finds the
+// last word also brings the values.
 __device__ __forceinline__ bool ll_wait8(const uint64_t* p, LL8& r, unsigned tag, const ProgParams& P) {
   if (__all_sync(0xffffffffu, ll_ready8(r, tag))) return true;
   Poll pl;
   for (;;) {
     if (!pl.again(P, tag)) return false;
-    if (!__all_sync(0xffffffffu, ll_has(ll_ld(p + 7), tag))) continue;
     ll_load8(p, r);
     if (__all_sync(0xffffffffu, ll_ready8(r, tag))) return true;
   }
@@ -321,17 +334,55 @@ __device__ bool ll_rms_total(const uint64_t* sums, int G, unsigned tag, const Pr
   return true;
 }
 
-// Activation prologue of warp cw for one phase: its super-blocks
-// b = cw (mod W) of every token, read from the producer's tagged words as
-// soon as they exist, RMS-normalized (times the norm weight) when the phase
-// asks for it, and quantized to Q8_K in shared memory with the standalone
-// quantizer's helpers (same bits).  The first loads of all the warp's blocks
-// go out together (when they fit in registers: T x blocks <= kRegItems), the
-// group sums are folded while they are in flight.
+// Q8_K of one tagged input block of warp cw (block b, token t) into the
+// warp's activation slot, after an RMSNorm (1/rms inv, times the norm weight)
+// when rms is set -- the standalone quantizer's arithmetic.  w holds a first
+// load of the block; the wait for its tags is bounded.
+template <int T>
+__device__ __forceinline__ bool quant_block(const ProgParams& P, const ActSmem& act, const PhaseDev& D,
+                                            const uint64_t* src, LL8& w, bool rms, float inv, int b, int slot,
+                                            int lane, unsigned tag) {
+  if (!ll_wait8(src, w, tag, P)) return false;
+  float u[8];
+#pragma unroll
+  for (int k = 0; k < 8; ++k) u[k] = ll_val(w.w[k]);
+  if (rms) {
+#pragma unroll
+    for (int k = 0; k < 8; ++k) u[k] = __fmul_rn(u[k], inv);
+    if (D.norm_w) {
+      const float4 g0 = __ldg(reinterpret_cast<const float4*>(D.norm_w + b * QK_K + lane * 8));
+      const float4 g1 = __ldg(reinterpret_cast<const float4*>(D.norm_w + b * QK_K + lane * 8 + 4));
+      u[0] = __fmul_rn(u[0], g0.x);
+      u[1] = __fmul_rn(u[1], g0.y);
+      u[2] = __fmul_rn(u[2], g0.z);
+      u[3] = __fmul_rn(u[3], g0.w);
+      u[4] = __fmul_rn(u[4], g1.x);
+      u[5] = __fmul_rn(u[5], g1.y);
+      u[6] = __fmul_rn(u[6], g1.z);
+      u[7] = __fmul_rn(u[7], g1.w);
+    }
+  }
+  store_q8k_smem(q8k_quantize_lane(u), act, slot);
+  return true;
+}
+
+// Activation prologue of warp cw for one phase.  Its super-blocks are
+// b = cw (mod W); item it = i * T + t is block cw + i * W of token t.
+//  * Q8_K input (caller memory): staged into the warp's slots.
+//  * RMSNorm input: the producer's group sums and the warp's block are
+//    polled in ONE loop (one token, one block per warp, k <= 8192),
+//    so the retry that finds the last word also holds every value; then the
+//    blocks are normalized and quantized.  Returns *ready = all items.
+//  * plain input: nothing here -- ensure_item() polls and quantizes each
+//    block when the warp first needs it, so the phase starts on its early
+//    blocks while later ones are still being produced.
 template <int T>
 __device__ __forceinline__ bool prologue(const ProgParams& P, const ActSmem& act, const PhaseDev& D, int cw,
-                                         int W, int lane, unsigned tag, int64_t so) {
+                                         int W, int lane, unsigned tag, int64_t so, unsigned& ready,
+                                         unsigned* m_rms_claim, unsigned* m_rms_ready, float* m_rms_inv,
+                                         unsigned& nrms) {
   const int nb = D.nb;
+  ready = 0u;
   if (D.in_mode == kInQ8K) {  // caller memory, complete before the launch
     const uint32_t* src = reinterpret_cast<const uint32_t*>(D.xq);
     for (int b = cw; b < nb; b += W) {
@@ -339,68 +390,110 @@ __device__ __forceinline__ bool prologue(const ProgParams& P, const ActSmem& act
       for (int t = 0; t < T; ++t)
         copy_q8k_smem(src + ((int64_t)t * nb + b) * Q8K_BLOCK_WORDS, act, act_slot(cw, W, T, b / W, t), lane);
     }
+    ready = ~0u;
     return true;
   }
-  constexpr int kRegItems = T == 1 ? 3 : (T == 2 ? 2 : 1);
-  const bool rms = D.in_mode == kInF32Rms;
+  if (D.in_mode != kInF32Rms) return true;
   const uint64_t* x = set_ptr(D.x_ll, so);
   const int nbw = cw < nb ? (nb - cw + W - 1) / W : 0;  // blocks of this warp
-  const int items = nbw * T;                            // item = i * T + t, block cw + i * W
+  const int items = nbw * T;
   auto src = [&](int it) { return x + (it % T) * D.ld_xll + (cw + (it / T) * W) * QK_K + lane * 8; };
-  LL8 r[kRegItems];
-  const bool inreg = items <= kRegItems;
-  if (inreg) {
-#pragma unroll
-    for (int it = 0; it < kRegItems; ++it)
-      if (it < items) ll_load8(src(it), r[it]);
+  const int G = nb * 8;  // group sums per token
+  const int n = (int)(nrms & 3);
+  // the warp's blocks and norm weights go out first; they are checked (and,
+  // if still incomplete, re-read) once 1/rms is known
+  LL8 r0;
+  const bool one = items == 1;
+  if (one) ll_load8(src(0), r0);
+  float4 g0 = make_float4(0.f, 0.f, 0.f, 0.f), g1 = g0;
+  if (one && D.norm_w) {
+    g0 = __ldg(reinterpret_cast<const float4*>(D.norm_w + cw * QK_K + lane * 8));
+    g1 = __ldg(reinterpret_cast<const float4*>(D.norm_w + cw * QK_K + lane * 8 + 4));
   }
-  float inv[T];
-  if (rms) {
-    const int rep = (int)((blockIdx.x + cw) % kSumReps);
-    const uint64_t* s = set_ptr(D.xs_ll, so) + rep * D.ld_xsll;
+  unsigned prev = 0;
+  if (lane == 0) prev = atomicMax(m_rms_claim, nrms + 1);
+  prev = __shfl_sync(0xffffffffu, prev, 0);
+  if (prev < nrms + 1) {
+    // this warp polls the group sums (one replica per CTA) for the CTA
+    const uint64_t* sums = set_ptr(D.xs_ll, so) + (int)(blockIdx.x % kSumReps) * D.ld_xsll;
 #pragma unroll 1
     for (int t = 0; t < T; ++t) {
       float total;
-      if (!ll_rms_total(s + t * kSumReps * D.ld_xsll, nb * 8, tag, P, total)) return false;
-      inv[t] = rms_inv_from_sum(total, nb * QK_K, P.eps);
+      if (!ll_rms_total(sums + t * kSumReps * D.ld_xsll, G, tag, P, total)) return false;
+      if (lane == 0) m_rms_inv[n * 8 + t] = rms_inv_from_sum(total, nb * QK_K, P.eps);
     }
-  }
-  auto quant = [&](int it, LL8& w) -> bool {
-    if (!ll_wait8(src(it), w, tag, P)) return false;
-    const int t = it % T, b = cw + (it / T) * W;
-    float u[8];
-#pragma unroll
-    for (int k = 0; k < 8; ++k) u[k] = ll_val(w.w[k]);
-    if (rms) {
-#pragma unroll
-      for (int k = 0; k < 8; ++k) u[k] = __fmul_rn(u[k], inv[t]);
-      if (D.norm_w) {
-        const float4 g0 = __ldg(reinterpret_cast<const float4*>(D.norm_w + b * QK_K + lane * 8));
-        const float4 g1 = __ldg(reinterpret_cast<const float4*>(D.norm_w + b * QK_K + lane * 8 + 4));
-        u[0] = __fmul_rn(u[0], g0.x);
-        u[1] = __fmul_rn(u[1], g0.y);
-        u[2] = __fmul_rn(u[2], g0.z);
-        u[3] = __fmul_rn(u[3], g0.w);
-        u[4] = __fmul_rn(u[4], g1.x);
-        u[5] = __fmul_rn(u[5], g1.y);
-        u[6] = __fmul_rn(u[6], g1.z);
-        u[7] = __fmul_rn(u[7], g1.w);
+    __syncwarp();
+    __threadfence_block();
+    if (lane == 0) *reinterpret_cast<volatile unsigned*>(m_rms_ready + n) = nrms + 1;
+  } else {
+    // another warp polls: wait (bounded) for its shared-memory flag
+    const uint64_t t0 = global_timer_ns();
+    for (int k = 0; *reinterpret_cast<volatile unsigned*>(m_rms_ready + n) != nrms + 1; ++k) {
+      __nanosleep(20);
+      if ((k & 255) == 255) {
+        const uint64_t el = global_timer_ns() - t0;
+        if (el > kAbortCheckNs && ld_relaxed_gpu(P.ctl + 2) == tag) return false;
+        if (el > P.timeout_ns) {
+          fail(P, tag);
+          return false;
+        }
       }
     }
-    store_q8k_smem(q8k_quantize_lane(u), act, act_slot(cw, W, T, it / T, t));
-    return true;
-  };
-  if (inreg) {
+    __threadfence_block();
+  }
+  ++nrms;
+  float inv[T];
 #pragma unroll
-    for (int it = 0; it < kRegItems; ++it)
-      if (it < items && !quant(it, r[it])) return false;
+  for (int t = 0; t < T; ++t) inv[t] = *reinterpret_cast<volatile float*>(m_rms_inv + n * 8 + t);
+  if (one) {
+    if (!ll_wait8(src(0), r0, tag, P)) return false;
+    float u[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) u[k] = __fmul_rn(ll_val(r0.w[k]), inv[0]);
+    if (D.norm_w) {
+      u[0] = __fmul_rn(u[0], g0.x);
+      u[1] = __fmul_rn(u[1], g0.y);
+      u[2] = __fmul_rn(u[2], g0.z);
+      u[3] = __fmul_rn(u[3], g0.w);
+      u[4] = __fmul_rn(u[4], g1.x);
+      u[5] = __fmul_rn(u[5], g1.y);
+      u[6] = __fmul_rn(u[6], g1.z);
+      u[7] = __fmul_rn(u[7], g1.w);
+    }
+    store_q8k_smem(q8k_quantize_lane(u), act, act_slot(cw, W, T, 0, 0));
   } else {
     for (int it = 0; it < items; ++it) {
       LL8 w;
       ll_load8(src(it), w);
-      if (!quant(it, w)) return false;
+      if (!quant_block<T>(P, act, D, src(it), w, true, inv[it % T], cw + (it / T) * W,
+                          act_slot(cw, W, T, it / T, it % T), lane, tag))
+        return false;
     }
   }
+  ready = ~0u;
+  return true;
+}
+
+// Plain fp32 input: block i of warp cw (all tokens), polled and quantized
+// the first time the warp needs it.
+template <int T>
+__device__ __forceinline__ bool ensure_block(const ProgParams& P, const ActSmem& act, const PhaseDev& D, int cw,
+                                          int W, int lane, unsigned tag, int64_t so, int i, unsigned& ready) {
+  const uint64_t* x = set_ptr(D.x_ll, so);
+  const int b = cw + i * W;
+  constexpr int kBatch = T <= 2 ? T : 1;  // tokens whose loads go out together
+#pragma unroll 1
+  for (int t0 = 0; t0 < T; t0 += kBatch) {
+    LL8 w[kBatch];
+#pragma unroll
+    for (int t = 0; t < kBatch; ++t) ll_load8(x + (t0 + t) * D.ld_xll + b * QK_K + lane * 8, w[t]);
+#pragma unroll
+    for (int t = 0; t < kBatch; ++t)
+      if (!quant_block<T>(P, act, D, x + (t0 + t) * D.ld_xll + b * QK_K + lane * 8, w[t], false, 1.f, b,
+                          act_slot(cw, W, T, i, t0 + t), lane, tag))
+        return false;
+  }
+  ready |= 1u << i;
   return true;
 }
 
@@ -408,9 +501,22 @@ __device__ __forceinline__ bool prologue(const ProgParams& P, const ActSmem& act
 // (the arithmetic of finish_group in q2k_gemv.cu); the caller-visible store,
 // the tagged store, and the group sums of squares when a later phase reads
 // this output through an RMSNorm.
+// Issue the residual loads of a row group (one tagged word per lane and
+// token) ahead of the wait for the group's terms.
+template <int T>
+__device__ __forceinline__ void resid_issue(const PhaseDev& D, int64_t group, int lane, unsigned tag, int64_t so,
+                                            uint64_t (&w)[T]) {
+  const int64_t orow = group * 32 + lane;
+#pragma unroll
+  for (int t = 0; t < T; ++t)
+    w[t] = (D.epi == kEpiResidual && orow < D.n_rows) ? ll_ld(set_ptr(D.r_ll, so) + t * D.ld_rll + orow)
+                                                      : ((uint64_t)tag << 32);
+}
+
 template <int T>
 __device__ __forceinline__ bool finish_group_prog(const ProgParams& P, const float* terms, const PhaseDev& D,
-                                                  int64_t group, int lane, unsigned tag, int64_t so) {
+                                                  int64_t group, int lane, unsigned tag, int64_t so,
+                                                  uint64_t (&w)[T]) {
   const int nb = D.nb;
   uint64_t* yl = set_ptr(D.y_ll, so);
   if (D.epi == kEpiSiluMul) {
@@ -437,11 +543,8 @@ __device__ __forceinline__ bool finish_group_prog(const ProgParams& P, const flo
   const int64_t orow = group * 32 + lane;
   const bool live = orow < D.n_rows;
   float r[T];
-  if (D.epi == kEpiResidual) {  // issue the residual loads before the sums
+  if (D.epi == kEpiResidual) {  // the residual loads went out before the terms wait
     const uint64_t* rl = set_ptr(D.r_ll, so);
-    uint64_t w[T];
-#pragma unroll
-    for (int t = 0; t < T; ++t) w[t] = live ? ll_ld(rl + t * D.ld_rll + orow) : ((uint64_t)tag << 32);
     Poll pl;
     for (;;) {
       bool ok = true;
@@ -495,12 +598,13 @@ struct StageCursor {
   __device__ void load_phase(const ProgParams& P, int64_t cta) {
     for (; ph < n_phases; ++ph) {
       const PhaseDev& D = P.phases[ph];
-      if (cta < D.n_groups) {
+      const int64_t first = (cta + C - D.rot) % C;
+      if (first < D.n_groups) {
         nb = D.nb;
         nchunks = (nb + W - 1) / W;
         ng = D.n_groups;
         tiles = D.tiles;
-        g = cta;
+        g = first;
         c = 0;
         return;
       }
@@ -555,7 +659,7 @@ template <int T>
 __global__ void __launch_bounds__(kMaxWarps * 32, 1) q2k_program_kernel(const ProgParams P) {
   extern __shared__ __align__(128) uint8_t smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int W = (blockDim.x >> 5) - 1;
+  const int W = (blockDim.x >> 5) - 3;   // warp 0 producer, 1..W consumers, W+1 and W+2 finishers
   const int S = P.stages, lgS = P.log2_stages, smask = S - 1;
   const int64_t C = gridDim.x, cta = blockIdx.x;
   const int stage_bytes = W * kTileBytes;
@@ -573,6 +677,8 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1) q2k_program_kernel(const Pr
       mbar_init(&m.grp[b], W);
       mbar_init(&m.tfree[b], 1);
     }
+    *m.rms_claim = 0u;
+    for (int k = 0; k < 4; ++k) m.rms_ready[k] = 0u;
     mbar_fence_init();
   }
   __syncthreads();
@@ -598,6 +704,34 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1) q2k_program_kernel(const Pr
         fail(P, tag);
         for (int64_t j = (i > S ? i - S : 0); j < i; ++j)
           mbar_wait_bounded(&m.full[j & smask], (unsigned)((j >> lgS) & 1), P.timeout_ns);
+      }
+    }
+    return;
+  }
+
+  if (warp > W) {
+    // ---- finishers: finisher f owns terms buffer f and finishes the CTA's
+    // row groups jj = f (mod tbufs) in order -- the ordered sum, the
+    // epilogue and the stores run beside the consumers' next tiles instead
+    // of in one consumer's path; each group's residual loads go out before
+    // the wait for its terms
+    const int f = warp - W - 1;
+    if (f >= P.tbufs) return;
+    int jj = 0;
+    for (int ph = 0; ph < P.n_phases; ++ph) {
+      const PhaseDev& D = P.phases[ph];
+      const int64_t ngr = D.n_groups;
+      const int64_t first = (cta + C - D.rot) % C;
+      for (int64_t g = first; g < ngr; g += C, ++jj) {
+        if (jj % P.tbufs != f) continue;
+        const int use = P.tbufs == 2 ? (jj >> 1) : jj;
+        const float* terms = m.terms + (size_t)f * T * P.nb_max * 32;
+        uint64_t rw[T];
+        resid_issue<T>(D, g, lane, tag, so, rw);
+        if (!pwait(&m.grp[f], (unsigned)(use & 1), P, tag)) return;
+        const bool ok = finish_group_prog<T>(P, terms, D, g, lane, tag, so, rw);
+        mbar_arrive_warp(&m.tfree[f]);
+        if (!ok) return;
       }
     }
     return;
@@ -634,18 +768,21 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1) q2k_program_kernel(const Pr
   if (ld_relaxed_gpu(P.ctl + 2) == tag) return;
 
   int64_t i = 0;  // ring stage, in step with the producer
-  int jj = 0;     // row groups processed by this CTA (terms buffers, finisher rota)
+  int jj = 0;     // row groups processed by this CTA (terms buffers)
+  unsigned nrms = 0;  // RMSNorm phases this warp has entered
   for (int ph = 0; ph < P.n_phases; ++ph) {
     const PhaseDev& D = P.phases[ph];
     const int64_t ngr = D.n_groups;
-    if (cta >= ngr) continue;
+    const int64_t first = (cta + C - D.rot) % C;
+    if (first >= ngr) continue;
     const int nb = D.nb;
     const int nchunks = (nb + W - 1) / W;
-    if (!prologue<T>(P, act, D, cw, W, lane, tag, so)) return;
+    unsigned ready;
+    if (!prologue<T>(P, act, D, cw, W, lane, tag, so, ready, m.rms_claim, m.rms_ready, m.rms_inv, nrms)) return;
     __syncwarp();
 
-    // this CTA's row groups of the phase: cta, cta + C, ...
-    for (int64_t g = cta; g < ngr; g += C, ++jj) {
+    // this CTA's row groups of the phase: first, first + C, ...
+    for (int64_t g = first; g < ngr; g += C, ++jj) {
       // terms buffer of this group and how many times it was used before
       const int buf = P.tbufs == 2 ? (jj & 1) : 0;
       const int use = P.tbufs == 2 ? (jj >> 1) : jj;
@@ -655,23 +792,20 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1) q2k_program_kernel(const Pr
       for (int c = 0; c < nchunks; ++c, ++i) {
         const int s = (int)(i & smask);
         const int b = c * W + cw;
+        if (b < nb && !(ready & (1u << c)) && !ensure_block<T>(P, act, D, cw, W, lane, tag, so, c, ready)) return;
         if (!pwait(&m.full[s], (unsigned)((i >> lgS) & 1), P, tag)) return;
         if (b >= nb) {  // the group's last chunk is short
           mbar_arrive_warp(&m.empty[s]);
           continue;
         }
+        // the slot is released after the integer core has used every loaded
+        // register (the arrive follows their last use in program order)
         const WBlock wb = load_wblock(m.ring + (size_t)s * stage_bytes + (size_t)cw * kTileBytes, lane);
-        mbar_arrive_warp(&m.empty[s], wblock_dep(wb));
         block_terms<T, false>(wb, act, act_slot(cw, W, T, c, 0), W, nb, b, terms, lane, row, D.n_rows, nullptr,
                               nullptr);
+        mbar_arrive_warp(&m.empty[s]);
       }
       mbar_arrive_warp(&m.grp[buf]);
-      if (cw == (jj % W)) {
-        if (!pwait(&m.grp[buf], (unsigned)(use & 1), P, tag)) return;
-        const bool ok = finish_group_prog<T>(P, terms, D, g, lane, tag, so);
-        mbar_arrive_warp(&m.tfree[buf]);
-        if (!ok) return;
-      }
     }
   }
 }
@@ -916,7 +1050,7 @@ int q2k_program_create(const ProgPhase* phases, int n_phases, int n_cols, float 
   }
   SMEAI_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   int per_sm = 0;
-  SMEAI_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, (consumers + 1) * 32, smem));
+  SMEAI_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, (consumers + 3) * 32, smem));
   if (per_sm < 1) {
     set_last_error("q2k_program: the kernel cannot be resident (smem %zu)", smem);
     return kUnsupported;
@@ -945,6 +1079,7 @@ int q2k_program_create(const ProgPhase* phases, int n_phases, int n_cols, float 
   }
   uint64_t* ll = pr->d_ll;
   std::vector<PhaseDev> hp((size_t)n);
+  int64_t rot = 0;
   for (int p = 0; p < n; ++p) {
     const ProgPhase& s = phases[p];
     const Q2KWeight& w = *s.w;
@@ -963,6 +1098,8 @@ int q2k_program_create(const ProgPhase* phases, int n_phases, int n_cols, float 
     }
     d.n_rows = w.n_rows;
     d.n_groups = w.n_groups;
+    d.rot = rot % sms;
+    rot += w.n_groups;
     d.nb = w.nb;
     d.epi = s.epi;
     if (s.in_mode == kInQ8K) {
@@ -1048,7 +1185,7 @@ int q2k_program_run(Q2KProgram* pr, cudaStream_t stream) {
   P.tbufs = pr->tbufs;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)pr->grid);
-  cfg.blockDim = dim3((unsigned)((pr->consumers + 1) * 32));
+  cfg.blockDim = dim3((unsigned)((pr->consumers + 3) * 32));
   cfg.dynamicSmemBytes = pr->smem;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
