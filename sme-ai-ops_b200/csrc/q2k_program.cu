@@ -426,10 +426,21 @@ __device__ __forceinline__ bool prologue(const ProgParams& P, const ActSmem& act
     __threadfence_block();
     if (lane == 0) *reinterpret_cast<volatile unsigned*>(m_rms_ready + n) = nrms + 1;
   } else {
-    // another warp polls: wait (bounded) for its shared-memory flag
+    // another warp polls: wait (bounded) for its shared-memory flag; meanwhile
+    // watch the warp's own block (one word per 32-value group: 64 bytes per
+    // retry) and fetch it whole once every group has landed, so the block is
+    // in registers when 1/rms arrives
+    bool have = !one || __all_sync(0xffffffffu, ll_ready8(r0, tag));
     const uint64_t t0 = global_timer_ns();
     for (int k = 0; *reinterpret_cast<volatile unsigned*>(m_rms_ready + n) != nrms + 1; ++k) {
-      __nanosleep(20);
+      if (!have && (k & 7) == 7) {
+        const bool probe_ok = (lane & 3) != 3 || ll_has(ll_ld(src(0) + 7), tag);
+        if (__all_sync(0xffffffffu, probe_ok)) {
+          ll_load8(src(0), r0);
+          have = __all_sync(0xffffffffu, ll_ready8(r0, tag));
+        }
+      }
+      __nanosleep(32);
       if ((k & 255) == 255) {
         const uint64_t el = global_timer_ns() - t0;
         if (el > kAbortCheckNs && ld_relaxed_gpu(P.ctl + 2) == tag) return false;

@@ -91,22 +91,30 @@ __device__ __forceinline__ float rms_inv_from_sum(float total, int k, float eps)
   return __fdiv_rn(1.f, __fsqrt_rn(__fadd_rn(mean, eps)));
 }
 
+// The block's value of largest magnitude, the first one on ties (ggml scans
+// the block in order with a strict '>'), NaNs never chosen: two warp
+// reductions on the magnitudes' bit patterns (which order like the values
+// for non-negative floats) and one shuffle of the winner's signed value.
 __device__ __forceinline__ Q8KLane q8k_quantize_lane(const float (&v)[8]) {
   const int lane = threadIdx.x & 31;
-  float amax = 0.f, vmax = 0.f;
-  int idx = 0x7fffffff;
+  unsigned mag[8], m = 0u;
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
-    const float a = fabsf(v[i]);
-    if (a > amax) { amax = a; vmax = v[i]; idx = lane * 8 + i; }
+    mag[i] = __float_as_uint(v[i]) & 0x7fffffffu;
+    if (mag[i] <= 0x7f800000u && mag[i] > m) m = mag[i];   // NaN (> 0x7f800000) skipped
   }
+  const unsigned abits = __reduce_max_sync(0xffffffffu, m);
+  unsigned first = 0xffffffffu;
 #pragma unroll
-  for (int off = 16; off >= 1; off >>= 1) {
-    const float a2 = __shfl_xor_sync(0xffffffffu, amax, off);
-    const float v2 = __shfl_xor_sync(0xffffffffu, vmax, off);
-    const int i2 = __shfl_xor_sync(0xffffffffu, idx, off);
-    if (a2 > amax || (a2 == amax && i2 < idx)) { amax = a2; vmax = v2; idx = i2; }
-  }
+  for (int i = 7; i >= 0; --i)
+    if (mag[i] == abits) first = (unsigned)(lane * 8 + i);
+  const unsigned idx = __reduce_min_sync(0xffffffffu, first);
+  float mine = v[0];
+#pragma unroll
+  for (int i = 1; i < 8; ++i)
+    if ((int)(idx & 7u) == i) mine = v[i];
+  const float vmax = __shfl_sync(0xffffffffu, mine, (int)(idx >> 3) & 31);
+  const float amax = __uint_as_float(abits);
   Q8KLane r;
   if (amax == 0.f) {
     r.w0 = r.w1 = r.bsum_pair = 0u;
