@@ -67,6 +67,7 @@ constexpr uint64_t kAbortCheckNs = 20000;        // waits shorter than this neve
 // cache lines every warp of the grid needs for an RMSNorm are spread over
 // kSumReps places instead of one.
 constexpr int kSumReps = 16;
+constexpr int kDefaultL2Ahead = 0;  // measured on B200: 0.860 ms/token at 0, 0.863 at 4, 0.869 at 8, 0.94 at 12+
 
 // Descriptor of one phase.  The *_ll pointers address the tagged buffers of
 // set 0; the kernel adds the set offset of its launch.  Token t, row r of a
@@ -120,6 +121,7 @@ struct ProgParams {
   uint64_t timeout_ns;  // every bounded wait
   int64_t set_bytes;    // distance between the two sets of tagged buffers
   int tbufs;            // row-group terms buffers: 2 (double-buffered) or 1 when two do not fit
+  int l2_ahead;         // ring stages the L2 prefetch stream runs ahead of the ring loads
 };
 
 struct PSmem {
@@ -698,11 +700,19 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1) q2k_program_kernel(const Pr
   if (warp == 0) {
     // ---- producer: every phase's tiles of this CTA, in program order
     if (lane == 0) {
-      StageCursor issue;
+      // A second cursor runs l2_ahead stages ahead and asks the TMA engine to
+      // bring those tiles into L2: while the consumers wait at a phase
+      // boundary with the ring full, HBM keeps streaming into L2, and the ring
+      // then refills from L2 instead of at the HBM rate.
+      StageCursor issue, pref;
       issue.start(P, cta, C, W);
+      pref.start(P, cta, C, W);
+      int64_t npref = 0;
       bool ok = true;
       int64_t i = 0;
       for (; issue.valid(); issue.advance(P, cta), ++i) {
+        for (; P.l2_ahead > 0 && pref.valid() && npref < i + P.l2_ahead; pref.advance(P, cta), ++npref)
+          bulk_prefetch_l2(pref.src(), pref.bytes());
         const int s = (int)(i & smask);
         if (i >= S && !pwait(&m.empty[s], (unsigned)(((i >> lgS) - 1) & 1), P, tag)) {
           ok = false;
@@ -832,6 +842,7 @@ struct Q2KProgram {
   int consumers = 0;
   int stages = 0;
   int tbufs = 2;
+  int l2_ahead = 0;
   int grid = 0;
   size_t smem = 0;
   float eps = 0.f;
@@ -1074,6 +1085,10 @@ int q2k_program_create(const ProgPhase* phases, int n_phases, int n_cols, float 
   pr->consumers = consumers;
   pr->stages = stages;
   pr->tbufs = tbufs;
+  // L2 prefetch distance in ring stages: SMEAI_PROGRAM_L2_AHEAD=n overrides
+  // the default (for tuning sweeps)
+  pr->l2_ahead = kDefaultL2Ahead;
+  if (const char* e = getenv("SMEAI_PROGRAM_L2_AHEAD")) pr->l2_ahead = atoi(e) < 0 ? 0 : atoi(e);
   pr->grid = sms;  // one CTA per SM: every SM streams
   pr->smem = smem;
   pr->eps = eps;
@@ -1194,6 +1209,7 @@ int q2k_program_run(Q2KProgram* pr, cudaStream_t stream) {
   P.timeout_ns = wait_timeout_ns();
   P.set_bytes = (int64_t)pr->set_bytes;
   P.tbufs = pr->tbufs;
+  P.l2_ahead = pr->l2_ahead;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)pr->grid);
   cfg.blockDim = dim3((unsigned)((pr->consumers + 3) * 32));
