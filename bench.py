@@ -57,7 +57,8 @@ def parse_args():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["decode", "gemv", "prefill", "attention"], default="decode")
+    ap.add_argument("--workload", choices=["decode", "gemv", "prefill", "prefill-stack", "attention"],
+                    default="decode")
     ap.add_argument("--attn-seq", type=int, default=2048, help="attention workload: tokens")
     ap.add_argument("--attn-dim", type=int, default=4096, help="attention workload: model_dim")
     ap.add_argument("--attn-heads", type=int, default=32, help="attention workload: heads")
@@ -674,10 +675,13 @@ def run_ours(args):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
-    if args.workload == "decode":
+    stack = None
+    if args.workload in ("decode", "prefill-stack"):
         L, H, F, V = args.layers, 4096, 11008, 32000
-        stack = Q2KDecodeStack(n_layers=L, hidden=H, ffn=F, vocab=V, batch=1, rank=rank, world=world,
-                               device=dev, seed=0, quant=args.quant)
+        prefill_stack = args.workload == "prefill-stack"
+        stack = Q2KDecodeStack(n_layers=L, hidden=H, ffn=F, vocab=V, batch=args.prefill_tokens if prefill_stack
+                               else 1, rank=rank, world=world, device=dev, seed=0,
+                               quant="tc" if prefill_stack else args.quant)
         x_in = torch.empty_like(stack.x0)
         x_in.copy_(stack.x0)
 
@@ -690,6 +694,10 @@ def run_ours(args):
         out_buf = stack.logits
         workload = (f"llama2-7b-shape Q2_K linear stack decode, batch 1: {L} layers x (qkv, o, gate+up, down)"
                     " + lm_head 32000x4096, RMSNorm+Q8_K re-quantization between linears")
+        if prefill_stack:
+            workload = (f"llama2-7b-shape Q2_K linear stack prefill, {args.prefill_tokens} tokens: {L} layers x "
+                        "(qkv, o, gate+up, down) + lm_head 32000x4096 on the tcgen05 GEMM (residual and silu*mul "
+                        "in its epilogue), RMSNorm+Q8_K between linears")
         gemvs = stack.gemv_list()
     else:
         rows, k, epi = args.gemv_rows, args.gemv_k, args.gemv_epilogue
@@ -776,8 +784,8 @@ def run_ours(args):
         step()
     stream.synchronize()
     barrier()
-    steps_per_replay = {"decode": 1, "gemv": len(gemvs), "prefill": len(mats) if args.workload == "prefill"
-                        else 0}[args.workload]
+    steps_per_replay = {"decode": 1, "prefill-stack": 1, "gemv": len(gemvs),
+                        "prefill": len(mats) if args.workload == "prefill" else 0}[args.workload]
     graph = torch.cuda.CUDAGraph()
     with torch.cuda.graph(graph, stream=stream):
         for _ in range(steps_per_replay):
@@ -862,7 +870,18 @@ def run_ours(args):
     # ---- roofline of the dominant kernel: every GEMV of a step timed alone
     # (events around each launch, queued behind a sleep so launch gaps do not
     # count; consecutive GEMVs read distinct weights, so nothing sits in L2)
-    if args.workload == "decode" and stack.quant == "program":
+    if args.workload == "prefill-stack":
+        # every GEMM of the step on the tensor cores: this rank's ops per step
+        # over the device step time, against the int8 dense rate (2 x the
+        # measured bf16 GEMM rate)
+        tpeak, tkind = tensor_peak()
+        rank_ops = stack.ops_per_step()
+        achieved = rank_ops / (ms / 1e3) / 1e12
+        roofline = {"bound": "tensor", "kernel": "q2k_gemm_tc_kernel (the step's GEMMs)", "achieved": achieved,
+                    "peak": 2 * tpeak, "unit": "TOPS", "frac": achieved / (2 * tpeak),
+                    "peak_kind": f"int8 dense taken as 2 x the {tkind} bf16 GEMM rate ({tpeak:.1f} TFLOP/s)",
+                    "traffic": None, "ops_per_step_per_rank": rank_ops}
+    elif args.workload == "decode" and stack.quant in ("program", "mgprog"):
         roofline = program_roofline(stack, stream, peak, peak_kind)
         roofline["gemv_per_launch"] = gemv_roofline(gemvs, stream, dev, peak, peak_kind)
     elif gemvs:
@@ -883,30 +902,43 @@ def run_ours(args):
     if rank == 0 and world == 1 and args.workload == "decode" and not args.no_configs:
         configs = run_configs(dev, stream, args, peak, peak_kind)
 
+    unit = "GB/s"
+    if args.workload == "prefill-stack":   # tokens of the (row-sharded) prefill per second
+        value, e2e_value, unit = args.prefill_tokens / (ms / 1e3), args.prefill_tokens / (e2e_ms / 1e3), "tokens/s"
     if rank == 0:
+        if args.workload == "prefill-stack":
+            parallel = f"row-shard tp{world}, NCCL all-gathers of the output slices" if world > 1 else "single GPU"
+        elif args.workload == "decode":
+            parallel = (f"row-shard tp{world}, " + {
+                "peer": "all-gather fused into each GEMV (NVLink peer stores + signals)",
+                "mgprog": "one persistent kernel per rank; every finished row stored into every rank's copy of the "
+                          "phase's output over NVLink peer memory (tagged words, no collective library)"}.get(
+                stack.quant, "NCCL all-gathers")) if world > 1 else "single GPU"
+        else:
+            parallel = f"{world} independent replicas (each GPU runs the whole workload)" if world > 1 \
+                else "single GPU"
         line = {
-            "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "metric": METRIC, "value": value, "unit": unit, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
-            "scaling": "strong" if args.workload == "decode" else "weak",
+            "scaling": "strong" if args.workload in ("decode", "prefill-stack") else "weak",
             "vs_baseline": None, "dtype": "int8xu2", "data": "synthetic",
             "tokens_per_s": (1e3 / ms) if args.workload == "decode" else
-            ((args.prefill_tokens * 1e3 / ms) if args.workload == "prefill" else None),
-            "pct_of_hbm_peak": value / (peak * world) * 100,
+            ((args.prefill_tokens * 1e3 / ms) if args.workload in ("prefill", "prefill-stack") else None),
+            "pct_of_hbm_peak": (value / (peak * world) * 100) if unit == "GB/s" else None,
             "config": {"workload": workload,
-                       "global_batch": args.prefill_tokens if args.workload == "prefill" else 1, "seq_len": 1,
-                       "parallelism": (f"row-shard tp{world}, " + ("all-gather fused into each GEMV (NVLink "
-                                       "peer stores + signals)" if stack.quant == "peer" else "NCCL all-gather")
-                                       if args.workload == "decode" else
-                                       f"{world} independent replicas (each GPU runs the whole workload)")
-                       if world > 1 else "single GPU",
-                       "l2": "inputs larger than L2 (2.17 GB of weights per step)" if args.workload == "decode"
+                       "global_batch": args.prefill_tokens if args.workload in ("prefill", "prefill-stack") else 1,
+                       "seq_len": 1, "parallelism": parallel,
+                       "l2": "inputs larger than L2 (2.17 GB of weights per step)"
+                       if args.workload in ("decode", "prefill-stack")
                        else "inputs larger than L2 (rotating distinct weight copies)",
+                       **({"tops": stack.ops_per_step() * world / (ms / 1e3) / 1e12}
+                          if args.workload == "prefill-stack" else {}),
                        **({"prefill_ops_per_step": prefill_ops, "tops": prefill_ops / (ms / 1e3) / 1e12}
                           if args.workload == "prefill" else {}),
                        "cuda_graph": use_graph, "pdl": os.environ.get("SMEAI_PDL", "1") != "0",
-                       "q8k_placement": stack.quant if args.workload == "decode" else args.quant},
+                       "q8k_placement": stack.quant if stack is not None else args.quant},
             "clocks": clocks,
-            "e2e": {"value": e2e_value, "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+            "e2e": {"value": e2e_value, "unit": unit, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "ms_per_step": e2e_ms},
             "gpu_launches": launches_per_step * args.steps * steps_per_replay,
             "roofline": roofline,

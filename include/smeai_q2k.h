@@ -164,6 +164,45 @@ typedef struct smeai_q2k_phase {
 } smeai_q2k_phase;
 int smeai_q2k_program_create(const smeai_q2k_phase *phases, int n_phases, int64_t n_cols, float rms_eps,
                              void **prog_out);
+
+/* The decode program over the row shards of several GPUs of one node (one
+ * process and one program per GPU; row-sharded ggml weights, replicated
+ * activations).  The phases are wired explicitly: phase p reads rows
+ * x_row0.. of phase x_src's GLOBAL output (all ranks' rows), or, with
+ * x_src = -1, an outside input x (full rows, replicated on every rank);
+ * its local output rows [ex_lo, ex_hi) are global rows ex_row0.. of its own
+ * output.  Each finished row is stored, in the kernel that computes it, as a
+ * tagged word into every rank's copy of that output over NVLink peer memory
+ * (no collective library, no per-phase barrier: a rank starts a phase's
+ * block as soon as the words it needs carry the launch's tag).  y receives
+ * the local rows.  After create, every rank exports its handle, the ranks
+ * swap them (rank order) and connect; then run() on every rank runs a step,
+ * and gather() turns a phase's global output into plain floats.  The bounded
+ * waits use the peer limit (smeai_set_wait_timeouts).  Bit-identical to the
+ * one-GPU program on the unsharded weights. */
+typedef struct smeai_q2k_mg_phase {
+  const void *w;        /* this rank's row shard (smeai_q2k_repack handle) */
+  int input;            /* SMEAI_IN_F32 or SMEAI_IN_F32_RMS */
+  int x_src;            /* producing phase, or -1: outside input x */
+  int64_t x_row0;
+  const float *x;
+  size_t ld_x;
+  int epilogue;         /* SMEAI_EPI_* */
+  int resid_src;        /* residual: rows resid_row0.. of phase resid_src's output, or -1: */
+  int64_t resid_row0;   /*   outside resid[t * ld_resid + resid_row0 + r] for local row r */
+  const float *resid;
+  size_t ld_resid;
+  const float *norm_w;  /* RMSNorm weight (SMEAI_IN_F32_RMS), or NULL */
+  int64_t out_rows;     /* rows of the global output */
+  int64_t ex_lo, ex_hi, ex_row0;
+  float *y;
+  size_t ldy;
+} smeai_q2k_mg_phase;
+int smeai_q2k_mg_program_create(const smeai_q2k_mg_phase *phases, int n_phases, int64_t n_cols, float rms_eps,
+                                int rank, int world, void **prog_out);
+int smeai_q2k_program_ipc_handle(void *prog, void *handle64);
+int smeai_q2k_program_connect(void *prog, const void *handles, int world);
+int smeai_q2k_program_gather(void *prog, int phase, float *y_dev, size_t ldy, void *stream);
 int smeai_q2k_program_run(void *prog, void *stream);
 int smeai_q2k_program_reset(void *prog, void *stream);
 void smeai_q2k_program_free(void *prog);

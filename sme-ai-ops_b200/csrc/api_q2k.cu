@@ -316,6 +316,56 @@ int smeai_q2k_program_create(const smeai_q2k_phase* phases, int n_phases, int64_
   return st;
 }
 
+int smeai_q2k_mg_program_create(const smeai_q2k_mg_phase* phases, int n_phases, int64_t n_cols, float rms_eps,
+                                int rank, int world, void** prog_out) {
+  if (!phases || !prog_out || n_phases <= 0 || n_cols <= 0 || n_cols > 8) {
+    set_last_error("smeai_q2k_mg_program_create: bad arguments");
+    return kBadArgument;
+  }
+  *prog_out = nullptr;
+  std::vector<MGPhase> ph((size_t)n_phases);
+  for (int p = 0; p < n_phases; ++p) {
+    const Handle* h = as_fmt(phases[p].w, kFmtQ2K, "smeai_q2k_mg_program_create");
+    if (!h) return kBadArgument;
+    const smeai_q2k_mg_phase& s = phases[p];
+    MGPhase& d = ph[(size_t)p];
+    d.w = &h->w;
+    d.in_mode = s.input;
+    d.x_src = s.x_src;
+    d.x_row0 = s.x_row0;
+    d.x = s.x;
+    d.ld_x = (int64_t)s.ld_x;
+    d.epi = s.epilogue;
+    d.r_src = s.resid_src;
+    d.r_row0 = s.resid_row0;
+    d.resid = s.resid;
+    d.ld_resid = (int64_t)s.ld_resid;
+    d.norm_w = s.norm_w;
+    d.out_rows = s.out_rows;
+    d.ex_lo = s.ex_lo;
+    d.ex_hi = s.ex_hi;
+    d.ex_row0 = s.ex_row0;
+    d.y = s.y;
+    d.ldy = (int64_t)s.ldy;
+  }
+  Q2KProgram* pr = nullptr;
+  const int st = q2k_mg_program_create(ph.data(), n_phases, (int)n_cols, rms_eps, rank, world, &pr);
+  if (st == kOk) *prog_out = pr;
+  return st;
+}
+
+int smeai_q2k_program_ipc_handle(void* prog, void* handle64) {
+  return q2k_program_ipc_handle(static_cast<Q2KProgram*>(prog), handle64);
+}
+
+int smeai_q2k_program_connect(void* prog, const void* handles, int world) {
+  return q2k_program_connect(static_cast<Q2KProgram*>(prog), handles, world);
+}
+
+int smeai_q2k_program_gather(void* prog, int phase, float* y_dev, size_t ldy, void* stream) {
+  return q2k_program_gather(static_cast<Q2KProgram*>(prog), phase, y_dev, (int64_t)ldy, as_stream(stream));
+}
+
 int smeai_q2k_program_run(void* prog, void* stream) {
   return q2k_program_run(static_cast<Q2KProgram*>(prog), as_stream(stream));
 }

@@ -126,6 +126,37 @@ struct ProgPhase {
 };
 struct Q2KProgram;
 int q2k_program_create(const ProgPhase* phases, int n_phases, int n_cols, float rms_eps, Q2KProgram** out);
+// The same over the row shards of several GPUs (one program per rank), with
+// the phases wired explicitly: a phase reads rows x_row0.. of phase x_src's
+// global output (or an outside input x replicated on every rank), and stores
+// its local output rows [ex_lo, ex_hi) as global rows ex_row0.. of its own
+// output -- into every rank's copy, over peer memory.
+struct MGPhase {
+  const Q2KWeight* w = nullptr;
+  int in_mode = kInF32;
+  int x_src = -1;
+  int64_t x_row0 = 0;
+  const float* x = nullptr;
+  int64_t ld_x = 0;
+  int epi = kEpiStore;
+  int r_src = -1;           // residual: rows r_row0.. of phase r_src's global output, or outside
+  int64_t r_row0 = 0;       //   (outside: resid[t * ld_resid + r_row0 + r] for local row r)
+  const float* resid = nullptr;
+  int64_t ld_resid = 0;
+  const float* norm_w = nullptr;
+  int64_t out_rows = 0;     // rows of the global output
+  int64_t ex_lo = 0, ex_hi = 0, ex_row0 = 0;
+  float* y = nullptr;       // this rank's local output rows
+  int64_t ldy = 0;
+};
+int q2k_mg_program_create(const MGPhase* phases, int n_phases, int n_cols, float rms_eps, int rank, int world,
+                          Q2KProgram** out);
+// Multi-GPU: this rank's IPC handle of its tagged buffers (64 bytes), and the
+// mapping of every rank's buffers from the handles of all ranks (rank order).
+int q2k_program_ipc_handle(Q2KProgram* prog, void* handle64);
+int q2k_program_connect(Q2KProgram* prog, const void* handles, int world);
+// After a run: a phase's global output (all ranks' rows) as plain floats.
+int q2k_program_gather(Q2KProgram* prog, int phase, float* y, int64_t ldy, cudaStream_t stream);
 int q2k_program_run(Q2KProgram* prog, cudaStream_t stream);
 int q2k_program_reset(Q2KProgram* prog, cudaStream_t stream);
 void q2k_program_free(Q2KProgram* prog);

@@ -35,8 +35,10 @@
 //     at the start, followed by the kernel's one grid-wide barrier, so no
 //     phase can overwrite caller memory another CTA has yet to read;
 //   * the tag is the launch count + 1 (a device word advanced by CTA 0 after
-//     the barrier, when every CTA has read it), and the tagged buffers are
-//     double-buffered by the tag's parity.
+//     the barrier, when every CTA has read it), and the phases' tagged
+//     buffers are double-buffered by the tag's parity (with several GPUs a
+//     rank may run one launch ahead of another; their layout is the same on
+//     every rank, so a peer's copy is this rank's address plus one offset).
 // All CTAs must be resident at once: the launch is cooperative (the runtime
 // refuses a grid that cannot be co-resident).  Every wait is bounded; on
 // expiry the kernel records kDevErrTimeout, stores the launch's tag into the
@@ -44,6 +46,7 @@
 // returns (the program must then be reset before its next run).
 #include <stdio.h>
 #include <stdlib.h>
+#include <string.h>
 
 #include <vector>
 
@@ -87,6 +90,11 @@ struct PhaseDev {
   int64_t ld_xll, ld_xsll, ldy, ld_yll, ld_ysll, ld_rll;
   int64_t n_rows;
   int64_t n_groups;
+  // local output rows [ex_lo, ex_hi) are rows ex_row0.. of the phase's tagged
+  // (global) output; with several GPUs every rank stores them into every
+  // rank's copy.  One GPU: the identity.
+  int64_t ex_lo, ex_hi, ex_row0;
+  int x_ext, r_ext;          // input / residual is a copy of outside data: one buffer, no set offset
   int64_t rot;               // row group g of this phase runs on CTA (g + rot) % grid: the dealing
                              // continues from the previous phase, so no CTA takes every phase's extra group
   int nb;
@@ -96,6 +104,8 @@ struct PhaseDev {
 };
 
 // Inputs written before the launch, copied into tagged buffers at its start.
+// These copies are this GPU's own (never written by peers) and single: the
+// previous launch on this GPU, their only other reader, has completed.
 struct CopyDev {
   const float* src;
   int64_t ld_src;
@@ -122,6 +132,9 @@ struct ProgParams {
   int64_t set_bytes;    // distance between the two sets of tagged buffers
   int tbufs;            // row-group terms buffers: 2 (double-buffered) or 1 when two do not fit
   int l2_ahead;         // ring stages the L2 prefetch stream runs ahead of the ring loads
+  int sys;              // tagged words at system scope (peers store into this GPU's buffers)
+  int n_peers;          // other ranks whose copies of the tagged buffers this rank stores into
+  int64_t peer_delta[kMaxPeers];  // byte offset from this rank's buffers to peer q's mapping of its own
 };
 
 struct PSmem {
@@ -193,16 +206,21 @@ __device__ __forceinline__ uint64_t ll_pack(float v, unsigned tag) {
 }
 __device__ __forceinline__ bool ll_has(uint64_t w, unsigned tag) { return (unsigned)(w >> 32) == tag; }
 __device__ __forceinline__ float ll_val(uint64_t w) { return __uint_as_float((unsigned)w); }
-__device__ __forceinline__ void ll_st(uint64_t* p, uint64_t w) {
-  asm volatile("st.relaxed.gpu.global.b64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+// Tagged words are read and written at GPU scope on one GPU, at system scope
+// when other GPUs store into this GPU's buffers (the flag is uniform).
+__device__ __forceinline__ void ll_st_scoped(uint64_t* p, uint64_t w, int sys) {
+  if (sys) asm volatile("st.relaxed.sys.global.b64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+  else asm volatile("st.relaxed.gpu.global.b64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
 }
-__device__ __forceinline__ uint64_t ll_ld(const uint64_t* p) {
+__device__ __forceinline__ uint64_t ll_ld_scoped(const uint64_t* p, int sys) {
   uint64_t w;
-  asm volatile("ld.relaxed.gpu.global.b64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
+  if (sys) asm volatile("ld.relaxed.sys.global.b64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
+  else asm volatile("ld.relaxed.gpu.global.b64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
   return w;
 }
-__device__ __forceinline__ void ll_ld2(const uint64_t* p, uint64_t& a, uint64_t& b) {
-  asm volatile("ld.relaxed.gpu.global.v2.b64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
+__device__ __forceinline__ void ll_ld2_scoped(const uint64_t* p, uint64_t& a, uint64_t& b, int sys) {
+  if (sys) asm volatile("ld.relaxed.sys.global.v2.b64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
+  else asm volatile("ld.relaxed.gpu.global.v2.b64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
 }
 template <typename Ptr>
 __device__ __forceinline__ Ptr set_ptr(Ptr p, int64_t off) {
@@ -224,6 +242,12 @@ __device__ __forceinline__ void red_release_gpu_add(unsigned* p, unsigned v) {
 }
 __device__ __forceinline__ void st_relaxed_gpu(unsigned* p, unsigned v) {
   asm volatile("st.relaxed.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// A finished tagged word into this rank's buffer and every peer's copy.
+__device__ __forceinline__ void ll_put(const ProgParams& P, uint64_t* p, uint64_t w) {
+  ll_st_scoped(p, w, P.sys);
+  for (int q = 0; q < P.n_peers; ++q) ll_st_scoped(set_ptr(p, P.peer_delta[q]), w, 1);
 }
 
 // Record a timeout and make every other waiter of this launch give up.
@@ -277,9 +301,9 @@ struct Poll {
 struct LL8 {
   uint64_t w[8];
 };
-__device__ __forceinline__ void ll_load8(const uint64_t* p, LL8& r) {
+__device__ __forceinline__ void ll_load8(const uint64_t* p, LL8& r, int sys) {
 #pragma unroll
-  for (int k = 0; k < 8; k += 2) ll_ld2(p + k, r.w[k], r.w[k + 1]);
+  for (int k = 0; k < 8; k += 2) ll_ld2_scoped(p + k, r.w[k], r.w[k + 1], sys);
 }
 __device__ __forceinline__ bool ll_ready8(const LL8& r, unsigned tag) {
   bool ok = true;
@@ -295,7 +319,7 @@ __device__ __forceinline__ bool ll_wait8(const uint64_t* p, LL8& r, unsigned tag
   Poll pl;
   for (;;) {
     if (!pl.again(P, tag)) return false;
-    ll_load8(p, r);
+    ll_load8(p, r, P.sys);
     if (__all_sync(0xffffffffu, ll_ready8(r, tag))) return true;
   }
 }
@@ -311,7 +335,7 @@ __device__ bool ll_rms_total(const uint64_t* sums, int G, unsigned tag, const Pr
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
       const int g = g0 + lane + 32 * j;
-      w[j] = g < G ? ll_ld(sums + g) : ((uint64_t)tag << 32);
+      w[j] = g < G ? ll_ld_scoped(sums + g, P.sys) : ((uint64_t)tag << 32);
     }
     Poll pl;
     for (;;) {
@@ -323,7 +347,7 @@ __device__ bool ll_rms_total(const uint64_t* sums, int G, unsigned tag, const Pr
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
         const int g = g0 + lane + 32 * j;
-        if (g < G && !ll_has(w[j], tag)) w[j] = ll_ld(sums + g);
+        if (g < G && !ll_has(w[j], tag)) w[j] = ll_ld_scoped(sums + g, P.sys);
       }
     }
 #pragma unroll
@@ -396,7 +420,7 @@ __device__ __forceinline__ bool prologue(const ProgParams& P, const ActSmem& act
     return true;
   }
   if (D.in_mode != kInF32Rms) return true;
-  const uint64_t* x = set_ptr(D.x_ll, so);
+  const uint64_t* x = set_ptr(D.x_ll, D.x_ext ? 0 : so);
   const int nbw = cw < nb ? (nb - cw + W - 1) / W : 0;  // blocks of this warp
   const int items = nbw * T;
   auto src = [&](int it) { return x + (it % T) * D.ld_xll + (cw + (it / T) * W) * QK_K + lane * 8; };
@@ -406,7 +430,7 @@ __device__ __forceinline__ bool prologue(const ProgParams& P, const ActSmem& act
   // if still incomplete, re-read) once 1/rms is known
   LL8 r0;
   const bool one = items == 1;
-  if (one) ll_load8(src(0), r0);
+  if (one) ll_load8(src(0), r0, P.sys);
   float4 g0 = make_float4(0.f, 0.f, 0.f, 0.f), g1 = g0;
   if (one && D.norm_w) {
     g0 = __ldg(reinterpret_cast<const float4*>(D.norm_w + cw * QK_K + lane * 8));
@@ -417,7 +441,7 @@ __device__ __forceinline__ bool prologue(const ProgParams& P, const ActSmem& act
   prev = __shfl_sync(0xffffffffu, prev, 0);
   if (prev < nrms + 1) {
     // this warp polls the group sums (one replica per CTA) for the CTA
-    const uint64_t* sums = set_ptr(D.xs_ll, so) + (int)(blockIdx.x % kSumReps) * D.ld_xsll;
+    const uint64_t* sums = set_ptr(D.xs_ll, D.x_ext ? 0 : so) + (int)(blockIdx.x % kSumReps) * D.ld_xsll;
 #pragma unroll 1
     for (int t = 0; t < T; ++t) {
       float total;
@@ -436,9 +460,9 @@ __device__ __forceinline__ bool prologue(const ProgParams& P, const ActSmem& act
     const uint64_t t0 = global_timer_ns();
     for (int k = 0; *reinterpret_cast<volatile unsigned*>(m_rms_ready + n) != nrms + 1; ++k) {
       if (!have && (k & 7) == 7) {
-        const bool probe_ok = (lane & 3) != 3 || ll_has(ll_ld(src(0) + 7), tag);
+        const bool probe_ok = (lane & 3) != 3 || ll_has(ll_ld_scoped(src(0) + 7, P.sys), tag);
         if (__all_sync(0xffffffffu, probe_ok)) {
-          ll_load8(src(0), r0);
+          ll_load8(src(0), r0, P.sys);
           have = __all_sync(0xffffffffu, ll_ready8(r0, tag));
         }
       }
@@ -477,7 +501,7 @@ __device__ __forceinline__ bool prologue(const ProgParams& P, const ActSmem& act
   } else {
     for (int it = 0; it < items; ++it) {
       LL8 w;
-      ll_load8(src(it), w);
+      ll_load8(src(it), w, P.sys);
       if (!quant_block<T>(P, act, D, src(it), w, true, inv[it % T], cw + (it / T) * W,
                           act_slot(cw, W, T, it / T, it % T), lane, tag))
         return false;
@@ -492,14 +516,14 @@ __device__ __forceinline__ bool prologue(const ProgParams& P, const ActSmem& act
 template <int T>
 __device__ __forceinline__ bool ensure_block(const ProgParams& P, const ActSmem& act, const PhaseDev& D, int cw,
                                           int W, int lane, unsigned tag, int64_t so, int i, unsigned& ready) {
-  const uint64_t* x = set_ptr(D.x_ll, so);
+  const uint64_t* x = set_ptr(D.x_ll, D.x_ext ? 0 : so);
   const int b = cw + i * W;
   constexpr int kBatch = T <= 2 ? T : 1;  // tokens whose loads go out together
 #pragma unroll 1
   for (int t0 = 0; t0 < T; t0 += kBatch) {
     LL8 w[kBatch];
 #pragma unroll
-    for (int t = 0; t < kBatch; ++t) ll_load8(x + (t0 + t) * D.ld_xll + b * QK_K + lane * 8, w[t]);
+    for (int t = 0; t < kBatch; ++t) ll_load8(x + (t0 + t) * D.ld_xll + b * QK_K + lane * 8, w[t], P.sys);
 #pragma unroll
     for (int t = 0; t < kBatch; ++t)
       if (!quant_block<T>(P, act, D, x + (t0 + t) * D.ld_xll + b * QK_K + lane * 8, w[t], false, 1.f, b,
@@ -518,11 +542,11 @@ __device__ __forceinline__ bool ensure_block(const ProgParams& P, const ActSmem&
 // token) ahead of the wait for the group's terms.
 template <int T>
 __device__ __forceinline__ void resid_issue(const PhaseDev& D, int64_t group, int lane, unsigned tag, int64_t so,
-                                            uint64_t (&w)[T]) {
+                                            uint64_t (&w)[T], int sys) {
   const int64_t orow = group * 32 + lane;
 #pragma unroll
   for (int t = 0; t < T; ++t)
-    w[t] = (D.epi == kEpiResidual && orow < D.n_rows) ? ll_ld(set_ptr(D.r_ll, so) + t * D.ld_rll + orow)
+    w[t] = (D.epi == kEpiResidual && orow < D.n_rows) ? ll_ld_scoped(set_ptr(D.r_ll, D.r_ext ? 0 : so) + t * D.ld_rll + orow, sys)
                                                       : ((uint64_t)tag << 32);
 }
 
@@ -547,7 +571,7 @@ __device__ __forceinline__ bool finish_group_prog(const ProgParams& P, const flo
           const float sg = __fdiv_rn(g, __fadd_rn(1.0f, expf(-g)));
           const float h = __fmul_rn(sg, u);
           D.y[t * D.ldy + orow] = h;
-          ll_st(yl + t * D.ld_yll + orow, ll_pack(h, tag));
+          if (orow >= D.ex_lo && orow < D.ex_hi) ll_put(P, yl + t * D.ld_yll + D.ex_row0 + (orow - D.ex_lo), ll_pack(h, tag));
         }
       }
     }
@@ -557,7 +581,7 @@ __device__ __forceinline__ bool finish_group_prog(const ProgParams& P, const flo
   const bool live = orow < D.n_rows;
   float r[T];
   if (D.epi == kEpiResidual) {  // the residual loads went out before the terms wait
-    const uint64_t* rl = set_ptr(D.r_ll, so);
+    const uint64_t* rl = set_ptr(D.r_ll, D.r_ext ? 0 : so);
     Poll pl;
     for (;;) {
       bool ok = true;
@@ -567,7 +591,7 @@ __device__ __forceinline__ bool finish_group_prog(const ProgParams& P, const flo
       if (!pl.again(P, tag)) return false;
 #pragma unroll
       for (int t = 0; t < T; ++t)
-        if (live && !ll_has(w[t], tag)) w[t] = ll_ld(rl + t * D.ld_rll + orow);
+        if (live && !ll_has(w[t], tag)) w[t] = ll_ld_scoped(rl + t * D.ld_rll + orow, P.sys);
     }
 #pragma unroll
     for (int t = 0; t < T; ++t) r[t] = ll_val(w[t]);
@@ -589,11 +613,13 @@ __device__ __forceinline__ bool finish_group_prog(const ProgParams& P, const flo
     if (live) {
       if (D.epi == kEpiResidual) s = __fadd_rn(r[t], s);
       D.y[t * D.ldy + orow] = s;
-      ll_st(yl + t * D.ld_yll + orow, ll_pack(s, tag));
+      if (orow >= D.ex_lo && orow < D.ex_hi) ll_put(P, yl + t * D.ld_yll + D.ex_row0 + (orow - D.ex_lo), ll_pack(s, tag));
     }
-    if (ysl) {
+    if (ysl) {  // the group's sum of squares (its rows all exchanged: ex_lo, ex_row0 32-row aligned)
       const float ss = group_sumsq_lane(live ? s : 0.f);
-      if (lane < kSumReps) ll_st(ysl + (t * kSumReps + lane) * D.ld_ysll + group, ll_pack(ss, tag));
+      const int64_t gg = (D.ex_row0 + group * 32 - D.ex_lo) >> 5;
+      if (lane < kSumReps && group * 32 >= D.ex_lo && group * 32 < D.ex_hi)
+        ll_put(P, ysl + (t * kSumReps + lane) * D.ld_ysll + gg, ll_pack(ss, tag));
     }
   }
   return true;
@@ -660,10 +686,11 @@ __device__ void copy_inputs(const ProgParams& P, unsigned tag, int64_t so, int64
     const int64_t t = (u - base) / per_tok, grp = (u - base) - t * per_tok;
     const int64_t i = grp * 32 + lane;
     const float v = i < cp.len ? cp.src[t * cp.ld_src + i] : 0.f;
-    if (i < cp.len) ll_st(set_ptr(cp.dst, so) + t * cp.ld_dst + i, ll_pack(v, tag));
+    if (i < cp.len) ll_st_scoped(set_ptr(cp.dst, so) + t * cp.ld_dst + i, ll_pack(v, tag), P.sys);
     if (cp.sums) {
       const float ss = group_sumsq_lane(v);
-      if (lane < kSumReps) ll_st(set_ptr(cp.sums, so) + (t * kSumReps + lane) * cp.ld_sums + grp, ll_pack(ss, tag));
+      if (lane < kSumReps)
+        ll_st_scoped(set_ptr(cp.sums, so) + (t * kSumReps + lane) * cp.ld_sums + grp, ll_pack(ss, tag), P.sys);
     }
   }
 }
@@ -748,7 +775,7 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1) q2k_program_kernel(const Pr
         const int use = P.tbufs == 2 ? (jj >> 1) : jj;
         const float* terms = m.terms + (size_t)f * T * P.nb_max * 32;
         uint64_t rw[T];
-        resid_issue<T>(D, g, lane, tag, so, rw);
+        resid_issue<T>(D, g, lane, tag, so, rw, P.sys);
         if (!pwait(&m.grp[f], (unsigned)(use & 1), P, tag)) return;
         const bool ok = finish_group_prog<T>(P, terms, D, g, lane, tag, so, rw);
         mbar_arrive_warp(&m.tfree[f]);
@@ -764,7 +791,7 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1) q2k_program_kernel(const Pr
 
   // outside inputs -> tagged buffers, then the one grid-wide barrier: after
   // it no CTA reads caller memory a phase may overwrite
-  copy_inputs(P, tag, so, cta * W + cw, C * W, lane);
+  copy_inputs(P, tag, 0, cta * W + cw, C * W, lane);
   asm volatile("bar.sync 1, %0;" ::"r"(W * 32) : "memory");
   if (cw == 0) {
     int ok = 1;
@@ -831,6 +858,32 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1) q2k_program_kernel(const Pr
   }
 }
 
+// Final output of a phase on every rank: its tagged (global) words of the
+// launch that just completed, as plain floats (bounded wait for the words
+// other ranks store).
+__global__ void q2k_program_gather_kernel(const uint64_t* src, int64_t ld_src, int64_t rows, int T, float* dst,
+                                          int64_t ldd, const unsigned* ctl, int64_t set_bytes, int sys,
+                                          uint64_t timeout_ns, unsigned* err) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= rows * T) return;
+  const unsigned tag = ld_relaxed_gpu(ctl);
+  const int64_t t = i / rows, r = i - t * rows;
+  const uint64_t* p = set_ptr(src, (int64_t)(tag & 1u) * set_bytes) + t * ld_src + r;
+  uint64_t w = ll_ld_scoped(p, sys);
+  if (!ll_has(w, tag)) {
+    const uint64_t t0 = global_timer_ns();
+    while (!ll_has(w, tag)) {
+      if (global_timer_ns() - t0 > timeout_ns) {
+        raise_device_error(err, kDevErrTimeout);
+        return;
+      }
+      __nanosleep(128);
+      w = ll_ld_scoped(p, sys);
+    }
+  }
+  dst[t * ldd + r] = ll_val(w);
+}
+
 }  // namespace
 
 struct Q2KProgram {
@@ -847,11 +900,20 @@ struct Q2KProgram {
   size_t smem = 0;
   float eps = 0.f;
   int device = 0;
+  int rank = 0, world = 1;
   PhaseDev* d_phases = nullptr;
   CopyDev* d_copies = nullptr;
   unsigned* d_ctl = nullptr;
-  uint64_t* d_ll = nullptr;  // both sets of tagged buffers
+  uint64_t* d_ll = nullptr;  // both sets of the phases' tagged outputs (same layout on every rank)
   size_t set_bytes = 0;
+  uint64_t* d_ext = nullptr; // tagged copies of outside inputs (this GPU's own)
+  size_t ext_bytes = 0;
+  std::vector<PhaseDev> host_phases;
+  std::vector<int64_t> out_rows_global;
+  int n_peers = 0;
+  int64_t peer_delta[kMaxPeers] = {};
+  void* peer_base[kMaxPeers] = {};
+  bool connected = true;
 };
 
 namespace {
@@ -870,12 +932,12 @@ Range rows_range(const void* base, int64_t ld, int64_t cols, int64_t len, size_t
 
 int64_t round_up(int64_t v, int64_t a) { return (v + a - 1) / a * a; }
 
-// A region of fp32 token rows read by some phase: produced by phase `src`
-// (at row offset r0 of its output), or written before the launch (src < 0).
+// Where a phase's fp32 input or residual comes from: rows r0.. of phase
+// src's tagged (global) output, or an outside input (ext >= 0).
 struct Source {
   int src = -1;
   int64_t r0 = 0;
-  int ext = -1;  // index into the outside-input list when src < 0
+  int ext = -1;
 };
 
 struct Ext {
@@ -885,126 +947,65 @@ struct Ext {
   int64_t off_ll = 0, off_sums = 0, ld_ll = 0, ld_sums = 0;  // word offsets in a set
 };
 
-}  // namespace
+// One phase with its wiring resolved.
+struct Spec {
+  const Q2KWeight* w;
+  int in_mode, epi;
+  const uint8_t* xq;     // kInQ8K input (caller memory)
+  Source x, r;
+  const float* norm_w;
+  float* y;
+  int64_t ldy;
+  int64_t out_local;     // local output rows
+  int64_t out_global;    // rows of the tagged output
+  int64_t ex_lo, ex_hi, ex_row0;
+};
 
-int q2k_program_create(const ProgPhase* phases, int n_phases, int n_cols, float eps, Q2KProgram** out) {
-  if (!phases || !out || n_phases <= 0 || n_phases > (1 << 20)) {
-    set_last_error("q2k_program: bad arguments");
-    return kBadArgument;
-  }
-  *out = nullptr;
-  const int T = n_cols;
-  if (T != 1 && T != 2 && T != 4 && T != 8) {
-    set_last_error("q2k_program: n_cols must be 1, 2, 4 or 8 (got %d)", n_cols);
-    return kBadArgument;
-  }
-  int dev = 0;
-  SMEAI_CUDA_TRY(cudaGetDevice(&dev));
-  const int n = n_phases;
-  std::vector<int64_t> out_rows((size_t)n);
-  std::vector<Range> yr((size_t)n);
+int add_ext(std::vector<Ext>& ext, const float* ptr, int64_t ld, int64_t len, bool sums) {
+  for (size_t e = 0; e < ext.size(); ++e)
+    if (ext[e].ptr == ptr && ext[e].ld == ld && ext[e].len == len) {
+      ext[e].sums = ext[e].sums || sums;
+      return (int)e;
+    }
+  ext.push_back(Ext{ptr, ld, len, sums});
+  return (int)ext.size() - 1;
+}
+
+// Checks common to both front ends, then device state, descriptors and the
+// launch shape.
+int build_program(std::vector<Spec>& sp, std::vector<Ext>& ext, int T, float eps, int dev, int rank, int world,
+                  Q2KProgram** out) {
+  const int n = (int)sp.size();
   int nb_max = 0;
-  for (int p = 0; p < n; ++p) {
-    const ProgPhase& s = phases[p];
-    if (!s.w || !s.w->tiles || !s.x || !s.y || s.w->device != dev || s.w->fmt != kFmtQ2K) {
-      set_last_error("q2k_program: phase %d: missing weight, input or output (or a weight on another device, or not Q2_K)", p);
-      return kBadArgument;
-    }
-    const Q2KWeight& w = *s.w;
-    if (s.in_mode != kInQ8K && s.in_mode != kInF32 && s.in_mode != kInF32Rms) {
-      set_last_error("q2k_program: phase %d: unknown input mode %d", p, s.in_mode);
-      return kBadArgument;
-    }
-    if (s.in_mode == kInQ8K ? (reinterpret_cast<uintptr_t>(s.x) & 3) != 0 : (s.ld_x < w.k)) {
-      set_last_error("q2k_program: phase %d: Q8_K input must be 4-byte aligned; fp32 input needs ld_x >= k", p);
-      return kBadArgument;
-    }
-    if (s.norm_w && (s.in_mode != kInF32Rms || (reinterpret_cast<uintptr_t>(s.norm_w) & 15))) {
-      set_last_error("q2k_program: phase %d: an RMSNorm weight needs the RMS input mode and 16-byte alignment", p);
-      return kBadArgument;
-    }
-    if (s.epi != kEpiStore && s.epi != kEpiResidual && s.epi != kEpiSiluMul) {
-      set_last_error("q2k_program: phase %d: unknown epilogue %d", p, s.epi);
-      return kBadArgument;
-    }
-    if (s.epi == kEpiResidual && !s.resid) {
-      set_last_error("q2k_program: phase %d: residual epilogue needs a residual pointer", p);
-      return kBadArgument;
-    }
-    if (s.epi == kEpiSiluMul && (w.n_rows & 1)) {
-      set_last_error("q2k_program: phase %d: silu*mul needs interleaved (gate, up) row pairs", p);
-      return kBadArgument;
-    }
-    out_rows[(size_t)p] = s.epi == kEpiSiluMul ? w.n_rows / 2 : w.n_rows;
-    if (s.ldy < out_rows[(size_t)p] || (s.epi == kEpiResidual && s.ld_resid < out_rows[(size_t)p])) {
-      set_last_error("q2k_program: phase %d: leading dimension smaller than the output rows", p);
-      return kBadArgument;
-    }
-    yr[(size_t)p] = rows_range(s.y, s.ldy, T, out_rows[(size_t)p], 4);
-    nb_max = nb_max > w.nb ? nb_max : w.nb;
-  }
-
-  // Where each fp32 input and residual comes from: the latest earlier phase
-  // whose output overlaps it (it must then be a slice of that output with the
-  // same token stride), or the caller's memory before the launch.
-  std::vector<Ext> ext;
-  auto find_src = [&](int p, const void* ptr, int64_t ld, int64_t len, bool rms, const char* what,
-                      Source& src) -> int {
-    const Range want = rows_range(ptr, ld, T, len, 4);
-    for (int q = p - 1; q >= 0; --q) {
-      if (!yr[(size_t)q].overlaps(want)) continue;
-      const ProgPhase& sq = phases[q];
-      const intptr_t off = reinterpret_cast<intptr_t>(ptr) - reinterpret_cast<intptr_t>(sq.y);
-      if (ld != sq.ldy || off < 0 || off % 128 || off / 4 + len > out_rows[(size_t)q] ||
-          (rms && sq.epi == kEpiSiluMul)) {
-        set_last_error("q2k_program: phase %d: a %s written by phase %d must be a 32-row aligned slice of its "
-                       "output with the same row stride (and, for an RMSNorm input, not a silu*mul output)",
-                       p, what, q);
-        return kBadArgument;
-      }
-      src.src = q;
-      src.r0 = off / 4;
-      return kOk;
-    }
-    const float* f = static_cast<const float*>(ptr);
-    for (size_t e = 0; e < ext.size(); ++e)
-      if (ext[e].ptr == f && ext[e].ld == ld && ext[e].len == len) {
-        ext[e].sums = ext[e].sums || rms;
-        src.ext = (int)e;
-        return kOk;
-      }
-    ext.push_back(Ext{f, ld, len, rms});
-    src.ext = (int)ext.size() - 1;
-    return kOk;
-  };
-  std::vector<Source> xin((size_t)n), rin((size_t)n);
   std::vector<char> need_sums((size_t)n, 0);
   for (int p = 0; p < n; ++p) {
-    const ProgPhase& s = phases[p];
-    const Q2KWeight& w = *s.w;
-    if (s.in_mode != kInQ8K) {
-      int st = find_src(p, s.x, s.ld_x, w.k, s.in_mode == kInF32Rms, "input", xin[(size_t)p]);
-      if (st) return st;
-      if (s.in_mode == kInF32Rms && xin[(size_t)p].src >= 0) need_sums[(size_t)xin[(size_t)p].src] = 1;
-    } else {
-      const Range q8 = rows_range(s.x, w.nb * (int64_t)Q8K_BLOCK_BYTES, T, w.nb * (int64_t)Q8K_BLOCK_BYTES, 1);
-      for (int q = 0; q < n; ++q)
-        if (yr[(size_t)q].overlaps(q8)) {
-          set_last_error("q2k_program: phase %d's Q8_K input overlaps phase %d's output", p, q);
-          return kBadArgument;
-        }
+    const Spec& s = sp[(size_t)p];
+    nb_max = nb_max > s.w->nb ? nb_max : s.w->nb;
+    if (s.in_mode == kInF32Rms && s.x.src >= 0) {
+      const Spec& q = sp[(size_t)s.x.src];
+      if (q.epi == kEpiSiluMul || s.x.r0 % 32 || q.ex_lo % 32 || q.ex_row0 % 32) {
+        set_last_error("q2k_program: phase %d: an RMSNorm input must be a 32-row aligned slice of a store or "
+                       "residual output", p);
+        return kBadArgument;
+      }
+      need_sums[(size_t)s.x.src] = 1;
     }
-    if (s.epi == kEpiResidual) {
-      int st = find_src(p, s.resid, s.ld_resid, out_rows[(size_t)p], false, "residual", rin[(size_t)p]);
-      if (st) return st;
+    for (const Source* src : {&s.x, &s.r}) {
+      if (src->src < 0) continue;
+      if (src->src >= p) {
+        set_last_error("q2k_program: phase %d reads phase %d, which does not run before it", p, src->src);
+        return kBadArgument;
+      }
     }
-    if (s.norm_w) {
-      const Range nw = rows_range(s.norm_w, 0, 1, w.k, 4);
-      for (int q = 0; q < n; ++q)
-        if (yr[(size_t)q].overlaps(nw)) {
-          set_last_error("q2k_program: phase %d's RMSNorm weight overlaps phase %d's output", p, q);
-          return kBadArgument;
-        }
+    if (s.x.src >= 0 && (s.x.r0 < 0 || s.x.r0 % 32 || s.x.r0 + s.w->k > sp[(size_t)s.x.src].out_global)) {
+      set_last_error("q2k_program: phase %d: input rows [%lld, +%lld) are not a 32-row aligned slice of phase "
+                     "%d's output", p, (long long)s.x.r0, (long long)s.w->k, s.x.src);
+      return kBadArgument;
+    }
+    if (s.epi == kEpiResidual && s.r.src >= 0 &&
+        (s.r.r0 < 0 || s.r.r0 + s.out_local > sp[(size_t)s.r.src].out_global)) {
+      set_last_error("q2k_program: phase %d: the residual lies outside phase %d's output", p, s.r.src);
+      return kBadArgument;
     }
   }
 
@@ -1013,33 +1014,35 @@ int q2k_program_create(const ProgPhase* phases, int n_phases, int n_cols, float 
   std::vector<int64_t> off_y((size_t)n), ld_yll((size_t)n), off_ys((size_t)n, -1), ld_ys((size_t)n, 0);
   int64_t words = 0;
   for (int p = 0; p < n; ++p) {
-    ld_yll[(size_t)p] = round_up(out_rows[(size_t)p], 32);
+    ld_yll[(size_t)p] = round_up(sp[(size_t)p].out_global, 32);
     off_y[(size_t)p] = words;
     words += T * ld_yll[(size_t)p];
     if (need_sums[(size_t)p]) {
-      ld_ys[(size_t)p] = round_up((out_rows[(size_t)p] + 31) / 32, 2);
+      ld_ys[(size_t)p] = round_up((sp[(size_t)p].out_global + 31) / 32, 2);
       off_ys[(size_t)p] = words;
       words += (int64_t)T * kSumReps * ld_ys[(size_t)p];
     }
   }
+  const size_t set_bytes = (size_t)round_up(words * 8, 256);
+  int64_t ewords = 0;
   for (Ext& e : ext) {
     e.ld_ll = round_up(e.len, 32);
-    e.off_ll = words;
-    words += T * e.ld_ll;
+    e.off_ll = ewords;
+    ewords += T * e.ld_ll;
     if (e.sums) {
       e.ld_sums = round_up((e.len + 31) / 32, 2);
-      e.off_sums = words;
-      words += (int64_t)T * kSumReps * e.ld_sums;
+      e.off_sums = ewords;
+      ewords += (int64_t)T * kSumReps * e.ld_sums;
     }
   }
-  const size_t set_bytes = (size_t)round_up(words * 8, 256);
+  const size_t ext_bytes = (size_t)round_up((ewords > 0 ? ewords : 1) * 8, 256);
 
   // launch shape: 16 consumer warps (8 when the activation planes of 8 tokens
   // leave too little room) and the deepest power-of-two ring that fits
+  // (a single terms buffer as the last resort: 8 tokens of a k = 11008 input)
   int sms = 0, optin = 0;
   SMEAI_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
   SMEAI_CUDA_TRY(cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev));
-  // (a single terms buffer as the last resort: 8 tokens of a k = 11008 input)
   int consumers = 0, stages = 0, tbufs = 0;
   for (int tb : {2, 1}) {
     for (int W : {16, 8}) {
@@ -1093,21 +1096,27 @@ int q2k_program_create(const ProgPhase* phases, int n_phases, int n_cols, float 
   pr->smem = smem;
   pr->eps = eps;
   pr->device = dev;
+  pr->rank = rank;
+  pr->world = world;
+  pr->connected = world == 1;
   pr->set_bytes = set_bytes;
+  pr->ext_bytes = ext_bytes;
   if (device_malloc((void**)&pr->d_phases, sizeof(PhaseDev) * (size_t)n) != cudaSuccess ||
       device_malloc((void**)&pr->d_copies, sizeof(CopyDev) * (ext.empty() ? 1 : ext.size())) != cudaSuccess ||
       device_malloc((void**)&pr->d_ctl, sizeof(unsigned) * 4) != cudaSuccess ||
-      device_malloc((void**)&pr->d_ll, 2 * set_bytes) != cudaSuccess) {
+      device_malloc((void**)&pr->d_ll, 2 * set_bytes) != cudaSuccess ||
+      device_malloc((void**)&pr->d_ext, ext_bytes) != cudaSuccess) {
     cudaGetLastError();
     q2k_program_free(pr);
     set_last_error("q2k_program: cudaMalloc failed");
     return kAllocFailed;
   }
   uint64_t* ll = pr->d_ll;
+  uint64_t* el = pr->d_ext;
   std::vector<PhaseDev> hp((size_t)n);
   int64_t rot = 0;
   for (int p = 0; p < n; ++p) {
-    const ProgPhase& s = phases[p];
+    const Spec& s = sp[(size_t)p];
     const Q2KWeight& w = *s.w;
     PhaseDev& d = hp[(size_t)p];
     d = PhaseDev{};
@@ -1124,39 +1133,40 @@ int q2k_program_create(const ProgPhase* phases, int n_phases, int n_cols, float 
     }
     d.n_rows = w.n_rows;
     d.n_groups = w.n_groups;
+    d.ex_lo = s.ex_lo;
+    d.ex_hi = s.ex_hi;
+    d.ex_row0 = s.ex_row0;
     d.rot = rot % sms;
     rot += w.n_groups;
     d.nb = w.nb;
     d.epi = s.epi;
     if (s.in_mode == kInQ8K) {
-      d.xq = static_cast<const uint8_t*>(s.x);
+      d.xq = s.xq;
+    } else if (s.x.src >= 0) {
+      d.x_ll = ll + off_y[(size_t)s.x.src] + s.x.r0;
+      d.ld_xll = ld_yll[(size_t)s.x.src];
+      if (s.in_mode == kInF32Rms) {
+        d.xs_ll = ll + off_ys[(size_t)s.x.src] + s.x.r0 / 32;
+        d.ld_xsll = ld_ys[(size_t)s.x.src];
+      }
     } else {
-      const Source& src = xin[(size_t)p];
-      if (src.src >= 0) {
-        d.x_ll = ll + off_y[(size_t)src.src] + src.r0;
-        d.ld_xll = ld_yll[(size_t)src.src];
-        if (s.in_mode == kInF32Rms) {
-          d.xs_ll = ll + off_ys[(size_t)src.src] + src.r0 / 32;
-          d.ld_xsll = ld_ys[(size_t)src.src];
-        }
-      } else {
-        const Ext& e = ext[(size_t)src.ext];
-        d.x_ll = ll + e.off_ll;
-        d.ld_xll = e.ld_ll;
-        if (s.in_mode == kInF32Rms) {
-          d.xs_ll = ll + e.off_sums;
-          d.ld_xsll = e.ld_sums;
-        }
+      const Ext& e = ext[(size_t)s.x.ext];
+      d.x_ext = 1;
+      d.x_ll = el + e.off_ll;
+      d.ld_xll = e.ld_ll;
+      if (s.in_mode == kInF32Rms) {
+        d.xs_ll = el + e.off_sums;
+        d.ld_xsll = e.ld_sums;
       }
     }
     if (s.epi == kEpiResidual) {
-      const Source& src = rin[(size_t)p];
-      if (src.src >= 0) {
-        d.r_ll = ll + off_y[(size_t)src.src] + src.r0;
-        d.ld_rll = ld_yll[(size_t)src.src];
+      if (s.r.src >= 0) {
+        d.r_ll = ll + off_y[(size_t)s.r.src] + s.r.r0;
+        d.ld_rll = ld_yll[(size_t)s.r.src];
       } else {
-        d.r_ll = ll + ext[(size_t)src.ext].off_ll;
-        d.ld_rll = ext[(size_t)src.ext].ld_ll;
+        d.r_ext = 1;
+        d.r_ll = el + ext[(size_t)s.r.ext].off_ll + s.r.r0;
+        d.ld_rll = ext[(size_t)s.r.ext].ld_ll;
       }
     }
   }
@@ -1165,9 +1175,9 @@ int q2k_program_create(const ProgPhase* phases, int n_phases, int n_cols, float 
     CopyDev& c = hc[e];
     c.src = ext[e].ptr;
     c.ld_src = ext[e].ld;
-    c.dst = ll + ext[e].off_ll;
+    c.dst = el + ext[e].off_ll;
     c.ld_dst = ext[e].ld_ll;
-    c.sums = ext[e].sums ? ll + ext[e].off_sums : nullptr;
+    c.sums = ext[e].sums ? el + ext[e].off_sums : nullptr;
     c.ld_sums = ext[e].ld_sums;
     c.len = ext[e].len;
     c.units = (int64_t)T * ((ext[e].len + 31) / 32);
@@ -1176,19 +1186,275 @@ int q2k_program_create(const ProgPhase* phases, int n_phases, int n_cols, float 
       (!hc.empty() &&
        cudaMemcpy(pr->d_copies, hc.data(), sizeof(CopyDev) * hc.size(), cudaMemcpyHostToDevice) != cudaSuccess) ||
       cudaMemset(pr->d_ctl, 0, sizeof(unsigned) * 4) != cudaSuccess ||
-      cudaMemset(pr->d_ll, 0, 2 * set_bytes) != cudaSuccess) {
+      cudaMemset(pr->d_ll, 0, 2 * set_bytes) != cudaSuccess || cudaMemset(pr->d_ext, 0, ext_bytes) != cudaSuccess ||
+      cudaDeviceSynchronize() != cudaSuccess) {
     const cudaError_t e = cudaGetLastError();
     q2k_program_free(pr);
     set_last_error("q2k_program: %s", cudaGetErrorString(e));
     return kCudaError;
   }
+  pr->host_phases = hp;
+  for (const Spec& s : sp) pr->out_rows_global.push_back(s.out_global);
   *out = pr;
+  return kOk;
+}
+
+int check_phase_common(int p, const Q2KWeight* w, int dev, int in_mode, int epi, const float* norm_w) {
+  if (!w || !w->tiles || w->device != dev || w->fmt != kFmtQ2K) {
+    set_last_error("q2k_program: phase %d: missing weight (or a weight on another device, or not Q2_K)", p);
+    return kBadArgument;
+  }
+  if (in_mode != kInQ8K && in_mode != kInF32 && in_mode != kInF32Rms) {
+    set_last_error("q2k_program: phase %d: unknown input mode %d", p, in_mode);
+    return kBadArgument;
+  }
+  if (norm_w && (in_mode != kInF32Rms || (reinterpret_cast<uintptr_t>(norm_w) & 15))) {
+    set_last_error("q2k_program: phase %d: an RMSNorm weight needs the RMS input mode and 16-byte alignment", p);
+    return kBadArgument;
+  }
+  if (epi != kEpiStore && epi != kEpiResidual && epi != kEpiSiluMul) {
+    set_last_error("q2k_program: phase %d: unknown epilogue %d", p, epi);
+    return kBadArgument;
+  }
+  if (epi == kEpiSiluMul && (w->n_rows & 1)) {
+    set_last_error("q2k_program: phase %d: silu*mul needs interleaved (gate, up) row pairs", p);
+    return kBadArgument;
+  }
+  return kOk;
+}
+
+}  // namespace
+
+int q2k_program_create(const ProgPhase* phases, int n_phases, int n_cols, float eps, Q2KProgram** out) {
+  if (!phases || !out || n_phases <= 0 || n_phases > (1 << 20)) {
+    set_last_error("q2k_program: bad arguments");
+    return kBadArgument;
+  }
+  *out = nullptr;
+  const int T = n_cols;
+  if (T != 1 && T != 2 && T != 4 && T != 8) {
+    set_last_error("q2k_program: n_cols must be 1, 2, 4 or 8 (got %d)", n_cols);
+    return kBadArgument;
+  }
+  int dev = 0;
+  SMEAI_CUDA_TRY(cudaGetDevice(&dev));
+  const int n = n_phases;
+  std::vector<int64_t> out_rows((size_t)n);
+  std::vector<Range> yr((size_t)n);
+  for (int p = 0; p < n; ++p) {
+    const ProgPhase& s = phases[p];
+    int st = check_phase_common(p, s.w, dev, s.in_mode, s.epi, s.norm_w);
+    if (st) return st;
+    if (!s.x || !s.y) {
+      set_last_error("q2k_program: phase %d: missing input or output", p);
+      return kBadArgument;
+    }
+    const Q2KWeight& w = *s.w;
+    if (s.in_mode == kInQ8K ? (reinterpret_cast<uintptr_t>(s.x) & 3) != 0 : (s.ld_x < w.k)) {
+      set_last_error("q2k_program: phase %d: Q8_K input must be 4-byte aligned; fp32 input needs ld_x >= k", p);
+      return kBadArgument;
+    }
+    if (s.epi == kEpiResidual && !s.resid) {
+      set_last_error("q2k_program: phase %d: residual epilogue needs a residual pointer", p);
+      return kBadArgument;
+    }
+    out_rows[(size_t)p] = s.epi == kEpiSiluMul ? w.n_rows / 2 : w.n_rows;
+    if (s.ldy < out_rows[(size_t)p] || (s.epi == kEpiResidual && s.ld_resid < out_rows[(size_t)p])) {
+      set_last_error("q2k_program: phase %d: leading dimension smaller than the output rows", p);
+      return kBadArgument;
+    }
+    yr[(size_t)p] = rows_range(s.y, s.ldy, T, out_rows[(size_t)p], 4);
+  }
+
+  // Where each fp32 input and residual comes from: the latest earlier phase
+  // whose output overlaps it (it must then be a slice of that output with the
+  // same token stride), or the caller's memory before the launch.
+  std::vector<Ext> ext;
+  auto find_src = [&](int p, const void* ptr, int64_t ld, int64_t len, bool rms, const char* what,
+                      Source& src) -> int {
+    const Range want = rows_range(ptr, ld, T, len, 4);
+    for (int q = p - 1; q >= 0; --q) {
+      if (!yr[(size_t)q].overlaps(want)) continue;
+      const ProgPhase& sq = phases[q];
+      const intptr_t off = reinterpret_cast<intptr_t>(ptr) - reinterpret_cast<intptr_t>(sq.y);
+      if (ld != sq.ldy || off < 0 || off % 128 || off / 4 + len > out_rows[(size_t)q] ||
+          (rms && sq.epi == kEpiSiluMul)) {
+        set_last_error("q2k_program: phase %d: a %s written by phase %d must be a 32-row aligned slice of its "
+                       "output with the same row stride (and, for an RMSNorm input, not a silu*mul output)",
+                       p, what, q);
+        return kBadArgument;
+      }
+      src.src = q;
+      src.r0 = off / 4;
+      return kOk;
+    }
+    src.ext = add_ext(ext, static_cast<const float*>(ptr), ld, len, rms);
+    return kOk;
+  };
+  std::vector<Spec> sp((size_t)n);
+  for (int p = 0; p < n; ++p) {
+    const ProgPhase& s = phases[p];
+    const Q2KWeight& w = *s.w;
+    Spec& d = sp[(size_t)p];
+    d = Spec{};
+    d.w = s.w;
+    d.in_mode = s.in_mode;
+    d.epi = s.epi;
+    d.norm_w = s.norm_w;
+    d.y = s.y;
+    d.ldy = s.ldy;
+    d.out_local = d.out_global = out_rows[(size_t)p];
+    d.ex_lo = 0;
+    d.ex_hi = out_rows[(size_t)p];
+    d.ex_row0 = 0;
+    if (s.in_mode != kInQ8K) {
+      int st = find_src(p, s.x, s.ld_x, w.k, s.in_mode == kInF32Rms, "input", d.x);
+      if (st) return st;
+    } else {
+      d.xq = static_cast<const uint8_t*>(s.x);
+      const Range q8 = rows_range(s.x, w.nb * (int64_t)Q8K_BLOCK_BYTES, T, w.nb * (int64_t)Q8K_BLOCK_BYTES, 1);
+      for (int q = 0; q < n; ++q)
+        if (yr[(size_t)q].overlaps(q8)) {
+          set_last_error("q2k_program: phase %d's Q8_K input overlaps phase %d's output", p, q);
+          return kBadArgument;
+        }
+    }
+    if (s.epi == kEpiResidual) {
+      int st = find_src(p, s.resid, s.ld_resid, out_rows[(size_t)p], false, "residual", d.r);
+      if (st) return st;
+    }
+    if (s.norm_w) {
+      const Range nw = rows_range(s.norm_w, 0, 1, w.k, 4);
+      for (int q = 0; q < n; ++q)
+        if (yr[(size_t)q].overlaps(nw)) {
+          set_last_error("q2k_program: phase %d's RMSNorm weight overlaps phase %d's output", p, q);
+          return kBadArgument;
+        }
+    }
+  }
+  return build_program(sp, ext, T, eps, dev, 0, 1, out);
+}
+
+int q2k_mg_program_create(const MGPhase* phases, int n_phases, int n_cols, float eps, int rank, int world,
+                          Q2KProgram** out) {
+  if (!phases || !out || n_phases <= 0 || n_phases > (1 << 20) || world < 1 || world > kMaxPeers ||
+      rank < 0 || rank >= world) {
+    set_last_error("q2k_mg_program: bad arguments (1 <= world <= %d)", kMaxPeers);
+    return kBadArgument;
+  }
+  *out = nullptr;
+  const int T = n_cols;
+  if (T != 1 && T != 2 && T != 4 && T != 8) {
+    set_last_error("q2k_mg_program: n_cols must be 1, 2, 4 or 8 (got %d)", n_cols);
+    return kBadArgument;
+  }
+  int dev = 0;
+  SMEAI_CUDA_TRY(cudaGetDevice(&dev));
+  std::vector<Ext> ext;
+  std::vector<Spec> sp((size_t)n_phases);
+  for (int p = 0; p < n_phases; ++p) {
+    const MGPhase& s = phases[p];
+    int st = check_phase_common(p, s.w, dev, s.in_mode, s.epi, s.norm_w);
+    if (st) return st;
+    if (s.in_mode == kInQ8K) {
+      set_last_error("q2k_mg_program: phase %d: the multi-GPU program takes fp32 inputs", p);
+      return kBadArgument;
+    }
+    const Q2KWeight& w = *s.w;
+    Spec& d = sp[(size_t)p];
+    d = Spec{};
+    d.w = s.w;
+    d.in_mode = s.in_mode;
+    d.epi = s.epi;
+    d.norm_w = s.norm_w;
+    d.y = s.y;
+    d.ldy = s.ldy;
+    d.out_local = s.epi == kEpiSiluMul ? w.n_rows / 2 : w.n_rows;
+    d.out_global = s.out_rows;
+    d.ex_lo = s.ex_lo;
+    d.ex_hi = s.ex_hi;
+    d.ex_row0 = s.ex_row0;
+    if (!s.y || s.ldy < d.out_local || s.ex_lo < 0 || s.ex_hi > d.out_local || s.ex_lo > s.ex_hi ||
+        s.ex_row0 < 0 || s.ex_row0 + (s.ex_hi - s.ex_lo) > s.out_rows || s.ex_lo % 16 || s.ex_row0 % 16) {
+      set_last_error("q2k_mg_program: phase %d: bad output (local rows [ex_lo, ex_hi) must map inside the "
+                     "%lld global rows, 16-row aligned)", p, (long long)s.out_rows);
+      return kBadArgument;
+    }
+    if (s.x_src >= 0) {
+      d.x.src = s.x_src;
+      d.x.r0 = s.x_row0;
+    } else {
+      if (!s.x || s.ld_x < w.k) {
+        set_last_error("q2k_mg_program: phase %d: an outside input needs x with ld_x >= k", p);
+        return kBadArgument;
+      }
+      d.x.ext = add_ext(ext, s.x, s.ld_x, w.k, s.in_mode == kInF32Rms);
+    }
+    if (s.epi == kEpiResidual) {
+      if (s.r_src >= 0) {
+        d.r.src = s.r_src;
+        d.r.r0 = s.r_row0;
+      } else {
+        if (!s.resid || s.ld_resid < s.r_row0 + d.out_local) {
+          set_last_error("q2k_mg_program: phase %d: an outside residual needs resid rows covering the output", p);
+          return kBadArgument;
+        }
+        // the whole residual row is copied; the phase reads from r_row0 on
+        d.r.ext = add_ext(ext, s.resid, s.ld_resid, s.r_row0 + d.out_local, false);
+        d.r.r0 = s.r_row0;
+      }
+    }
+  }
+  return build_program(sp, ext, T, eps, dev, rank, world, out);
+}
+
+int q2k_program_ipc_handle(Q2KProgram* pr, void* handle64) {
+  if (!pr || pr->magic != kProgramMagic || !handle64) {
+    set_last_error("q2k_program_ipc_handle: bad arguments");
+    return kBadArgument;
+  }
+  cudaIpcMemHandle_t h;
+  SMEAI_CUDA_TRY(cudaIpcGetMemHandle(&h, pr->d_ll));
+  memcpy(handle64, &h, sizeof(h) < 64 ? sizeof(h) : 64);
+  return kOk;
+}
+
+int q2k_program_connect(Q2KProgram* pr, const void* handles, int world) {
+  if (!pr || pr->magic != kProgramMagic || !handles || world != pr->world) {
+    set_last_error("q2k_program_connect: bad arguments (world must match the program's)");
+    return kBadArgument;
+  }
+  const uint8_t* hb = static_cast<const uint8_t*>(handles);
+  int k = 0;
+  for (int q = 0; q < world; ++q) {
+    if (q == pr->rank) continue;
+    cudaIpcMemHandle_t h;
+    memcpy(&h, hb + (size_t)q * 64, sizeof(h));
+    void* ptr = nullptr;
+    const cudaError_t e = cudaIpcOpenMemHandle(&ptr, h, cudaIpcMemLazyEnablePeerAccess);
+    if (e != cudaSuccess) {
+      cudaGetLastError();
+      for (int j = 0; j < k; ++j) cudaIpcCloseMemHandle(pr->peer_base[j]);
+      pr->n_peers = 0;
+      set_last_error("q2k_program_connect: mapping rank %d's buffers failed: %s", q, cudaGetErrorString(e));
+      return kCudaError;
+    }
+    pr->peer_base[k] = ptr;
+    pr->peer_delta[k] = reinterpret_cast<intptr_t>(ptr) - reinterpret_cast<intptr_t>(pr->d_ll);
+    ++k;
+  }
+  pr->n_peers = k;
+  pr->connected = true;
   return kOk;
 }
 
 int q2k_program_run(Q2KProgram* pr, cudaStream_t stream) {
   if (!pr || pr->magic != kProgramMagic) {
     set_last_error("q2k_program_run: not a program handle");
+    return kBadArgument;
+  }
+  if (!pr->connected) {
+    set_last_error("q2k_program_run: a multi-GPU program must be connected to its peers first");
     return kBadArgument;
   }
   ProgParams P;
@@ -1206,10 +1472,13 @@ int q2k_program_run(Q2KProgram* pr, cudaStream_t stream) {
     set_last_error("q2k_program_run: device error word unavailable");
     return kCudaError;
   }
-  P.timeout_ns = wait_timeout_ns();
+  P.timeout_ns = pr->world > 1 ? peer_wait_timeout_ns() : wait_timeout_ns();
   P.set_bytes = (int64_t)pr->set_bytes;
   P.tbufs = pr->tbufs;
   P.l2_ahead = pr->l2_ahead;
+  P.sys = pr->world > 1 ? 1 : 0;
+  P.n_peers = pr->n_peers;
+  for (int q = 0; q < kMaxPeers; ++q) P.peer_delta[q] = pr->peer_delta[q];
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)pr->grid);
   cfg.blockDim = dim3((unsigned)((pr->consumers + 3) * 32));
@@ -1236,6 +1505,27 @@ int q2k_program_run(Q2KProgram* pr, cudaStream_t stream) {
   return kOk;
 }
 
+int q2k_program_gather(Q2KProgram* pr, int phase, float* y, int64_t ldy, cudaStream_t stream) {
+  if (!pr || pr->magic != kProgramMagic || phase < 0 || phase >= pr->n_phases || !y ||
+      ldy < pr->out_rows_global[(size_t)phase]) {
+    set_last_error("q2k_program_gather: bad arguments");
+    return kBadArgument;
+  }
+  unsigned* err = device_error_ptr();
+  if (!err) {
+    set_last_error("q2k_program_gather: device error word unavailable");
+    return kCudaError;
+  }
+  const PhaseDev& d = pr->host_phases[(size_t)phase];
+  const int64_t rows = pr->out_rows_global[(size_t)phase];
+  const int64_t n = rows * pr->T;
+  q2k_program_gather_kernel<<<(unsigned)((n + 255) / 256), 256, 0, stream>>>(
+      d.y_ll, d.ld_yll, rows, pr->T, y, ldy, pr->d_ctl, (int64_t)pr->set_bytes, pr->world > 1 ? 1 : 0,
+      pr->world > 1 ? peer_wait_timeout_ns() : wait_timeout_ns(), err);
+  SMEAI_CUDA_TRY(cudaGetLastError());
+  return kOk;
+}
+
 int q2k_program_reset(Q2KProgram* pr, cudaStream_t stream) {
   if (!pr || pr->magic != kProgramMagic) {
     set_last_error("q2k_program_reset: not a program handle");
@@ -1243,15 +1533,19 @@ int q2k_program_reset(Q2KProgram* pr, cudaStream_t stream) {
   }
   SMEAI_CUDA_TRY(cudaMemsetAsync(pr->d_ctl, 0, sizeof(unsigned) * 4, stream));
   SMEAI_CUDA_TRY(cudaMemsetAsync(pr->d_ll, 0, 2 * pr->set_bytes, stream));
+  SMEAI_CUDA_TRY(cudaMemsetAsync(pr->d_ext, 0, pr->ext_bytes, stream));
   return kOk;
 }
 
 void q2k_program_free(Q2KProgram* pr) {
   if (!pr || pr->magic != kProgramMagic) return;
+  for (int q = 0; q < pr->n_peers; ++q)
+    if (pr->peer_base[q]) cudaIpcCloseMemHandle(pr->peer_base[q]);
   if (pr->d_phases) cudaFree(pr->d_phases);
   if (pr->d_copies) cudaFree(pr->d_copies);
   if (pr->d_ctl) cudaFree(pr->d_ctl);
   if (pr->d_ll) cudaFree(pr->d_ll);
+  if (pr->d_ext) cudaFree(pr->d_ext);
   pr->magic = 0;
   delete pr;
 }

@@ -61,6 +61,16 @@ class Q2KPhase(ctypes.Structure):
                 ("norm_w", ctypes.c_void_p)]
 
 
+class Q2KMGPhase(ctypes.Structure):
+    """smeai_q2k_mg_phase: one phase of a multi-GPU decode program."""
+    _fields_ = [("w", ctypes.c_void_p), ("input", ctypes.c_int), ("x_src", ctypes.c_int),
+                ("x_row0", ctypes.c_int64), ("x", ctypes.c_void_p), ("ld_x", ctypes.c_size_t),
+                ("epilogue", ctypes.c_int), ("resid_src", ctypes.c_int), ("resid_row0", ctypes.c_int64),
+                ("resid", ctypes.c_void_p), ("ld_resid", ctypes.c_size_t), ("norm_w", ctypes.c_void_p),
+                ("out_rows", ctypes.c_int64), ("ex_lo", ctypes.c_int64), ("ex_hi", ctypes.c_int64),
+                ("ex_row0", ctypes.c_int64), ("y", ctypes.c_void_p), ("ldy", ctypes.c_size_t)]
+
+
 class PeerExchange(ctypes.Structure):
     """smeai_peer_exchange: the fused all-gather of a row-sharded GEMV."""
     _fields_ = [("n_dst", ctypes.c_int), ("dst", ctypes.c_void_p * 8), ("ld_dst", ctypes.c_int64),
@@ -142,6 +152,11 @@ def _declare(L: ctypes.CDLL) -> None:
         "smeai_q2k_block_sums": (I, [P, P, P, P, P]),
         "smeai_q2k_program_create": (I, [ctypes.POINTER(Q2KPhase), I, I64, F, ctypes.POINTER(ctypes.c_void_p)]),
         "smeai_q2k_program_run": (I, [P, P]),
+        "smeai_q2k_mg_program_create": (I, [ctypes.POINTER(Q2KMGPhase), I, I64, F, I, I,
+                                             ctypes.POINTER(ctypes.c_void_p)]),
+        "smeai_q2k_program_ipc_handle": (I, [P, P]),
+        "smeai_q2k_program_connect": (I, [P, P, I]),
+        "smeai_q2k_program_gather": (I, [P, I, P, SZ, P]),
         "smeai_q2k_program_reset": (I, [P, P]),
         "smeai_q2k_program_free": (None, [P]),
         "smeai_q2k_quantize_device": (I, [P, I64, P, P]),

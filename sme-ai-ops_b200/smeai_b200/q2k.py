@@ -379,3 +379,100 @@ class Q2KProgram:
             self.free()
         except Exception:
             pass
+
+
+class Q2KMGProgram:
+    """The decode program over the row shards of several GPUs
+    (smeai_q2k_mg_program_*): one per rank, phases wired explicitly.
+
+    phases: dicts with keys w (this rank's shard, Q2KMatrix), input
+    (IN_F32 / IN_F32_RMS), x_src / x_row0 (producing phase and its global
+    row) or x (outside input tensor), epilogue, resid_src / resid_row0 or
+    resid (outside), norm_w, out_rows (global rows), ex_lo / ex_hi / ex_row0
+    (local rows exchanged and their global position), y (local output tensor).
+    Construction is collective over `group`: the ranks swap the IPC handles of
+    their tagged buffers and map each other's; if any rank fails, every rank
+    raises RuntimeError (nobody is left waiting in a collective)."""
+
+    def __init__(self, phases, n_cols: int, rank: int, world: int, rms_eps: float = 1e-5, group=None):
+        import torch.distributed as dist
+        from . import Q2KMGPhase, IN_F32
+        arr = (Q2KMGPhase * len(phases))()
+        self._keep = []
+        for i, ph in enumerate(phases):
+            w, y = ph["w"], ph["y"]
+            epi = ph.get("epilogue", EPI_STORE)
+            x, resid, nw = ph.get("x"), ph.get("resid"), ph.get("norm_w")
+            a = arr[i]
+            a.w = w.handle
+            a.input = ph.get("input", IN_F32)
+            a.x_src = ph.get("x_src", -1)
+            a.x_row0 = ph.get("x_row0", 0)
+            a.x = 0 if x is None else x.data_ptr()
+            a.ld_x = 0 if x is None else (x.stride(0) if x.dim() == 2 else w.k)
+            a.epilogue = epi
+            a.resid_src = ph.get("resid_src", -1)
+            a.resid_row0 = ph.get("resid_row0", 0)
+            a.resid = 0 if resid is None else resid.data_ptr()
+            a.ld_resid = 0 if resid is None else (resid.stride(0) if resid.dim() == 2 else resid.numel())
+            a.norm_w = 0 if nw is None else nw.data_ptr()
+            a.out_rows = ph["out_rows"]
+            a.ex_lo, a.ex_hi, a.ex_row0 = ph.get("ex_lo", 0), ph["ex_hi"], ph.get("ex_row0", 0)
+            a.y = y.data_ptr()
+            a.ldy = y.stride(0) if y.dim() == 2 else y.numel()
+            self._keep += [w, x, resid, nw, y]
+        h = ctypes.c_void_p()
+        ok = False
+        try:
+            ok = lib().smeai_q2k_mg_program_create(arr, len(phases), n_cols, ctypes.c_float(rms_eps), rank, world,
+                                                   ctypes.byref(h)) == 0
+        except Exception:
+            ok = False
+        err = "" if ok else str(lib().smeai_last_error().decode(errors="replace"))
+        handle = (ctypes.c_ubyte * 64)()
+        if ok:
+            ok = lib().smeai_q2k_program_ipc_handle(h, handle) == 0
+        self.handle = h
+        self.n_phases = len(phases)
+        handles = [None] * world
+        if world == 1:
+            handles = [bytes(handle) if ok else None]
+        else:
+            dist.all_gather_object(handles, bytes(handle) if ok else None, group=group)
+        if all(x is not None for x in handles):
+            blob = (ctypes.c_ubyte * (64 * world)).from_buffer_copy(b"".join(handles))
+            ok = lib().smeai_q2k_program_connect(h, blob, world) == 0
+            if not ok:
+                err = str(lib().smeai_last_error().decode(errors="replace"))
+        else:
+            ok = False
+        oks = [ok]
+        if world > 1:
+            oks = [None] * world
+            dist.all_gather_object(oks, ok, group=group)
+        if not all(oks):
+            self.free()
+            raise RuntimeError(f"multi-GPU program unavailable on some rank ({err or 'a peer failed'})")
+
+    def run(self):
+        check(lib().smeai_q2k_program_run(self.handle, cur_stream()), "q2k_program_run")
+
+    def gather(self, phase: int, out: torch.Tensor):
+        """Phase `phase`'s global output of the last run (all ranks' rows) into `out`."""
+        check(lib().smeai_q2k_program_gather(self.handle, phase, _ptr(out), out.stride(0), cur_stream()),
+              "q2k_program_gather")
+        return out
+
+    def reset(self):
+        check(lib().smeai_q2k_program_reset(self.handle, cur_stream()), "q2k_program_reset")
+
+    def free(self):
+        if getattr(self, "handle", None) and self.handle.value:
+            lib().smeai_q2k_program_free(self.handle)
+            self.handle = ctypes.c_void_p()
+
+    def __del__(self):
+        try:
+            self.free()
+        except Exception:
+            pass

@@ -94,14 +94,21 @@ class Q2KDecodeStack:
         # batch): every linear on the tensor-core GEMM with the same epilogues,
         # the quantizers as separate kernels -- same bits as the GEMV placements;
         # on N GPUs its slices are all-gathered over NCCL.
-        assert quant in ("fused", "separate", "mixed", "program", "peer", "tc")
-        if quant in ("program", "peer") and world > 1:
-            aligned = all((shard_range(hidden, q, world)[1] - shard_range(hidden, q, world)[0]) % 32 == 0
-                          for q in range(world))
-            quant = "peer" if aligned and batch in (1, 2, 4, 8) else "separate"
+        # "mgprog" (N GPUs, or one GPU to check the wiring; batch 1, 2, 4 or 8):
+        # the whole step as ONE persistent kernel per rank over its row shards,
+        # every finished row stored into every rank's copy of the phase's
+        # output in the same kernel (Q2KMGProgram) -- the default on N > 1.
+        assert quant in ("fused", "separate", "mixed", "program", "peer", "tc", "mgprog")
+        if quant in ("program", "peer", "mgprog") and world > 1:
+            aligned = all((shard_range(n, q, world)[1] - shard_range(n, q, world)[0]) % 32 == 0
+                          for n in (hidden, ffn, vocab) for q in range(world - 1))
+            if not (aligned and batch in (1, 2, 4, 8)):
+                quant = "separate"
+            elif quant == "program":
+                quant = "mgprog"
         elif quant == "peer":
             quant = "program"
-        if quant == "program" and batch not in (1, 2, 4, 8):
+        if quant in ("program", "mgprog") and batch not in (1, 2, 4, 8):
             quant = "separate"
         self.prog = None
         self.quant = quant
@@ -159,6 +166,7 @@ class Q2KDecodeStack:
         self.hq = torch.empty((B, ffn // QK_K * Q8K_BLOCK_BYTES), dtype=u8, device=d)
         self.lg_loc = torch.empty((B, vs), dtype=f32, device=d)
         self.logits = torch.empty((B, vocab), dtype=f32, device=d)
+        self.x_loc_d = torch.empty((B, hs), dtype=f32, device=d)   # the down phase's local rows (mgprog)
         self.arena = None
         if self.quant == "peer":
             self._setup_peer()
@@ -262,6 +270,12 @@ class Q2KDecodeStack:
                 self.prog = self._build_program()
             self.prog.run()
             return self.logits
+        if self.quant == "mgprog":
+            if self.prog is None:
+                self.prog = self._build_mg_program()
+            self.prog.run()
+            self.prog.gather(4 * self.L, self.logits)
+            return self.logits
         if self.quant == "peer":
             return self._step_peer()
         L = self._lin
@@ -304,6 +318,31 @@ class Q2KDecodeStack:
         phases.append(dict(w=self.lm, x=self.x, input=IN_F32_RMS, y=self.logits, norm_w=self.out_norm))
         return Q.Q2KProgram(phases, self.B, rms_eps=self.eps)
 
+    def _build_mg_program(self):
+        """The step as one kernel per rank over the rank's row shards; every
+        phase names the phase it reads (global rows) explicitly."""
+        from . import IN_F32, IN_F32_RMS
+        H, F, V, hs = self.H, self.F, self.V, self.hs
+        phases = []
+        for li, (wqkv, wo, wgu, wd) in enumerate(self.layers):
+            b = 4 * li
+            x_in = dict(x_src=b - 1) if li else dict(x=self.x)
+            resid_in = dict(resid_src=b - 1, resid_row0=self.h_lo) if li else \
+                dict(resid=self.x, resid_row0=self.h_lo)
+            phases += [
+                dict(w=wqkv, input=IN_F32_RMS, norm_w=self.attn_norm[li], out_rows=H, ex_lo=2 * hs, ex_hi=3 * hs,
+                     ex_row0=self.h_lo, y=self.qkv, **x_in),
+                dict(w=wo, input=IN_F32, x_src=b, epilogue=EPI_RESIDUAL, out_rows=H, ex_hi=hs, ex_row0=self.h_lo,
+                     y=self.x_loc, **resid_in),
+                dict(w=wgu, input=IN_F32_RMS, x_src=b + 1, norm_w=self.ffn_norm[li], epilogue=EPI_SILU_MUL,
+                     out_rows=F, ex_hi=self.fs, ex_row0=self.f_lo, y=self.h_loc),
+                dict(w=wd, input=IN_F32, x_src=b + 2, epilogue=EPI_RESIDUAL, resid_src=b + 1, resid_row0=self.h_lo,
+                     out_rows=H, ex_hi=hs, ex_row0=self.h_lo, y=self.x_loc_d),
+            ]
+        phases.append(dict(w=self.lm, input=IN_F32_RMS, x_src=4 * self.L - 1, norm_w=self.out_norm, out_rows=V,
+                           ex_hi=self.vs, ex_row0=self.v_lo, y=self.lg_loc))
+        return Q.Q2KMGProgram(phases, self.B, self.rank, self.world, rms_eps=self.eps, group=self.group)
+
     # --------------------------------------------------------------- accounting
     def ops_per_step(self) -> int:
         """Integer multiply-adds x 2 of every linear in a step on this rank
@@ -316,6 +355,8 @@ class Q2KDecodeStack:
         linear whose quantization is not fused."""
         if self.quant == "program":
             return 1
+        if self.quant == "mgprog":
+            return 2                       # the program and the gather of the logits
         if self.quant == "peer":
             return self.L * 4 + 2          # the GEMVs and the step-end kernel
         if self.quant == "tc":             # per linear: quantizer, operand prepass, GEMM

@@ -1,8 +1,10 @@
-"""Row-sharded decode stack on 2 GPUs against the single-GPU stack, with NCCL
-all-gathers ("separate") and with the all-gather fused into each GEMV over
-CUDA-IPC peer memory ("peer"): logits must be bit-identical (sharding only
-moves rows between GPUs; every row's arithmetic is unchanged), eagerly and
-from a CUDA graph replayed twice.  Skips with < 2 GPUs."""
+"""Row-sharded decode stack on 2 (and 4) GPUs against the single-GPU stack,
+with NCCL all-gathers ("separate"), with the all-gather fused into each GEMV
+over CUDA-IPC peer memory ("peer"), and as one persistent kernel per rank
+whose finishers store every row into every rank's copy ("mgprog", the
+default on several GPUs): logits must be bit-identical (sharding only moves
+rows between GPUs; every row's arithmetic is unchanged), eagerly and from a
+CUDA graph replayed twice.  Skips without enough GPUs."""
 import datetime
 import os
 import socket
@@ -61,16 +63,16 @@ def _rank(rank, world, port, quant, results):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("quant", ["separate", "peer"])
-def test_two_gpu_sharded_stack_matches_single_gpu(cuda, quant):
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs 2 GPUs")
+@pytest.mark.parametrize("world,quant", [(2, "separate"), (2, "peer"), (2, "mgprog"), (4, "mgprog")])
+def test_sharded_stack_matches_single_gpu(cuda, world, quant):
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     from smeai_b200.stack import Q2KDecodeStack
     ref = Q2KDecodeStack(device=cuda, **DIMS).step().cpu().clone()
     torch.cuda.synchronize()
     results = mp.get_context("spawn").Manager().dict()
-    mp.start_processes(_rank, args=(2, _port(), quant, results), nprocs=2, start_method="spawn")
-    for r in range(2):
+    mp.start_processes(_rank, args=(world, _port(), quant, results), nprocs=world, start_method="spawn")
+    for r in range(world):
         eager, graphed, code = results[r]
         assert code == 0, (r, code)
         assert torch.equal(eager, ref), r

@@ -185,3 +185,28 @@ def test_tc_gemm_epilogues_match_gemv(cuda):
     assert torch.equal(y, m.mul_mat(xq, cols, epilogue=S.EPI_RESIDUAL, resid=r))
     assert torch.equal(m.mul_mat_tc(xq, cols, epilogue=S.EPI_SILU_MUL),
                        m.mul_mat(xq, cols, epilogue=S.EPI_SILU_MUL))
+
+
+@pytest.mark.parametrize("batch", [1, 2])
+def test_mg_program_wiring_on_one_gpu(cuda, batch):
+    """The multi-GPU program's explicit phase wiring, run with one rank (no
+    peers), gives the one-GPU program's logits bit for bit, eagerly and
+    twice from a CUDA graph (tags advance, the double-buffered sets swap)."""
+    kw = dict(n_layers=2, hidden=1024, ffn=2816, vocab=2048, batch=batch, device=cuda, seed=13)
+    a = Q2KDecodeStack(quant="program", **kw).step().clone()
+    st = Q2KDecodeStack(quant="mgprog", **kw)
+    assert torch.equal(st.step(), a)
+    stream = torch.cuda.Stream()
+    st.logits.zero_()
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=stream):
+        st.step()
+    for _ in range(2):
+        with torch.cuda.stream(stream):
+            g.replay()
+        stream.synchronize()
+        assert torch.equal(st.logits, a)
+    del g
+    st.free()
+    assert S.take_device_error() == 0
