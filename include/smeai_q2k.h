@@ -140,10 +140,11 @@ int smeai_q2k_mul_mat_tc_ex(const void *w_dev, const void *x_q8k_dev, int64_t n_
  * Phase p reads the complete output of phase p-1 (its input buffer is, or
  * contains, that output); each phase is one smeai_q2k_mul_mat_ex /
  * smeai_q2k_mul_mat_f32_ex call and gives the same bits.  One CTA per SM
- * streams every phase's weights back to back while the phases wait on one
- * another through completion counters in device memory, so a decode step is
- * one launch instead of one per linear (ggml's graph of MUL_MAT nodes over a
- * layer stack, run as a single kernel).  n_cols (tokens) is 1, 2, 4 or 8.
+ * streams every phase's weights back to back; each finished output value is
+ * published as one 8-byte tagged word (value + launch tag) that the next
+ * phase's warps poll block by block, so a decode step is one launch instead
+ * of one per linear (ggml's graph of MUL_MAT nodes over a layer stack, run
+ * as a single kernel).  n_cols (tokens) is 1, 2, 4 or 8.
  * The launch is cooperative; a run that hits a bounded-wait timeout (never
  * expected; reported by smeai_take_device_error) needs
  * smeai_q2k_program_reset before the next run. */
