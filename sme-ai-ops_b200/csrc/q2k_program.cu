@@ -70,6 +70,11 @@ constexpr uint64_t kAbortCheckNs = 20000;        // waits shorter than this neve
 // cache lines every warp of the grid needs for an RMSNorm are spread over
 // kSumReps places instead of one.
 constexpr int kSumReps = 16;
+// Row-group terms buffers between the consumer warps and the two finisher
+// warps (group jj uses buffer jj mod tbufs).  Measured on B200: four buffers
+// (consumers up to three groups ahead of the finishing) took 0.894 ms per
+// 7B-shape token against 0.842 ms with two.
+constexpr int kMaxTbufs = 2;
 constexpr int kDefaultL2Ahead = 0;  // measured on B200: 0.860 ms/token at 0, 0.863 at 4, 0.869 at 8, 0.94 at 12+
 
 // Descriptor of one phase.  The *_ll pointers address the tagged buffers of
@@ -130,7 +135,8 @@ struct ProgParams {
   unsigned* err;
   uint64_t timeout_ns;  // every bounded wait
   int64_t set_bytes;    // distance between the two sets of tagged buffers
-  int tbufs;            // row-group terms buffers: 2 (double-buffered) or 1 when two do not fit
+  int tbufs;            // row-group terms buffers: 2, or 1 when two do not fit
+  int log2_tbufs;
   int l2_ahead;         // ring stages the L2 prefetch stream runs ahead of the ring loads
   int sys;              // tagged words at system scope (peers store into this GPU's buffers)
   int n_peers;          // other ranks whose copies of the tagged buffers this rank stores into
@@ -145,8 +151,8 @@ struct PSmem {
   float* terms;       // [tbufs][T * nb_max][32]
   uint64_t* full;
   uint64_t* empty;
-  uint64_t* grp;      // [2] all consumer warps wrote a row group's terms
-  uint64_t* tfree;    // [2] the finisher has consumed them
+  uint64_t* grp;      // [kMaxTbufs] all consumer warps wrote a row group's terms
+  uint64_t* tfree;    // [kMaxTbufs] the finisher has consumed them
   // RMSNorm inputs: the first consumer warp to reach the CTA's n-th RMSNorm
   // phase polls the group sums and publishes 1/rms of every token in slot
   // n % 4 (a warp can run at most two phases ahead of the slowest one)
@@ -168,8 +174,8 @@ __host__ __device__ __forceinline__ size_t act_slots(int T, int nb_max, int W) {
 
 __host__ __device__ __forceinline__ size_t prog_fixed_bytes(int T, int nb_max, int W, int tbufs) {
   const size_t slots = act_slots(T, nb_max, W);
-  return al16(slots * 256) + al16(slots * 32) + al16(slots * 4) + al16((size_t)tbufs * T * nb_max * 128) + 8 * 4 +
-         16 + 16 + 32 + 128;
+  return al16(slots * 256) + al16(slots * 32) + al16(slots * 4) + al16((size_t)tbufs * T * nb_max * 128) +
+         8 * 2 * kMaxTbufs + 16 + 16 + 32 + 128;
 }
 __host__ __device__ __forceinline__ size_t prog_smem_bytes(int T, int nb_max, int stages, int consumers, int tbufs) {
   return (size_t)stages * consumers * kTileBytes + prog_fixed_bytes(T, nb_max, consumers, tbufs) +
@@ -193,8 +199,8 @@ __device__ __forceinline__ PSmem pcarve(uint8_t* base, int T, int nb_max, int st
   m.full = reinterpret_cast<uint64_t*>(base + o);
   m.empty = m.full + stages;
   m.grp = m.empty + stages;
-  m.tfree = m.grp + 2;
-  m.rms_claim = reinterpret_cast<unsigned*>(m.tfree + 2);
+  m.tfree = m.grp + kMaxTbufs;
+  m.rms_claim = reinterpret_cast<unsigned*>(m.tfree + kMaxTbufs);
   m.rms_ready = m.rms_claim + 4;
   m.rms_inv = reinterpret_cast<float*>(m.rms_ready + 8);
   return m;
@@ -625,6 +631,40 @@ __device__ __forceinline__ bool finish_group_prog(const ProgParams& P, const flo
   return true;
 }
 
+// Walks this CTA's row groups in program order (phase, then c, c + C, ...);
+// jj counts them (the terms buffer of group jj is jj mod tbufs).
+struct GroupCursor {
+  int ph = 0, n_phases = 0, jj = 0;
+  int64_t g = 0, ng = 0;
+
+  __device__ void seek(const ProgParams& P, int64_t cta, int64_t C) {
+    for (; ph < n_phases; ++ph) {
+      const PhaseDev& D = P.phases[ph];
+      const int64_t first = (cta + C - D.rot) % C;
+      if (first < D.n_groups) {
+        g = first;
+        ng = D.n_groups;
+        return;
+      }
+    }
+  }
+  __device__ void start(const ProgParams& P, int64_t cta, int64_t C) {
+    n_phases = P.n_phases;
+    ph = 0;
+    jj = 0;
+    seek(P, cta, C);
+  }
+  __device__ bool valid() const { return ph < n_phases; }
+  __device__ void next(const ProgParams& P, int64_t cta, int64_t C) {
+    if (!valid()) return;
+    ++jj;
+    g += C;
+    if (g < ng) return;
+    ++ph;
+    seek(P, cta, C);
+  }
+};
+
 // Walks this CTA's ring stages in program order: phase, row group (c, c + C,
 // ...), chunk of up to W consecutive super-blocks (incrementally: the
 // producer thread does no division per stage).
@@ -713,7 +753,7 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1) q2k_program_kernel(const Pr
       mbar_init(&m.full[s], 1);
       mbar_init(&m.empty[s], W);
     }
-    for (int b = 0; b < 2; ++b) {
+    for (int b = 0; b < kMaxTbufs; ++b) {
       mbar_init(&m.grp[b], W);
       mbar_init(&m.tfree[b], 1);
     }
@@ -758,29 +798,38 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1) q2k_program_kernel(const Pr
   }
 
   if (warp > W) {
-    // ---- finishers: finisher f owns terms buffer f and finishes the CTA's
-    // row groups jj = f (mod tbufs) in order -- the ordered sum, the
-    // epilogue and the stores run beside the consumers' next tiles instead
-    // of in one consumer's path; each group's residual loads go out before
-    // the wait for its terms
+    // ---- finishers: finisher f finishes the CTA's row groups jj = f
+    // (mod 2) in order, group jj from terms buffer jj mod tbufs -- the
+    // ordered sum, the epilogue and the stores run beside the consumers'
+    // next tiles instead of in one consumer's path; a group's residual loads
+    // go out before the wait for the finisher's previous group
+    const int nfin = P.tbufs < 2 ? P.tbufs : 2;
     const int f = warp - W - 1;
-    if (f >= P.tbufs) return;
-    int jj = 0;
-    for (int ph = 0; ph < P.n_phases; ++ph) {
-      const PhaseDev& D = P.phases[ph];
-      const int64_t ngr = D.n_groups;
-      const int64_t first = (cta + C - D.rot) % C;
-      for (int64_t g = first; g < ngr; g += C, ++jj) {
-        if (jj % P.tbufs != f) continue;
-        const int use = P.tbufs == 2 ? (jj >> 1) : jj;
-        const float* terms = m.terms + (size_t)f * T * P.nb_max * 32;
-        uint64_t rw[T];
-        resid_issue<T>(D, g, lane, tag, so, rw, P.sys);
-        if (!pwait(&m.grp[f], (unsigned)(use & 1), P, tag)) return;
-        const bool ok = finish_group_prog<T>(P, terms, D, g, lane, tag, so, rw);
-        mbar_arrive_warp(&m.tfree[f]);
-        if (!ok) return;
-      }
+    if (f >= nfin) return;
+    GroupCursor cur;
+    cur.start(P, cta, C);
+    for (int k = 0; k < f; ++k) cur.next(P, cta, C);
+    uint64_t rw[T];
+    if (cur.valid()) resid_issue<T>(P.phases[cur.ph], cur.g, lane, tag, so, rw, P.sys);
+    while (cur.valid()) {
+      // the descriptor by value: the group's stores cannot make the compiler
+      // reload its fields from global memory
+      const PhaseDev D = P.phases[cur.ph];
+      const int64_t g = cur.g;
+      const int buf = cur.jj & (P.tbufs - 1), use = cur.jj >> P.log2_tbufs;
+      GroupCursor nx = cur;
+      for (int k = 0; k < nfin; ++k) nx.next(P, cta, C);
+      // the next group's residual loads go out before this group's wait
+      uint64_t rn[T];
+      if (nx.valid()) resid_issue<T>(P.phases[nx.ph], nx.g, lane, tag, so, rn, P.sys);
+      const float* terms = m.terms + (size_t)buf * T * P.nb_max * 32;
+      if (!pwait(&m.grp[buf], (unsigned)(use & 1), P, tag)) return;
+      const bool ok = finish_group_prog<T>(P, terms, D, g, lane, tag, so, rw);
+      mbar_arrive_warp(&m.tfree[buf]);
+      if (!ok) return;
+#pragma unroll
+      for (int t = 0; t < T; ++t) rw[t] = rn[t];
+      cur = nx;
     }
     return;
   }
@@ -832,8 +881,8 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1) q2k_program_kernel(const Pr
     // this CTA's row groups of the phase: first, first + C, ...
     for (int64_t g = first; g < ngr; g += C, ++jj) {
       // terms buffer of this group and how many times it was used before
-      const int buf = P.tbufs == 2 ? (jj & 1) : 0;
-      const int use = P.tbufs == 2 ? (jj >> 1) : jj;
+      const int buf = jj & (P.tbufs - 1);
+      const int use = jj >> P.log2_tbufs;
       float* terms = m.terms + (size_t)buf * T * P.nb_max * 32;
       if (use >= 1 && !pwait(&m.tfree[buf], (unsigned)((use - 1) & 1), P, tag)) return;
       const int64_t row = g * 32 + lane;
@@ -1038,26 +1087,29 @@ int build_program(std::vector<Spec>& sp, std::vector<Ext>& ext, int T, float eps
   const size_t ext_bytes = (size_t)round_up((ewords > 0 ? ewords : 1) * 8, 256);
 
   // launch shape: 16 consumer warps (8 when the activation planes of 8 tokens
-  // leave too little room) and the deepest power-of-two ring that fits
-  // (a single terms buffer as the last resort: 8 tokens of a k = 11008 input)
+  // leave too little room); then, in this order of preference, two terms
+  // buffers and a ring of at least 4 stages, two buffers and 2 stages, a
+  // single buffer (8 tokens of a k = 11008 input); the deepest power-of-two
+  // ring that fits
   int sms = 0, optin = 0;
   SMEAI_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
   SMEAI_CUDA_TRY(cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev));
   int consumers = 0, stages = 0, tbufs = 0;
-  for (int tb : {2, 1}) {
-    for (int W : {16, 8}) {
-      for (int S = 8; S >= 2; S >>= 1)
-        if (prog_smem_bytes(T, nb_max, S, W, tb) <= (size_t)optin) {
+  static const int kShapes[3][2] = {{kMaxTbufs, 4}, {kMaxTbufs, 2}, {1, 2}};  // {tbufs, min stages}
+  for (int W : {16, 8}) {
+    for (const auto& sh : kShapes) {
+      for (int S = 8; S >= sh[1]; S >>= 1)
+        if (prog_smem_bytes(T, nb_max, S, W, sh[0]) <= (size_t)optin) {
           stages = S;
           break;
         }
       if (stages) {
-        consumers = W;
+        tbufs = sh[0];
         break;
       }
     }
     if (stages) {
-      tbufs = tb;
+      consumers = W;
       break;
     }
   }
@@ -1475,6 +1527,7 @@ int q2k_program_run(Q2KProgram* pr, cudaStream_t stream) {
   P.timeout_ns = pr->world > 1 ? peer_wait_timeout_ns() : wait_timeout_ns();
   P.set_bytes = (int64_t)pr->set_bytes;
   P.tbufs = pr->tbufs;
+  P.log2_tbufs = pr->tbufs == 4 ? 2 : (pr->tbufs == 2 ? 1 : 0);
   P.l2_ahead = pr->l2_ahead;
   P.sys = pr->world > 1 ? 1 : 0;
   P.n_peers = pr->n_peers;
