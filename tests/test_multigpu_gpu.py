@@ -4,7 +4,7 @@ over CUDA-IPC peer memory ("peer"), and as one persistent kernel per rank
 whose finishers store every row into every rank's copy ("mgprog", the
 default on several GPUs): logits must be bit-identical (sharding only moves
 rows between GPUs; every row's arithmetic is unchanged), eagerly and from a
-CUDA graph replayed twice.  Skips without enough GPUs."""
+CUDA graph replayed twice (2, 4 and 8 ranks).  Skips without enough GPUs."""
 import datetime
 import os
 import socket
@@ -63,7 +63,7 @@ def _rank(rank, world, port, quant, results):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world,quant", [(2, "separate"), (2, "peer"), (2, "mgprog"), (4, "mgprog")])
+@pytest.mark.parametrize("world,quant", [(2, "separate"), (2, "peer"), (2, "mgprog"), (4, "mgprog"), (8, "mgprog")])
 def test_sharded_stack_matches_single_gpu(cuda, world, quant):
     if torch.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs")
