@@ -298,6 +298,122 @@ __global__ void __launch_bounds__(256, 2) linear_tiled_kernel(
   }
 }
 
+// FFMA GEMM for small and mid-sized fp16 problems (fewer than 120 tiles of
+// the register-tiled kernel, e.g. the 128 x 512 x 512 Linear): CTA tile 16 x
+// 32 outputs, 128 threads as 8 x 16, each owning a 2 x 2 block, so a small
+// problem still spreads over many SMs.  Every output is a chain of K
+// dependent FFMAs and a scheduler holds about one warp, so the products run in
+// batches of 8 k: the batch's operands are read from shared memory into
+// registers first (one latency per batch instead of one per k).  k advances
+// in chunks of 256: the next chunk's fp16 operands are fetched into registers
+// (12 16-byte loads per thread, all in flight together) while the current
+// chunk's products run from shared memory (fp32, k-major), then converted and
+// stored after a barrier.  Operands beyond K are zero: the accumulator starts
+// at +0 and never becomes -0, so 0 * 0 leaves it unchanged.  One accumulator
+// per output walked in k order: the results of linear_ffma_kernel bit for
+// bit.  Requirements (checked by the launcher): K, lda and ldb multiples of 8,
+// 16-byte aligned A and B, ldb >= N.
+constexpr int kSmallBM = 16, kSmallBN = 32, kSmallKC = 256, kSmallNT = 128;
+template <int EPI>
+__global__ void __launch_bounds__(kSmallNT) linear_small_kernel(const __half* __restrict__ A, int64_t M, int64_t K,
+                                                                int64_t lda, const __half* __restrict__ B,
+                                                                int64_t ldb, int64_t N,
+                                                                const float* __restrict__ bias, int act,
+                                                                float* __restrict__ C, __half* __restrict__ C16,
+                                                                int64_t ldc) {
+  constexpr int BM = kSmallBM, BN = kSmallBN, KC = kSmallKC, NT = kSmallNT;
+  constexpr int NA = BM * KC / 8 / NT, NB = KC * BN / 8 / NT;  // 16-byte loads per thread: 4 and 8
+  __shared__ __align__(16) float As[KC][BM];
+  __shared__ __align__(16) float Bs[KC][BN];
+  const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
+  const int64_t m0 = (int64_t)blockIdx.y * BM, n0 = (int64_t)blockIdx.x * BN;
+  float c00 = 0.f, c01 = 0.f, c10 = 0.f, c11 = 0.f;
+
+  // dependents launch once the products are done: launched at the start,
+  // their waiting CTAs share the SMs with this kernel's single warp per
+  // scheduler (measured 20-40% slower)
+  pdl_wait();
+
+  uint4 ra[NA], rb[NB];
+  // A load e = tid + NT i: row e % 16, k (e / 16) * 8; B load: k row e / 4, columns (e % 4) * 8
+  auto fetch = [&](int64_t k0) {
+#pragma unroll
+    for (int i = 0; i < NA; ++i) {
+      const int e = tid + NT * i, r = e % BM, kq = (e / BM) * 8;
+      ra[i] = (m0 + r < M && k0 + kq < K) ? *reinterpret_cast<const uint4*>(A + (m0 + r) * lda + k0 + kq)
+                                          : make_uint4(0, 0, 0, 0);
+    }
+#pragma unroll
+    for (int i = 0; i < NB; ++i) {
+      const int e = tid + NT * i, kr = e / 4, nq = (e % 4) * 8;
+      rb[i] = (k0 + kr < K && n0 + nq + 8 <= ldb) ? *reinterpret_cast<const uint4*>(B + (k0 + kr) * ldb + n0 + nq)
+                                                  : make_uint4(0, 0, 0, 0);
+    }
+  };
+  auto stash = [&]() {
+#pragma unroll
+    for (int i = 0; i < NA; ++i) {
+      const int e = tid + NT * i, r = e % BM, kq = (e / BM) * 8;
+      const __half* h = reinterpret_cast<const __half*>(&ra[i]);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) As[kq + j][r] = __half2float(h[j]);
+    }
+#pragma unroll
+    for (int i = 0; i < NB; ++i) {
+      const int e = tid + NT * i, kr = e / 4, nq = (e % 4) * 8;
+      const __half* h = reinterpret_cast<const __half*>(&rb[i]);
+      *reinterpret_cast<float4*>(&Bs[kr][nq]) =
+          make_float4(__half2float(h[0]), __half2float(h[1]), __half2float(h[2]), __half2float(h[3]));
+      *reinterpret_cast<float4*>(&Bs[kr][nq + 4]) =
+          make_float4(__half2float(h[4]), __half2float(h[5]), __half2float(h[6]), __half2float(h[7]));
+    }
+  };
+
+  fetch(0);
+  for (int64_t k0 = 0; k0 < K; k0 += KC) {
+    __syncthreads();  // the previous chunk's products are done with the shared tiles
+    stash();
+    __syncthreads();
+    if (k0 + KC < K) fetch(k0 + KC);
+#pragma unroll 1
+    for (int kb = 0; kb < KC; kb += 8) {
+      float2 a[8], b[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        a[u] = *reinterpret_cast<const float2*>(&As[kb + u][2 * ty]);
+        b[u] = *reinterpret_cast<const float2*>(&Bs[kb + u][2 * tx]);
+      }
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        c00 = __fmaf_rn(a[u].x, b[u].x, c00);
+        c01 = __fmaf_rn(a[u].x, b[u].y, c01);
+        c10 = __fmaf_rn(a[u].y, b[u].x, c10);
+        c11 = __fmaf_rn(a[u].y, b[u].y, c11);
+      }
+    }
+  }
+
+  pdl_trigger();
+  const float acc[2][2] = {{c00, c01}, {c10, c11}};
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const int64_t gm = m0 + 2 * ty + i;
+    if (gm >= M) continue;
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      const int64_t gn = n0 + 2 * tx + j;
+      if (gn >= N) continue;
+      float v = acc[i][j];
+      if (bias) v = v + bias[gn];
+      if constexpr (EPI == kEpiF16) {
+        C16[gm * ldc + gn] = __float2half_rn(activate(v, act));
+      } else {
+        C[gm * ldc + gn] = activate(v, act);
+      }
+    }
+  }
+}
+
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
 template <int EPI, typename TIn>
@@ -318,6 +434,14 @@ int launch_linear(const TIn* A, int64_t M, int64_t K, int64_t lda, const TIn* B,
       SMEAI_CUDA_TRY(launch(linear_tiled_kernel<TN, EPI>, grid, dim3(256), 0, s, A, M, K, lda, B, B2, ldb, N, bias,
                             bias2, act, C, C16, ldc));
       return kOk;
+    }
+    if constexpr (EPI != kEpiSwiGLU) {
+      if (K % 8 == 0 && lda % 8 == 0 && ldb % 8 == 0 && ldb >= N && aligned16(A) && aligned16(B)) {
+        dim3 grid((unsigned)((N + kSmallBN - 1) / kSmallBN), (unsigned)((M + kSmallBM - 1) / kSmallBM));
+        SMEAI_CUDA_TRY(launch(linear_small_kernel<EPI>, grid, dim3(kSmallNT), 0, s, A, M, K, lda, B, ldb, N, bias, act, C,
+                              C16, ldc));
+        return kOk;
+      }
     }
   }
   const int64_t big_tiles = ((M + 63) / 64) * ((N + 63) / 64);
