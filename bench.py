@@ -63,6 +63,8 @@ def parse_args():
     ap.add_argument("--attn-dim", type=int, default=4096, help="attention workload: model_dim")
     ap.add_argument("--attn-heads", type=int, default=32, help="attention workload: heads")
     ap.add_argument("--prefill-tokens", type=int, default=512, help="prefill workload: activation rows")
+    ap.add_argument("--prefill-shard", choices=["tokens", "rows"], default="tokens",
+                    help="prefill-stack on N > 1 GPUs: split the tokens over the ranks (full weights on every rank, no data-path collective) or the weight rows (NCCL all-gathers of every output)")
     ap.add_argument("--layers", type=int, default=32)
     ap.add_argument("--quant", choices=["fused", "separate", "mixed", "program"], default="program",
                     help="decode: 'program' (default) runs the whole step as one persistent kernel on one GPU; "
@@ -679,9 +681,16 @@ def run_ours(args):
     if args.workload in ("decode", "prefill-stack"):
         L, H, F, V = args.layers, 4096, 11008, 32000
         prefill_stack = args.workload == "prefill-stack"
-        stack = Q2KDecodeStack(n_layers=L, hidden=H, ffn=F, vocab=V, batch=args.prefill_tokens if prefill_stack
-                               else 1, rank=rank, world=world, device=dev, seed=0,
-                               quant="tc" if prefill_stack else args.quant)
+        seq_shard = prefill_stack and world > 1 and args.prefill_shard == "tokens"
+        if seq_shard:   # every rank: the full weights and its own tokens of the prefill
+            from smeai_b200.stack import token_range
+            tok = token_range(args.prefill_tokens, rank, world)
+            stack = Q2KDecodeStack(n_layers=L, hidden=H, ffn=F, vocab=V, batch=args.prefill_tokens, tokens=tok,
+                                   device=dev, seed=0, quant="tc")
+        else:
+            stack = Q2KDecodeStack(n_layers=L, hidden=H, ffn=F, vocab=V, batch=args.prefill_tokens if prefill_stack
+                                   else 1, rank=rank, world=world, device=dev, seed=0,
+                                   quant="tc" if prefill_stack else args.quant)
         x_in = torch.empty_like(stack.x0)
         x_in.copy_(stack.x0)
 
@@ -907,7 +916,11 @@ def run_ours(args):
         value, e2e_value, unit = args.prefill_tokens / (ms / 1e3), args.prefill_tokens / (e2e_ms / 1e3), "tokens/s"
     if rank == 0:
         if args.workload == "prefill-stack":
-            parallel = f"row-shard tp{world}, NCCL all-gathers of the output slices" if world > 1 else "single GPU"
+            parallel = ("single GPU" if world == 1 else
+                        f"sequence-shard sp{world}: each rank runs {stack.B} of the {args.prefill_tokens} tokens "
+                        "through the full weights, no data-path collective (tokens are independent through this "
+                        "linear stack; an attention layer would add a K/V all-gather)" if seq_shard else
+                        f"row-shard tp{world}, NCCL all-gathers of the output slices")
         elif args.workload == "decode":
             parallel = (f"row-shard tp{world}, " + {
                 "peer": "all-gather fused into each GEMV (NVLink peer stores + signals)",

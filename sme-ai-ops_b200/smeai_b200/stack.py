@@ -45,6 +45,14 @@ def shard_stride(n: int, world: int, align: int = 32) -> int:
     return int(math.ceil(n / world / align)) * align
 
 
+def token_range(n: int, rank: int, world: int):
+    """Tokens [lo, hi) of rank `rank` when the tokens of a prefill are split
+    over `world` ranks (sequence sharding): sizes differ by at most one."""
+    base, extra = divmod(n, world)
+    lo = rank * base + min(rank, extra)
+    return lo, lo + base + (1 if rank < extra else 0)
+
+
 def gather_rows(full, local, n: int, world: int, group=None, scratch=None):
     """full[:, :n] <- the ranks' row slices in rank order (torch.distributed).
 
@@ -77,7 +85,14 @@ def gemv_bytes(rows: int, k: int, cols: int, out_rows: int | None = None) -> int
 class Q2KDecodeStack:
     def __init__(self, n_layers=32, hidden=4096, ffn=11008, vocab=32000, batch=1, rank=0, world=1,
                  device=None, seed=0, std=0.02, eps=1e-5, group=None, keep_blocks=False, quant="separate",
-                 norm_weights=True):
+                 norm_weights=True, tokens=None):
+        # tokens=(lo, hi): this stack runs tokens lo..hi-1 of a batch of `batch`
+        # (sequence sharding of a prefill: every rank holds the full weights
+        # and its own tokens; rows of x0 are those of the whole batch's draw)
+        self.batch_global = batch
+        self.tok_lo, self.tok_hi = (0, batch) if tokens is None else (int(tokens[0]), int(tokens[1]))
+        assert 0 <= self.tok_lo < self.tok_hi <= batch, (tokens, batch)
+        batch = self.tok_hi - self.tok_lo
         self.L, self.H, self.F, self.V = n_layers, hidden, ffn, vocab
         self.B, self.rank, self.world, self.eps, self.group = batch, rank, world, eps, group
         # where each linear's input is quantized to Q8_K: "fused" = inside the
@@ -153,8 +168,8 @@ class Q2KDecodeStack:
         self.weight_bytes += self.lm.n_rows * self.lm.nb * 84
         torch.cuda.synchronize()
         B, d, f32, u8 = batch, self.dev, torch.float32, torch.uint8
-        self.x0 = torch.randn((B, hidden), generator=torch.Generator(device=d).manual_seed(seed + 12345),
-                              device=d, dtype=f32)
+        self.x0 = torch.randn((self.batch_global, hidden), generator=torch.Generator(device=d).manual_seed(seed + 12345),
+                              device=d, dtype=f32)[self.tok_lo:self.tok_hi].contiguous()
         self.x = torch.empty_like(self.x0)
         self.xq = torch.empty((B, hidden // QK_K * Q8K_BLOCK_BYTES), dtype=u8, device=d)
         self.qkv = torch.empty((B, 3 * hs), dtype=f32, device=d)

@@ -77,3 +77,18 @@ def test_shard_ranges_cover_rows():
             assert all(a[1] == b[0] for a, b in zip(spans, spans[1:]))
             assert all(hi - lo <= shard_stride(n, world) for lo, hi in spans)
             assert all(lo % 32 == 0 or lo == hi == n for lo, hi in spans)
+
+
+def test_token_ranges_partition_tokens():
+    """Sequence sharding of a prefill: the ranks' token ranges tile the batch
+    in order and differ in size by at most one."""
+    import sys
+    sys.path.insert(0, os.path.join(os.path.dirname(__file__), "..", "sme-ai-ops_b200"))
+    from smeai_b200.stack import token_range
+    for n in (8, 130, 512, 513):
+        for world in (1, 2, 3, 4, 8):
+            spans = [token_range(n, r, world) for r in range(world)]
+            assert spans[0][0] == 0 and spans[-1][1] == n
+            assert all(a[1] == b[0] for a, b in zip(spans, spans[1:]))
+            sizes = [hi - lo for lo, hi in spans]
+            assert max(sizes) - min(sizes) <= 1 and min(sizes) >= 1

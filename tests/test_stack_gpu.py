@@ -170,6 +170,24 @@ def test_prefill_stack_on_tensor_cores_matches_decode_stack(cuda, batch):
     assert torch.isfinite(b).all()
 
 
+def test_token_sharded_prefill_rows_match_whole_batch(cuda):
+    """Sequence sharding of the prefill (the multi-GPU prefill-stack bench):
+    a stack over tokens [lo, hi) of the batch gives rows lo..hi-1 of the
+    whole batch's logits bit for bit, for every rank of 3 (tokens are
+    independent through the linear stack; each rank holds the full weights)."""
+    from smeai_b200.stack import token_range
+    kw = dict(n_layers=2, hidden=1024, ffn=2816, vocab=2048, batch=130, device=cuda, seed=21, quant="tc")
+    whole = Q2KDecodeStack(**kw)
+    ref = whole.step().clone()
+    whole.free()
+    for r in range(3):
+        lo, hi = token_range(130, r, 3)
+        part = Q2KDecodeStack(tokens=(lo, hi), **kw)
+        assert part.B == hi - lo
+        assert torch.equal(part.step(), ref[lo:hi]), r
+        part.free()
+
+
 def test_tc_gemm_epilogues_match_gemv(cuda):
     from smeai_b200 import q2k as Q
     g = torch.Generator(device=cuda).manual_seed(8)
