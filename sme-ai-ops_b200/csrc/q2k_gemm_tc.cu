@@ -71,6 +71,7 @@ struct GemmParams {
   const float* resid;
   int64_t ld_resid;
   unsigned* err;
+  int raw_log2;           // log2 of the raw Q2_K tile slots (4, or 2 for a long k)
 };
 
 // ---- tcgen05 helpers ---------------------------------------------------------
@@ -192,12 +193,12 @@ struct GemmSmem {
   uint8_t* b;        // [4][kAtomBytes]
   uint8_t* a2;       // [2][kMinBytes]
   uint8_t* b2;       // [2][kMinBytes]
-  uint8_t* raw;      // [2][kRawBytes]
+  uint8_t* raw;      // [raw slots][kRawBytes]
   float* sdx;        // [nb][kTN]
   uint64_t* full;    // [4]  per atom slot: dequant (128) + producer (1, tx)
   uint64_t* empty;   // [4]  per atom slot: commit
-  uint64_t* rfull;   // [2]  producer (tx)
-  uint64_t* rempty;  // [2]  dequant (128)
+  uint64_t* rfull;   // [kMaxRaw]  producer (tx)
+  uint64_t* rempty;  // [kMaxRaw]  dequant (128)
   uint64_t* mfull;   // [2]  dequant (128) + producer (1, tx)
   uint64_t* mempty;  // [2]  commit
   uint64_t* afull;   // [2]  commit
@@ -207,12 +208,16 @@ struct GemmSmem {
   int* abort;
 };
 
-size_t gemm_smem_bytes(int nb) {
-  return 1024 /* alignment slack */ + 8 * (size_t)kAtomBytes + 4 * (size_t)kMinBytes + 2 * (size_t)kRawBytes +
-         (size_t)kTN * nb * 4 + 32 * 8 + 16;
+// Raw Q2_K tiles come from HBM: four super-blocks of them in flight keep the
+// dequant warps fed across the load latency; two when four do not fit (k
+// above 20224).
+constexpr int kMaxRaw = 4;
+size_t gemm_smem_bytes(int nb, int raw_slots) {
+  return 1024 /* alignment slack */ + 8 * (size_t)kAtomBytes + 4 * (size_t)kMinBytes +
+         (size_t)raw_slots * kRawBytes + (size_t)kTN * nb * 4 + 40 * 8 + 16;
 }
 
-__device__ __forceinline__ GemmSmem carve_gemm(uint8_t* base, int nb) {
+__device__ __forceinline__ GemmSmem carve_gemm(uint8_t* base, int nb, int raw_slots) {
   GemmSmem m;
   uint8_t* p = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(base) + 1023) & ~(uintptr_t)1023);
   m.a = p;
@@ -224,21 +229,21 @@ __device__ __forceinline__ GemmSmem carve_gemm(uint8_t* base, int nb) {
   m.b2 = p;
   p += 2 * kMinBytes;
   m.raw = p;
-  p += 2 * kRawBytes;
+  p += (size_t)raw_slots * kRawBytes;
   m.sdx = reinterpret_cast<float*>(p);
   p += (size_t)kTN * nb * 4;
   uint64_t* bars = reinterpret_cast<uint64_t*>(p);
   m.full = bars;
   m.empty = bars + 4;
   m.rfull = bars + 8;
-  m.rempty = bars + 10;
-  m.mfull = bars + 12;
-  m.mempty = bars + 14;
-  m.afull = bars + 16;
-  m.aempty = bars + 18;
-  m.drain = bars + 20;
-  m.tmem = reinterpret_cast<uint32_t*>(bars + 21);
-  m.abort = reinterpret_cast<int*>(bars + 22);
+  m.rempty = m.rfull + kMaxRaw;
+  m.mfull = m.rempty + kMaxRaw;
+  m.mempty = m.mfull + 2;
+  m.afull = m.mempty + 2;
+  m.aempty = m.afull + 2;
+  m.drain = m.aempty + 2;
+  m.tmem = reinterpret_cast<uint32_t*>(m.drain + 1);
+  m.abort = reinterpret_cast<int*>(m.drain + 2);
   return m;
 }
 
@@ -272,16 +277,19 @@ __global__ void __launch_bounds__(kThreads, 1) q2k_gemm_tc_kernel(const GemmPara
   const int nb = p.nb;
   const int64_t row_tile = blockIdx.x, tok_tile = blockIdx.y;
   const int64_t n0 = row_tile * kTM, m0 = tok_tile * kTN;
-  const GemmSmem m = carve_gemm(smem_raw, nb);
+  const int RL = p.raw_log2, RS = 1 << RL;
+  const GemmSmem m = carve_gemm(smem_raw, nb, RS);
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < 4; ++i) {
       mbar_init(&m.full[i], 128 + 1);  // the 4 dequant warps of the atom's half + the producer
       mbar_init(&m.empty[i], 1);
     }
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < kMaxRaw; ++i) {
       mbar_init(&m.rfull[i], 1);
       mbar_init(&m.rempty[i], 32 * kDqWarps);
+    }
+    for (int i = 0; i < 2; ++i) {
       mbar_init(&m.mfull[i], 32 * kDqWarps + 1);
       mbar_init(&m.mempty[i], 1);
       mbar_init(&m.afull[i], 1);
@@ -314,22 +322,22 @@ __global__ void __launch_bounds__(kThreads, 1) q2k_gemm_tc_kernel(const GemmPara
   if (warp == 0) {
     // ---------------- producer
     if (lane == 0) {
-      int issued_raw[2] = {-1, -1}, issued_m[2] = {-1, -1}, issued_b[4] = {-1, -1, -1, -1};
+      int issued_raw[kMaxRaw] = {-1, -1, -1, -1}, issued_m[2] = {-1, -1}, issued_b[4] = {-1, -1, -1, -1};
       for (int b = 0; b < nb; ++b) {
-        const int r = b & 1;
-        if (b >= 2 && (!wait_or_abort(m, &m.rempty[r], ((b >> 1) - 1) & 1, p.err) ||
-                       !wait_or_abort(m, &m.mempty[r], ((b >> 1) - 1) & 1, p.err)))
+        const int r = b & 1, rr = b & (RS - 1);
+        if ((b >= RS && !wait_or_abort(m, &m.rempty[rr], ((b >> RL) - 1) & 1, p.err)) ||
+            (b >= 2 && !wait_or_abort(m, &m.mempty[r], ((b >> 1) - 1) & 1, p.err)))
           break;
         int groups = 0;
         for (int gi = 0; gi < 4; ++gi)
           if (row_tile * 4 + gi < p.n_groups) ++groups;
-        mbar_arrive_expect_tx(&m.rfull[r], (unsigned)(groups * kTileBytes));
+        mbar_arrive_expect_tx(&m.rfull[rr], (unsigned)(groups * kTileBytes));
         for (int gi = 0; gi < groups; ++gi) {
           const int64_t g = row_tile * 4 + gi;
-          bulk_copy_g2s(m.raw + r * kRawBytes + gi * kTileBytes, p.tiles + (g * nb + b) * (int64_t)kTileBytes,
-                        kTileBytes, &m.rfull[r]);
+          bulk_copy_g2s(m.raw + rr * kRawBytes + gi * kTileBytes, p.tiles + (g * nb + b) * (int64_t)kTileBytes,
+                        kTileBytes, &m.rfull[rr]);
         }
-        issued_raw[r] = b;
+        issued_raw[rr] = b;
         mbar_arrive_expect_tx(&m.mfull[r], kMinBytes);
         bulk_copy_g2s(m.b2 + r * kMinBytes, p.bs + (tok_tile * nb + b) * (int64_t)kMinBytes, kMinBytes,
                       &m.mfull[r]);
@@ -350,10 +358,10 @@ __global__ void __launch_bounds__(kThreads, 1) q2k_gemm_tc_kernel(const GemmPara
       }
       if (*reinterpret_cast<volatile int*>(m.abort)) {
         // drain: the last copy issued into each slot lands before we leave
-        for (int r = 0; r < 2; ++r) {
-          if (issued_raw[r] >= 0) mbar_wait_bounded(&m.rfull[r], (issued_raw[r] >> 1) & 1, kTimeoutNs);
+        for (int rr = 0; rr < RS; ++rr)
+          if (issued_raw[rr] >= 0) mbar_wait_bounded(&m.rfull[rr], (issued_raw[rr] >> RL) & 1, kTimeoutNs);
+        for (int r = 0; r < 2; ++r)
           if (issued_m[r] >= 0) mbar_wait_bounded(&m.mfull[r], (issued_m[r] >> 1) & 1, kTimeoutNs);
-        }
         for (int sl = 0; sl < 4; ++sl)
           if (issued_b[sl] >= 0) mbar_wait_bounded(&m.full[sl], (issued_b[sl] >> 1) & 1, kTimeoutNs);
       }
@@ -402,11 +410,11 @@ __global__ void __launch_bounds__(kThreads, 1) q2k_gemm_tc_kernel(const GemmPara
     const int gi = t >> 5, l = t & 31;
     const bool present = row_tile * 4 + gi < p.n_groups;
     for (int b = 0; b < nb; ++b) {
-      const int r = b & 1;
-      if (!wait_warp(m, &m.rfull[r], (b >> 1) & 1, p.err)) break;
+      const int r = b & 1, rr = b & (RS - 1);
+      if (!wait_warp(m, &m.rfull[rr], (b >> RL) & 1, p.err)) break;
       uint4 q[4], sc;
       if (present) {
-        const uint8_t* tile = m.raw + r * kRawBytes + gi * kTileBytes;
+        const uint8_t* tile = m.raw + rr * kRawBytes + gi * kTileBytes;
 #pragma unroll
         for (int c = 0; c < 4; ++c)
           if ((c >> 1) % kHStep == h0 % kHStep) q[c] = reinterpret_cast<const uint4*>(tile + c * 512)[l];
@@ -416,7 +424,7 @@ __global__ void __launch_bounds__(kThreads, 1) q2k_gemm_tc_kernel(const GemmPara
         for (int c = 0; c < 4; ++c) q[c] = make_uint4(0, 0, 0, 0);
         sc = make_uint4(0, 0, 0, 0);
       }
-      mbar_arrive(&m.rempty[r]);
+      mbar_arrive(&m.rempty[rr]);
       const uint32_t scw[4] = {sc.x, sc.y, sc.z, sc.w};
       // this warp's halves' mins (8 each) into the no-swizzle 128 x 16 operand
       if (b >= 2 && !wait_warp(m, &m.mempty[r], ((b >> 1) - 1) & 1, p.err)) break;
@@ -528,7 +536,9 @@ __global__ void __launch_bounds__(kThreads, 1) q2k_gemm_tc_kernel(const GemmPara
     if (ok && p.epi == kEpiSiluMul) {
       // rows 2i (gate) and 2i+1 (up) sit in adjacent lanes: the even lane
       // writes h_i = silu(gate) * up, the arithmetic of the GEMV's epilogue
-#pragma unroll 4
+      // (fully unrolled: a runtime index into acc would put the accumulators
+      // in local memory for the whole main loop)
+#pragma unroll
       for (int c = 0; c < 64; ++c) {
         const int64_t tok = m0 + half * 64 + c;
         const float gsum = __uint_as_float((uint32_t)(acc[c >> 1] >> (32 * (c & 1))));
@@ -618,7 +628,8 @@ int q2k_gemm_tc(const Q2KWeight& w, const void* xq, int64_t n_cols, float* y, in
     set_last_error("q2k_gemm_tc: scratch of %zu bytes (256-aligned) required", need);
     return kBadArgument;
   }
-  const size_t smem = gemm_smem_bytes(nb);
+  const int raw_slots = gemm_smem_bytes(nb, kMaxRaw) <= 227 * 1024 ? kMaxRaw : 2;
+  const size_t smem = gemm_smem_bytes(nb, raw_slots);
   if (smem > 227 * 1024) {
     set_last_error("q2k_gemm_tc: k=%lld too large", (long long)w.k);
     return kBadArgument;
@@ -664,6 +675,7 @@ int q2k_gemm_tc(const Q2KWeight& w, const void* xq, int64_t n_cols, float* y, in
   p.resid = resid;
   p.ld_resid = ld_resid;
   p.err = err;
+  p.raw_log2 = raw_slots == 4 ? 2 : 1;
   const dim3 grid((unsigned)((w.n_rows + kTM - 1) / kTM), (unsigned)tiles);
   SMEAI_CUDA_TRY(launch(q2k_gemm_tc_kernel, grid, dim3(kThreads), smem, stream, p));
   return kOk;
