@@ -141,6 +141,7 @@ struct ProgParams {
   int sys;              // tagged words at system scope (peers store into this GPU's buffers)
   int n_peers;          // other ranks whose copies of the tagged buffers this rank stores into
   int64_t peer_delta[kMaxPeers];  // byte offset from this rank's buffers to peer q's mapping of its own
+  int act_chunks;       // Q8_K activation slot chunks per warp and token (the 8-token kernel may reuse them)
 };
 
 struct PSmem {
@@ -168,24 +169,31 @@ __host__ __device__ __forceinline__ size_t al16(size_t v) { return (v + 15) & ~(
 // on to the next phase's prologue cannot overwrite an activation a slower
 // warp of its CTA still reads.
 __device__ __forceinline__ int act_slot(int cw, int W, int T, int i, int t) { return cw + W * (t + T * i); }
-__host__ __device__ __forceinline__ size_t act_slots(int T, int nb_max, int W) {
-  return (size_t)W * T * ((nb_max + W - 1) / W);
+// Slots hold act_chunks chunks of W blocks per token.  A phase whose input
+// is a plain fp32 vector and which gives no CTA more than one row group uses
+// each block once per CTA: its chunk c is quantized just before use into
+// chunk slot c mod act_chunks, so its width does not size the slots (the
+// k = 11008 down projection of 8 tokens would take 100 KB).
+__host__ __device__ __forceinline__ size_t act_slots(int T, int act_chunks, int W) {
+  return (size_t)W * T * act_chunks;
 }
 
-__host__ __device__ __forceinline__ size_t prog_fixed_bytes(int T, int nb_max, int W, int tbufs) {
-  const size_t slots = act_slots(T, nb_max, W);
+__host__ __device__ __forceinline__ size_t prog_fixed_bytes(int T, int nb_max, int act_chunks, int W, int tbufs) {
+  const size_t slots = act_slots(T, act_chunks, W);
   return al16(slots * 256) + al16(slots * 32) + al16(slots * 4) + al16((size_t)tbufs * T * nb_max * 128) +
          8 * 2 * kMaxTbufs + 16 + 16 + 32 + 128;
 }
-__host__ __device__ __forceinline__ size_t prog_smem_bytes(int T, int nb_max, int stages, int consumers, int tbufs) {
-  return (size_t)stages * consumers * kTileBytes + prog_fixed_bytes(T, nb_max, consumers, tbufs) +
+__host__ __device__ __forceinline__ size_t prog_smem_bytes(int T, int nb_max, int act_chunks, int stages,
+                                                          int consumers, int tbufs) {
+  return (size_t)stages * consumers * kTileBytes + prog_fixed_bytes(T, nb_max, act_chunks, consumers, tbufs) +
          (size_t)stages * 16;
 }
 
-__device__ __forceinline__ PSmem pcarve(uint8_t* base, int T, int nb_max, int stages, int consumers, int tbufs) {
+__device__ __forceinline__ PSmem pcarve(uint8_t* base, int T, int nb_max, int act_chunks, int stages, int consumers,
+                                        int tbufs) {
   PSmem m;
   size_t o = 0;
-  const size_t slots = act_slots(T, nb_max, consumers);
+  const size_t slots = act_slots(T, act_chunks, consumers);
   m.ring = base;
   o += (size_t)stages * consumers * kTileBytes;
   m.qs = reinterpret_cast<int4*>(base + o);
@@ -518,10 +526,12 @@ __device__ __forceinline__ bool prologue(const ProgParams& P, const ActSmem& act
 }
 
 // Plain fp32 input: block i of warp cw (all tokens), polled and quantized
-// the first time the warp needs it.
+// the first time the warp needs it, into chunk slot ic (i, or i mod
+// act_chunks when the phase's blocks are used once per CTA).
 template <int T>
 __device__ __forceinline__ bool ensure_block(const ProgParams& P, const ActSmem& act, const PhaseDev& D, int cw,
-                                          int W, int lane, unsigned tag, int64_t so, int i, unsigned& ready) {
+                                          int W, int lane, unsigned tag, int64_t so, int i, int ic,
+                                          unsigned& ready) {
   const uint64_t* x = set_ptr(D.x_ll, D.x_ext ? 0 : so);
   const int b = cw + i * W;
   constexpr int kBatch = T <= 2 ? T : 1;  // tokens whose loads go out together
@@ -533,7 +543,7 @@ __device__ __forceinline__ bool ensure_block(const ProgParams& P, const ActSmem&
 #pragma unroll
     for (int t = 0; t < kBatch; ++t)
       if (!quant_block<T>(P, act, D, x + (t0 + t) * D.ld_xll + b * QK_K + lane * 8, w[t], false, 1.f, b,
-                          act_slot(cw, W, T, i, t0 + t), lane, tag))
+                          act_slot(cw, W, T, ic, t0 + t), lane, tag))
         return false;
   }
   ready |= 1u << i;
@@ -743,7 +753,9 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1) q2k_program_kernel(const Pr
   const int S = P.stages, lgS = P.log2_stages, smask = S - 1;
   const int64_t C = gridDim.x, cta = blockIdx.x;
   const int stage_bytes = W * kTileBytes;
-  const PSmem m = pcarve(smem, T, P.nb_max, S, W, P.tbufs);
+  // the 1/2/4-token kernels size the slots from nb_max (act_chunks is then
+  // ceil(nb_max / W)); only the 8-token kernel reads the reuse-aware count
+  const PSmem m = pcarve(smem, T, P.nb_max, T == 8 ? P.act_chunks : (P.nb_max + W - 1) / W, S, W, P.tbufs);
   // every thread reads the launch count before the CTA's first sync, i.e.
   // before its CTA can arrive at the grid barrier after which CTA 0 advances it
   const unsigned tag = ld_relaxed_gpu(P.ctl) + 1u;
@@ -886,10 +898,19 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1) q2k_program_kernel(const Pr
       float* terms = m.terms + (size_t)buf * T * P.nb_max * 32;
       if (use >= 1 && !pwait(&m.tfree[buf], (unsigned)((use - 1) & 1), P, tag)) return;
       const int64_t row = g * 32 + lane;
-      for (int c = 0; c < nchunks; ++c, ++i) {
+      // chunk slot of chunk c: c, wrapping at act_chunks in the 8-token kernel
+      // (only a phase whose blocks are used once wraps; the other kernels
+      // never reuse slots: their code and shared-memory carve are those of
+      // the kernel before slot reuse, which measured 1.8% faster at 1 token
+      // on B200 than one carving from act_chunks)
+      constexpr bool kReuse = T == 8;
+      int icw = 0;
+      for (int c = 0; c < nchunks; ++c, ++i, icw = icw + 1 == P.act_chunks ? 0 : icw + 1) {
+        const int ic = kReuse ? icw : c;
         const int s = (int)(i & smask);
         const int b = c * W + cw;
-        if (b < nb && !(ready & (1u << c)) && !ensure_block<T>(P, act, D, cw, W, lane, tag, so, c, ready)) return;
+        if (b < nb && !(ready & (1u << c)) && !ensure_block<T>(P, act, D, cw, W, lane, tag, so, c, ic, ready))
+          return;
         if (!pwait(&m.full[s], (unsigned)((i >> lgS) & 1), P, tag)) return;
         if (b >= nb) {  // the group's last chunk is short
           mbar_arrive_warp(&m.empty[s]);
@@ -898,7 +919,7 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1) q2k_program_kernel(const Pr
         // the slot is released after the integer core has used every loaded
         // register (the arrive follows their last use in program order)
         const WBlock wb = load_wblock(m.ring + (size_t)s * stage_bytes + (size_t)cw * kTileBytes, lane);
-        block_terms<T, false>(wb, act, act_slot(cw, W, T, c, 0), W, nb, b, terms, lane, row, D.n_rows, nullptr,
+        block_terms<T, false>(wb, act, act_slot(cw, W, T, ic, 0), W, nb, b, terms, lane, row, D.n_rows, nullptr,
                               nullptr);
         mbar_arrive_warp(&m.empty[s]);
       }
@@ -944,6 +965,7 @@ struct Q2KProgram {
   int consumers = 0;
   int stages = 0;
   int tbufs = 2;
+  int act_chunks = 1;
   int l2_ahead = 0;
   int grid = 0;
   size_t smem = 0;
@@ -1094,15 +1116,36 @@ int build_program(std::vector<Spec>& sp, std::vector<Ext>& ext, int T, float eps
   int sms = 0, optin = 0;
   SMEAI_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
   SMEAI_CUDA_TRY(cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev));
-  int consumers = 0, stages = 0, tbufs = 0;
+  int consumers = 0, stages = 0, tbufs = 0, act_chunks = 0;
+  // chunk slots per warp: the widest phase's chunks (full), or -- for 8
+  // tokens, when that does not fit the shape -- the same except plain fp32
+  // inputs of phases with at most one row group per CTA (their blocks are
+  // used once; the 8-token kernel reuses their slots)
+  auto chunks_for = [&](int W, bool reuse) {
+    int c = 1;
+    for (const Spec& s : sp) {
+      const int nch = (s.w->nb + W - 1) / W;
+      const int need = (reuse && s.in_mode == kInF32 && s.w->n_groups <= sms) ? 1 : nch;
+      c = c > need ? c : need;
+    }
+    return c;
+  };
   static const int kShapes[3][2] = {{kMaxTbufs, 4}, {kMaxTbufs, 2}, {1, 2}};  // {tbufs, min stages}
   for (int W : {16, 8}) {
     for (const auto& sh : kShapes) {
-      for (int S = 8; S >= sh[1]; S >>= 1)
-        if (prog_smem_bytes(T, nb_max, S, W, sh[0]) <= (size_t)optin) {
-          stages = S;
+      for (bool reuse : {false, true}) {
+        if (reuse && T != 8) continue;
+        const int ac = chunks_for(W, reuse);
+        for (int S = 8; S >= sh[1]; S >>= 1)
+          if (prog_smem_bytes(T, nb_max, ac, S, W, sh[0]) <= (size_t)optin) {
+            stages = S;
+            break;
+          }
+        if (stages) {
+          act_chunks = ac;
           break;
         }
+      }
       if (stages) {
         tbufs = sh[0];
         break;
@@ -1117,7 +1160,7 @@ int build_program(std::vector<Spec>& sp, std::vector<Ext>& ext, int T, float eps
     set_last_error("q2k_program: k=%d super-blocks x %d tokens does not fit in shared memory", nb_max, T);
     return kBadArgument;
   }
-  const size_t smem = prog_smem_bytes(T, nb_max, stages, consumers, tbufs);
+  const size_t smem = prog_smem_bytes(T, nb_max, act_chunks, stages, consumers, tbufs);
   void* kern = nullptr;
   switch (T) {
     case 1: kern = reinterpret_cast<void*>(q2k_program_kernel<1>); break;
@@ -1140,6 +1183,7 @@ int build_program(std::vector<Spec>& sp, std::vector<Ext>& ext, int T, float eps
   pr->consumers = consumers;
   pr->stages = stages;
   pr->tbufs = tbufs;
+  pr->act_chunks = act_chunks;
   // L2 prefetch distance in ring stages: SMEAI_PROGRAM_L2_AHEAD=n overrides
   // the default (for tuning sweeps)
   pr->l2_ahead = kDefaultL2Ahead;
@@ -1528,6 +1572,7 @@ int q2k_program_run(Q2KProgram* pr, cudaStream_t stream) {
   P.set_bytes = (int64_t)pr->set_bytes;
   P.tbufs = pr->tbufs;
   P.log2_tbufs = pr->tbufs == 4 ? 2 : (pr->tbufs == 2 ? 1 : 0);
+  P.act_chunks = pr->act_chunks;
   P.l2_ahead = pr->l2_ahead;
   P.sys = pr->world > 1 ? 1 : 0;
   P.n_peers = pr->n_peers;
