@@ -66,6 +66,8 @@ def parse_args():
     ap.add_argument("--prefill-shard", choices=["tokens", "rows"], default="tokens",
                     help="prefill-stack on N > 1 GPUs: split the tokens over the ranks (full weights on every rank, no data-path collective) or the weight rows (NCCL all-gathers of every output)")
     ap.add_argument("--layers", type=int, default=32)
+    ap.add_argument("--decode-batch", type=int, default=1, choices=[1, 2, 4, 8],
+                    help="decode workload: tokens per step (the batch of a decode step)")
     ap.add_argument("--quant", choices=["fused", "separate", "mixed", "program"], default="program",
                     help="decode: 'program' (default) runs the whole step as one persistent kernel on one GPU; "
                          "the others launch one GEMV per linear with the Q8_K quantization fused, separate or "
@@ -689,7 +691,7 @@ def run_ours(args):
                                    device=dev, seed=0, quant="tc")
         else:
             stack = Q2KDecodeStack(n_layers=L, hidden=H, ffn=F, vocab=V, batch=args.prefill_tokens if prefill_stack
-                                   else 1, rank=rank, world=world, device=dev, seed=0,
+                                   else args.decode_batch, rank=rank, world=world, device=dev, seed=0,
                                    quant="tc" if prefill_stack else args.quant)
         x_in = torch.empty_like(stack.x0)
         x_in.copy_(stack.x0)
@@ -701,7 +703,8 @@ def run_ours(args):
         local_bytes = stack.algorithmic_bytes()
         h2d, d2h = x_in.numel() * 4, stack.logits.numel() * 4
         out_buf = stack.logits
-        workload = (f"llama2-7b-shape Q2_K linear stack decode, batch 1: {L} layers x (qkv, o, gate+up, down)"
+        workload = (f"llama2-7b-shape Q2_K linear stack decode, batch {args.decode_batch}: {L} layers x "
+                    "(qkv, o, gate+up, down)"
                     " + lm_head 32000x4096, RMSNorm+Q8_K re-quantization between linears")
         if prefill_stack:
             workload = (f"llama2-7b-shape Q2_K linear stack prefill, {args.prefill_tokens} tokens: {L} layers x "
@@ -956,11 +959,12 @@ def run_ours(args):
             "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
             "scaling": "strong" if args.workload in ("decode", "prefill-stack") else "weak",
             "vs_baseline": None, "dtype": "int8xu2", "data": "synthetic",
-            "tokens_per_s": (1e3 / ms) if args.workload == "decode" else
+            "tokens_per_s": (args.decode_batch * 1e3 / ms) if args.workload == "decode" else
             ((args.prefill_tokens * 1e3 / ms) if args.workload in ("prefill", "prefill-stack") else None),
             "pct_of_hbm_peak": (value / (peak * world) * 100) if unit == "GB/s" else None,
             "config": {"workload": workload,
-                       "global_batch": args.prefill_tokens if args.workload in ("prefill", "prefill-stack") else 1,
+                       "global_batch": args.prefill_tokens if args.workload in ("prefill", "prefill-stack")
+                       else (args.decode_batch if args.workload == "decode" else 1),
                        "seq_len": 1, "parallelism": parallel,
                        "l2": "inputs larger than L2 (2.17 GB of weights per step)"
                        if args.workload in ("decode", "prefill-stack")
